@@ -1,0 +1,112 @@
+/*
+ * exl3_b200.h -- C ABI of the B200-native EXL3 routed-expert path.
+ *
+ * Every entry takes raw device pointers, element counts and a cudaStream_t
+ * (passed as void*), and returns an int status (EXL3_OK or an EXL3_ERR_*
+ * code); the message of the last failure on the calling thread is returned
+ * by exl3_last_error().  Arguments are validated on the host before anything
+ * is launched.  Kernels never trap: device-side problems (a null or
+ * misaligned pointer inside a pointer table, a per-expert K outside 2..8, an
+ * expired wait) record a code in the workspace's status word, read with
+ * exl3_device_status().  No entry synchronises the stream and no entry
+ * allocates device memory except where stated; work buffers are
+ * caller-owned workspaces sized by the matching *_workspace_size query.
+ *
+ * Packed EXL3 tensor (reference: vcruz305/vllm-exl3
+ * src/vllm_exl3/exl3.py:4405-4481, :113-117): trellis int16
+ * [in/16][out/16][16*K], suh fp16 [in], svh fp16 [out]; codebook
+ * 0 = 3INST, 1 = MCG, 2 = mul1.  in and out are multiples of 128.
+ *
+ * dtype codes: 0 = fp32, 1 = fp16, 2 = bf16, 3 = int32, 4 = int64.
+ */
+#ifndef EXL3_B200_H
+#define EXL3_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EXL3_B200_ABI_VERSION 1
+
+enum {
+    EXL3_OK = 0,
+    EXL3_ERR_ARG = 1,       /* invalid argument, rejected before launch */
+    EXL3_ERR_CUDA = 2,      /* CUDA runtime error at launch */
+    EXL3_ERR_WORKSPACE = 3  /* workspace missing or too small */
+};
+
+enum { EXL3_DT_F32 = 0, EXL3_DT_F16 = 1, EXL3_DT_BF16 = 2, EXL3_DT_I32 = 3, EXL3_DT_I64 = 4 };
+enum { EXL3_CB_3INST = 0, EXL3_CB_MCG = 1, EXL3_CB_MUL1 = 2 };
+enum { EXL3_ACT_SILU = 0, EXL3_ACT_SWIGLU_OAI = 3 };
+
+int exl3_abi_version(void);
+const char* exl3_last_error(void);
+
+/* Device status word of a workspace (0 = clean); `clear` resets it.  Reads
+ * device memory synchronously on `stream`. */
+int exl3_device_status(const void* workspace, int clear, void* stream, int* status_out);
+
+/* Replaces dequant_trellis (csrc/bindings.cpp:117-132, CPU dequant_cpu
+ * :15-100): W = diag(suh) H W~ H diag(svh) / 128 as fp16 [in][out],
+ * bit-identical to the reference's CPU result.  K in 2..8. */
+int exl3_reconstruct(const void* trellis, const void* suh, const void* svh, int64_t in_features,
+                     int64_t out_features, int K, int codebook, void* w_out, void* stream);
+
+/* Replaces ExLlamaV3 `reconstruct` (call sites src/vllm_exl3/exl3.py:3130-3156):
+ * the decoded W~ as fp16 [in][out], no rotation. */
+int exl3_decode_raw(const void* trellis, int64_t in_features, int64_t out_features, int K,
+                    int codebook, void* w_out, void* stream);
+
+/* Replaces ExLlamaV3 `had_r_128` (call sites src/vllm_exl3/exl3.py:3039-3156):
+ * y = fp16(H128(x o pre) / sqrt(128) o post * scale) per 128-column block of
+ * fp16 rows; pre and post may be NULL; y may alias x. */
+int exl3_had128(const void* x, void* y, int64_t rows, int64_t n, const void* pre, const void* post,
+                float scale, void* stream);
+
+/* Replaces exl3_gemv (csrc/bindings.cpp:134-147, csrc/exl3_gemv.cu:23-63) and
+ * exl3_gemm (csrc/exl3_gemm.cu:9-31): y[m][out] = x[m][in] W for any m.
+ * x fp16/bf16/fp32 (cast to fp16 as the reference does), y in y_dtype. */
+size_t exl3_linear_workspace_size(int64_t m, int64_t in_features, int64_t out_features, int K);
+int exl3_linear(const void* x, int x_dtype, int64_t m, const void* trellis, const void* suh,
+                const void* svh, int64_t in_features, int64_t out_features, int K, int codebook,
+                void* y, int y_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Replaces p2b_fused_moe / p2b_fused_moe_mk / p2b_fused_moe_padded
+ * (csrc/bindings.cpp:158-241, csrc/p2b_moe.cu:643-2428) and ExLlamaV3
+ * exl3_moe / exl3_moe_mixedk (call sites src/vllm_exl3/exl3.py:3495-3579):
+ * the routed-expert layer for ALL tokens in one call,
+ *   out[t] = sum_k w[t][k] * down_e(act(gate_e(x[t]), up_e(x[t]))),  e = local(ids[t][k]).
+ * Pointer tables: nine int64 device arrays [n_table] of per-expert data
+ * pointers, the layout of build_exl3_fused_state (exl3.py:2475-2508).
+ * K: per-expert int8 device tables k_gate/k_up/k_down [n_table] (mixed-K,
+ * p2b_fused_moe_mk) or, when they are NULL, the uniform k_uniform.
+ * ids [tokens][topk] int32/int64 global expert ids; expert_map (int32
+ * [n_global], may be NULL) maps them to local ids (exl3.py:2332-2354); ids
+ * that are negative, out of range or map outside [0, n_local) are skipped.
+ * n_valid (int32[1] device, may be NULL) limits live tokens; rows at or past
+ * it are written as zeros (p2b_fused_moe_padded).  swiglu_limit > 0 clamps
+ * gate from above and up on both sides (p2b_moe.cu:755-768).  out [tokens][hidden]
+ * in out_dtype.  `kmax` bounds every K in the tables (2..8). */
+size_t exl3_moe_workspace_size(int64_t tokens, int topk, int64_t hidden, int64_t intermediate,
+                               int n_local, int kmax);
+int exl3_moe_forward(const void* x, int x_dtype, int64_t tokens, int64_t hidden,
+                     int64_t intermediate, const int64_t* gate_trellis_ptrs,
+                     const int64_t* gate_suh_ptrs, const int64_t* gate_svh_ptrs,
+                     const int64_t* up_trellis_ptrs, const int64_t* up_suh_ptrs,
+                     const int64_t* up_svh_ptrs, const int64_t* down_trellis_ptrs,
+                     const int64_t* down_suh_ptrs, const int64_t* down_svh_ptrs,
+                     const void* topk_ids, int ids_dtype, const void* topk_weights, int w_dtype,
+                     int topk, const int32_t* expert_map, int64_t n_global, const int8_t* k_gate,
+                     const int8_t* k_up, const int8_t* k_down, int k_uniform, int kmax,
+                     int n_local, int codebook, int activation, float swiglu_limit,
+                     const int32_t* n_valid, void* out, int out_dtype, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXL3_B200_H */

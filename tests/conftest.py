@@ -1,0 +1,41 @@
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "vllm-exl3_b200")
+ORACLE = os.path.join(ROOT, "oracle")
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+for p in (PKG, ORACLE):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200); run with -m gpu")
+
+
+def cuda_ok() -> bool:
+    try:
+        import torch
+        return torch.cuda.is_available()
+    except Exception:
+        return False
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    if not cuda_ok():
+        pytest.skip("CUDA GPU required")
+    import torch
+    return torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="session")
+def native(cuda):
+    """The drop-in module on a GPU box; the CUDA library must load (no fallback)."""
+    import vllm_exl3_c
+    from exl3_b200 import _native
+    _native.load()
+    return vllm_exl3_c

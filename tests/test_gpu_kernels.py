@@ -1,0 +1,135 @@
+"""GPU parity of the decode kernels against the CPU oracle, through the C ABI.
+
+* exl3_reconstruct (dequant_trellis): bit-exact with the oracle and with the
+  reference fixtures, K 2..8 x codebooks 3INST/MCG/mul1;
+* exl3_decode_raw: bit-exact W~;
+* had_r_128: fp32 FWHT reference;
+* exl3_linear / exl3_gemv / exl3_gemm: dense fp32 matmul with the oracle's
+  fp16 weights; tolerance max|d| <= 2e-2 * RMS(ref) and cosine >= 0.9995.
+"""
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+import cpu_oracle as oracle
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+
+def _rand_packed(rng, in_f, out_f, K):
+    t = rng.integers(-32768, 32768, (in_f // 16, out_f // 16, 16 * K), dtype=np.int16)
+    u = (rng.integers(0, 2, in_f) * 2 - 1).astype(np.float16)
+    v = ((rng.integers(0, 2, out_f) * 2 - 1) * np.float16(0.75 / np.sqrt(in_f))).astype(np.float16)
+    return t, u, v
+
+
+def _close(actual, expected):
+    a = np.asarray(actual, np.float64).ravel()
+    e = np.asarray(expected, np.float64).ravel()
+    rms = np.sqrt(np.mean(e * e))
+    maxd = np.max(np.abs(a - e))
+    cos = float(a @ e / (np.linalg.norm(a) * np.linalg.norm(e) + 1e-30))
+    assert np.isfinite(a).all()
+    assert maxd <= 2e-2 * rms, f"max|d| {maxd:.3e} > 2e-2 * rms {rms:.3e}"
+    assert cos >= 0.9995, f"cosine {cos}"
+    return maxd / rms, cos
+
+
+@pytest.mark.parametrize("K", [2, 3, 4, 5, 6, 7, 8])
+@pytest.mark.parametrize("cb", [0, 1, 2])
+def test_reconstruct_bit_exact(native, cuda, K, cb):
+    import torch
+    rng = np.random.default_rng(100 + 10 * K + cb)
+    t, u, v = _rand_packed(rng, 256, 384, K)
+    want = oracle.dequant(t, u, v, K, cb=cb)
+    got = native.exl3_reconstruct(torch.from_numpy(t).to(cuda), torch.from_numpy(u).to(cuda),
+                                  torch.from_numpy(v).to(cuda), K, cb).cpu().numpy()
+    assert np.array_equal(got.view(np.uint16), want.view(np.uint16))
+    raw = native.exl3_decode_raw(torch.from_numpy(t).to(cuda), K, cb).cpu().numpy()
+    assert np.array_equal(raw.view(np.uint16), oracle.decode_raw(t, K, cb).view(np.uint16))
+
+
+def test_dequant_trellis_matches_reference_fixtures(native, cuda):
+    import torch
+    data = np.load(os.path.join(GOLDEN, "dequant.npz"))
+    with open(os.path.join(GOLDEN, "dequant_cases.json")) as f:
+        cases = json.load(f)
+    import hashlib
+    for c in cases:
+        tag = c["tag"]
+        w = native.dequant_trellis(torch.from_numpy(data[tag + "_trellis"]).to(cuda),
+                                   torch.from_numpy(data[tag + "_suh"]).to(cuda),
+                                   torch.from_numpy(data[tag + "_svh"]).to(cuda), c["K"], c["mcg"])
+        w = w.cpu().numpy()
+        assert hashlib.sha256(w.view(np.uint16).tobytes()).hexdigest() == c["sha256"], tag
+
+
+def test_dequant_trellis_rejects_bad_arguments(native, cuda):
+    import torch
+    t = torch.zeros((8, 8, 64), dtype=torch.int16, device=cuda)
+    ones = torch.ones(128, dtype=torch.float16, device=cuda)
+    with pytest.raises(RuntimeError, match="K must be one of"):
+        native.dequant_trellis(torch.zeros((8, 8, 80), dtype=torch.int16, device=cuda), ones, ones, 5, True)
+    with pytest.raises(RuntimeError, match="16\\*K"):
+        native.dequant_trellis(t, ones, ones, 3, True)
+    with pytest.raises(RuntimeError, match="float16"):
+        native.dequant_trellis(t, ones.float(), ones, 4, True)
+    with pytest.raises(RuntimeError, match="Hadamard"):
+        native.dequant_trellis(torch.zeros((4, 8, 64), dtype=torch.int16, device=cuda), ones, ones, 4, True)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        native.dequant_trellis(t.cpu(), ones.cpu(), ones.cpu(), 4, True)
+
+
+def test_had_r_128(native, cuda):
+    import torch
+    rng = np.random.default_rng(7)
+    x = rng.normal(0, 1, (5, 384)).astype(np.float16)
+    pre = (rng.integers(0, 2, 384) * 2 - 1).astype(np.float16)
+    post = rng.uniform(0.5, 1.5, 384).astype(np.float16)
+    H = np.array([[1.0]])
+    for _ in range(7):
+        H = np.block([[H, H], [H, -H]])
+    xf = x.astype(np.float64) * pre.astype(np.float64)
+    want = np.concatenate([xf[:, b * 128:(b + 1) * 128] @ H for b in range(3)], axis=1) / np.sqrt(128)
+    want = want * post.astype(np.float64) * 0.5
+    xt = torch.from_numpy(x).to(cuda)
+    y = torch.empty_like(xt)
+    native.had_r_128(xt, y, torch.from_numpy(pre).to(cuda), torch.from_numpy(post).to(cuda), 0.5)
+    np.testing.assert_allclose(y.cpu().numpy().astype(np.float64), want, rtol=2e-3, atol=2e-3)
+
+
+@pytest.mark.parametrize("m", [1, 5, 8, 16, 17, 40])
+@pytest.mark.parametrize("K,cb", [(2, 1), (3, 1), (4, 1), (3, 2), (4, 2), (8, 1)])
+def test_linear_matches_dense(native, cuda, m, K, cb):
+    import torch
+    rng = np.random.default_rng(1000 * m + 10 * K + cb)
+    in_f, out_f = 512, 384
+    t, u, v = _rand_packed(rng, in_f, out_f, K)
+    w = oracle.dequant(t, u, v, K, cb=cb).astype(np.float32)
+    x = rng.normal(0, 1, (m, in_f)).astype(np.float32)
+    want = x.astype(np.float16).astype(np.float32) @ w
+    y = native.exl3_linear(torch.from_numpy(x).to(cuda), torch.from_numpy(t).to(cuda),
+                           torch.from_numpy(u).to(cuda), torch.from_numpy(v).to(cuda), K, cb,
+                           out_dtype=torch.float32)
+    _close(y.cpu().numpy(), want)
+
+
+def test_gemv_and_gemm_entries(native, cuda):
+    import torch
+    rng = np.random.default_rng(3)
+    t, u, v = _rand_packed(rng, 256, 256, 4)
+    w = oracle.dequant(t, u, v, 4, True).astype(np.float32)
+    dev = lambda a: torch.from_numpy(a).to(cuda)
+    x = rng.normal(0, 1, (6, 256)).astype(np.float16)
+    y = native.exl3_gemv(dev(x), dev(t), dev(u), dev(v), 4, True)
+    assert y.dtype == torch.float16 and y.shape == (6, 256)
+    _close(y.float().cpu().numpy(), x.astype(np.float32) @ w)
+    with pytest.raises(RuntimeError, match="1 <= m <= 8"):
+        native.exl3_gemv(dev(np.zeros((9, 256), np.float16)), dev(t), dev(u), dev(v), 4, True)
+    x2 = rng.normal(0, 1, (2, 33, 256)).astype(np.float16)
+    y2 = native.exl3_gemm(dev(x2), dev(t), dev(u), dev(v), 4, True)
+    _close(y2.float().cpu().numpy().reshape(-1, 256), x2.reshape(-1, 256).astype(np.float32) @ w)

@@ -1,0 +1,222 @@
+// capi.cu -- the extern "C" boundary (include/exl3_b200.h).  Host-side
+// validation mirrors the reference's TORCH_CHECKs (csrc/bindings.cpp:117-147,
+// csrc/p2b_moe.cu:2437-2466, 2346-2428): everything is rejected before launch
+// with a message; nothing here reads device memory except exl3_device_status.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/exl3_b200.h"
+#include "exl3_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(EXL3_ERR_CUDA, "%s: CUDA error %d (%s)", what, int(e), cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+bool float_dtype(int d) { return d == EXL3_DT_F32 || d == EXL3_DT_F16 || d == EXL3_DT_BF16; }
+
+int check_packed(const char* who, const void* trellis, const void* suh, const void* svh,
+                 int64_t in_f, int64_t out_f, int K, int cb) {
+    if (!trellis || !suh || !svh) return fail(EXL3_ERR_ARG, "%s: null trellis/suh/svh pointer", who);
+    if (K < 2 || K > 8) return fail(EXL3_ERR_ARG, "%s: K must be in 2..8 (got %d)", who, K);
+    if (cb < 0 || cb > 2) return fail(EXL3_ERR_ARG, "%s: codebook must be 0, 1 or 2 (got %d)", who, cb);
+    if (in_f <= 0 || out_f <= 0 || in_f % 128 || out_f % 128)
+        return fail(EXL3_ERR_ARG,
+                    "%s: trellis dimensions must reconstruct whole 128-element Hadamard blocks "
+                    "(in=%lld out=%lld)",
+                    who, (long long)in_f, (long long)out_f);
+    if (!aligned(trellis, 16)) return fail(EXL3_ERR_ARG, "%s: trellis must be 16-byte aligned", who);
+    if (!aligned(suh, 2) || !aligned(svh, 2)) return fail(EXL3_ERR_ARG, "%s: suh/svh misaligned", who);
+    return EXL3_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int exl3_abi_version(void) { return EXL3_B200_ABI_VERSION; }
+
+const char* exl3_last_error(void) { return g_last_error.c_str(); }
+
+int exl3_device_status(const void* workspace, int clear, void* stream, int* status_out) {
+    if (!workspace || !status_out) return fail(EXL3_ERR_ARG, "exl3_device_status: null argument");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int v = 0;
+    cudaError_t e = cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "exl3_device_status");
+    if (clear && v) {
+        e = cudaMemsetAsync(const_cast<void*>(workspace), 0, sizeof(int), s);
+        if (e != cudaSuccess) return cuda_fail(e, "exl3_device_status");
+    }
+    *status_out = v;
+    return EXL3_OK;
+}
+
+int exl3_reconstruct(const void* trellis, const void* suh, const void* svh, int64_t in_f, int64_t out_f,
+                     int K, int cb, void* w_out, void* stream) {
+    if (int rc = check_packed("exl3_reconstruct", trellis, suh, svh, in_f, out_f, K, cb)) return rc;
+    if (!w_out) return fail(EXL3_ERR_ARG, "exl3_reconstruct: null output");
+    cudaError_t e = exl3::run_reconstruct(K, cb, true, trellis, suh, svh, in_f, out_f, w_out,
+                                          static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, "exl3_reconstruct");
+}
+
+int exl3_decode_raw(const void* trellis, int64_t in_f, int64_t out_f, int K, int cb, void* w_out,
+                    void* stream) {
+    static const uint16_t one = 0x3c00;  // placeholder scales: unused by the raw decode
+    if (int rc = check_packed("exl3_decode_raw", trellis, &one, &one, in_f, out_f, K, cb)) return rc;
+    if (!w_out) return fail(EXL3_ERR_ARG, "exl3_decode_raw: null output");
+    cudaError_t e = exl3::run_reconstruct(K, cb, false, trellis, nullptr, nullptr, in_f, out_f, w_out,
+                                          static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, "exl3_decode_raw");
+}
+
+int exl3_had128(const void* x, void* y, int64_t rows, int64_t n, const void* pre, const void* post,
+                float scale, void* stream) {
+    if (!x || !y) return fail(EXL3_ERR_ARG, "exl3_had128: null input/output");
+    if (rows < 0 || n <= 0 || n % 128)
+        return fail(EXL3_ERR_ARG, "exl3_had128: row width must be a positive multiple of 128");
+    if (!std::isfinite(scale)) return fail(EXL3_ERR_ARG, "exl3_had128: scale must be finite");
+    if (rows == 0) return EXL3_OK;
+    cudaError_t e = exl3::run_had128(x, y, rows, n, pre, post, scale, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, "exl3_had128");
+}
+
+size_t exl3_linear_workspace_size(int64_t m, int64_t in_f, int64_t out_f, int K) {
+    exl3::MoePlan p;
+    if (m < 1 || in_f > INT32_MAX || out_f > INT32_MAX) return 0;
+    if (!exl3::plan_moe(p, m, 1, int(in_f), int(out_f), 1, K < 2 ? 8 : K, true, exl3::num_sms_current()))
+        return 0;
+    return p.total;
+}
+
+int exl3_linear(const void* x, int x_dtype, int64_t m, const void* trellis, const void* suh,
+                const void* svh, int64_t in_f, int64_t out_f, int K, int cb, void* y, int y_dtype,
+                void* ws, size_t ws_bytes, void* stream) {
+    if (int rc = check_packed("exl3_linear", trellis, suh, svh, in_f, out_f, K, cb)) return rc;
+    if (!x || !y) return fail(EXL3_ERR_ARG, "exl3_linear: null x/y");
+    if (!float_dtype(x_dtype) || !float_dtype(y_dtype))
+        return fail(EXL3_ERR_ARG, "exl3_linear: x/y dtype must be fp32, fp16 or bf16");
+    if (m < 0) return fail(EXL3_ERR_ARG, "exl3_linear: m must be >= 0");
+    if (m == 0) return EXL3_OK;
+    if (in_f > INT32_MAX || out_f > INT32_MAX || m * in_f > (int64_t(1) << 40))
+        return fail(EXL3_ERR_ARG, "exl3_linear: dimensions exceed kernel indexing");
+    exl3::MoePlan p;
+    if (!exl3::plan_moe(p, m, 1, int(in_f), int(out_f), 1, K, true, exl3::num_sms_current()))
+        return fail(EXL3_ERR_ARG, "exl3_linear: unsupported geometry");
+    if (!ws || ws_bytes < p.total)
+        return fail(EXL3_ERR_WORKSPACE, "exl3_linear: workspace of %zu bytes required (got %zu)", p.total,
+                    ws_bytes);
+    if (!aligned(ws, 256)) return fail(EXL3_ERR_WORKSPACE, "exl3_linear: workspace must be 256-byte aligned");
+    exl3::MoeCall c;
+    c.x = x;
+    c.x_dtype = x_dtype;
+    c.up.trellis = trellis;
+    c.up.suh = suh;
+    c.up.svh = svh;
+    c.up.k_uniform = K;
+    c.cb = cb;
+    c.out = y;
+    c.out_dtype = y_dtype;
+    cudaError_t e = exl3::run_moe(p, c, ws, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, "exl3_linear");
+}
+
+size_t exl3_moe_workspace_size(int64_t tokens, int topk, int64_t hidden, int64_t inter, int n_local,
+                               int kmax) {
+    exl3::MoePlan p;
+    if (hidden > INT32_MAX || inter > INT32_MAX) return 0;
+    if (!exl3::plan_moe(p, tokens, topk, int(hidden), int(inter), n_local, kmax, false,
+                        exl3::num_sms_current()))
+        return 0;
+    return p.total;
+}
+
+int exl3_moe_forward(const void* x, int x_dtype, int64_t tokens, int64_t hidden, int64_t inter,
+                     const int64_t* gt, const int64_t* gu, const int64_t* gv, const int64_t* ut,
+                     const int64_t* uu, const int64_t* uv, const int64_t* dt, const int64_t* du,
+                     const int64_t* dv, const void* ids, int ids_dtype, const void* weights,
+                     int w_dtype, int topk, const int32_t* expert_map, int64_t n_global,
+                     const int8_t* kg, const int8_t* ku, const int8_t* kd, int k_uniform, int kmax,
+                     int n_local, int cb, int act, float limit, const int32_t* n_valid, void* out,
+                     int out_dtype, void* ws, size_t ws_bytes, void* stream) {
+    const char* who = "fused MoE";
+    if (!x || !out) return fail(EXL3_ERR_ARG, "%s: null x/out", who);
+    if (!gt || !gu || !gv || !ut || !uu || !uv || !dt || !du || !dv)
+        return fail(EXL3_ERR_ARG, "%s: null pointer table", who);
+    if (!ids || !weights) return fail(EXL3_ERR_ARG, "%s: null routing tensors", who);
+    if (!float_dtype(x_dtype) || !float_dtype(out_dtype) || !float_dtype(w_dtype))
+        return fail(EXL3_ERR_ARG, "%s: x/out/weights dtype must be fp32, fp16 or bf16", who);
+    if (ids_dtype != EXL3_DT_I32 && ids_dtype != EXL3_DT_I64)
+        return fail(EXL3_ERR_ARG, "%s: expert ids must be int32 or int64", who);
+    if (tokens < 0) return fail(EXL3_ERR_ARG, "%s: tokens must be >= 0", who);
+    if (hidden <= 0 || hidden % 128 || hidden > INT32_MAX)
+        return fail(EXL3_ERR_ARG, "%s hidden width must be a positive multiple of 128", who);
+    if (inter <= 0 || inter % 128 || inter > INT32_MAX)
+        return fail(EXL3_ERR_ARG, "%s local intermediate width must be a positive multiple of 128", who);
+    if (topk < 1) return fail(EXL3_ERR_ARG, "%s: topk must be >= 1", who);
+    if (n_local < 1 || n_local > 2048) return fail(EXL3_ERR_ARG, "%s: n_local must be in 1..2048", who);
+    if (!std::isfinite(limit) || limit < 0.f)
+        return fail(EXL3_ERR_ARG,
+                    "%s SwiGLU limit must be finite and nonnegative (0 disables clipping)", who);
+    if (cb < 0 || cb > 2) return fail(EXL3_ERR_ARG, "%s: codebook must be 0, 1 or 2", who);
+    if (act != EXL3_ACT_SILU && act != EXL3_ACT_SWIGLU_OAI)
+        return fail(EXL3_ERR_ARG, "%s: unsupported activation %d", who, act);
+    if (kmax < 2 || kmax > 8) return fail(EXL3_ERR_ARG, "%s: kmax must be in 2..8", who);
+    const bool tables = kg || ku || kd;
+    if (tables && !(kg && ku && kd))
+        return fail(EXL3_ERR_ARG, "%s: K tables must be given together", who);
+    if (!tables && (k_uniform < 2 || k_uniform > kmax))
+        return fail(EXL3_ERR_ARG, "%s: uniform K must be in 2..kmax", who);
+    if (expert_map && n_global < 1) return fail(EXL3_ERR_ARG, "%s: expert_map needs n_global >= 1", who);
+    if (tokens == 0) return EXL3_OK;
+    exl3::MoePlan p;
+    if (!exl3::plan_moe(p, tokens, topk, int(hidden), int(inter), n_local, kmax, false,
+                        exl3::num_sms_current()))
+        return fail(EXL3_ERR_ARG, "%s: unsupported geometry", who);
+    if (!ws || ws_bytes < p.total)
+        return fail(EXL3_ERR_WORKSPACE, "%s: workspace of %zu bytes required (got %zu)", who, p.total,
+                    ws_bytes);
+    if (!aligned(ws, 256)) return fail(EXL3_ERR_WORKSPACE, "%s: workspace must be 256-byte aligned", who);
+
+    exl3::MoeCall c;
+    c.x = x;
+    c.x_dtype = x_dtype;
+    c.ids = ids;
+    c.ids_dtype = ids_dtype;
+    c.weights = weights;
+    c.w_dtype = w_dtype;
+    c.expert_map = expert_map;
+    c.n_global = n_global;
+    c.n_valid = n_valid;
+    c.gate = {gt, gu, gv, kg, nullptr, nullptr, nullptr, k_uniform};
+    c.up = {ut, uu, uv, ku, nullptr, nullptr, nullptr, k_uniform};
+    c.down = {dt, du, dv, kd, nullptr, nullptr, nullptr, k_uniform};
+    c.cb = cb;
+    c.act = act;
+    c.limit = limit;
+    c.out = out;
+    c.out_dtype = out_dtype;
+    cudaError_t e = exl3::run_moe(p, c, ws, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, "fused MoE launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,85 @@
+// exl3_internal.h -- host-side launch plans shared by the kernels and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace exl3 {
+
+constexpr int kRowsPerSlot = 16;  // token rows one expert work slot carries (two m16n8 mma columns)
+constexpr int kKtPerStage = 8;    // k-tiles (16 input features each) per pipeline stage = one 128 block
+
+// One projection family (gate, up or down) of a layer: either per-expert
+// pointer tables (int64 device arrays of data_ptr values, the reference's
+// build_exl3_fused_state layout, src/vllm_exl3/exl3.py:2475-2508) or, for a
+// dense linear, direct pointers.
+struct ProjRef {
+    const int64_t* trellis_tbl = nullptr;
+    const int64_t* suh_tbl = nullptr;
+    const int64_t* svh_tbl = nullptr;
+    const int8_t* k_tbl = nullptr;  // per-expert K; nullptr -> k_uniform
+    const void* trellis = nullptr;  // direct (dense linear)
+    const void* suh = nullptr;
+    const void* svh = nullptr;
+    int k_uniform = 0;
+};
+
+// Workspace carve-up for one forward call.  All offsets are bytes from the
+// workspace base, 256-byte aligned.
+struct MoePlan {
+    // geometry
+    int64_t t_max = 0;  // token rows of x / out
+    int topk = 0;
+    int hidden = 0;
+    int inter = 0;
+    int n_local = 0;
+    int kmax = 8;
+    bool linear = false;  // dense linear: one expert, topk 1, no activation
+    int64_t routes = 0;   // t_max * topk
+    int64_t rpad = 0;     // sorted rows incl. per-expert padding to 16
+    int64_t smax = 0;     // max work slots
+    // per phase: column blocks, k splits, k-tiles per split, grid
+    int ncb1 = 0, nsplit1 = 1, ktps1 = 0, grid1 = 0, stages1 = 0;
+    int ncb2 = 0, nsplit2 = 1, ktps2 = 0, grid2 = 0, stages2 = 0;
+    size_t smem1 = 0, smem2 = 0;
+    // offsets
+    size_t off_status = 0, off_nslots = 0, off_slots = 0, off_route_pos = 0, off_sorted_tok = 0,
+           off_sorted_exp = 0, off_sorted_w = 0, off_xr = 0, off_a2 = 0, off_yd = 0,
+           off_part1 = 0, off_part2 = 0, off_cnt1 = 0, off_cnt2 = 0;
+    size_t total = 0;
+};
+
+// Fill a plan; returns false if the geometry is unsupported.
+bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_local, int kmax,
+              bool linear, int num_sms);
+
+struct MoeCall {
+    const void* x = nullptr;
+    int x_dtype = 1;
+    const void* ids = nullptr;
+    int ids_dtype = 3;
+    const void* weights = nullptr;
+    int w_dtype = 0;
+    const int32_t* expert_map = nullptr;
+    int64_t n_global = 0;
+    const int32_t* n_valid = nullptr;
+    ProjRef gate, up, down;
+    int cb = 1;
+    int act = 0;
+    float limit = 0.f;
+    void* out = nullptr;
+    int out_dtype = 0;
+    bool gateless = false;
+};
+
+cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s);
+
+cudaError_t run_reconstruct(int K, int cb, bool full, const void* trellis, const void* suh,
+                            const void* svh, int64_t in_f, int64_t out_f, void* w, cudaStream_t s);
+cudaError_t run_had128(const void* x, void* y, int64_t rows, int64_t n, const void* pre,
+                       const void* post, float scale, cudaStream_t s);
+
+int num_sms_current();
+
+}  // namespace exl3

@@ -1,0 +1,885 @@
+// moe.cu -- routed-expert EXL3 MoE forward (all tokens of a step in one
+// pass) and the dense EXL3 linear, for sm_100a.
+//
+// Replaces the reference's per-token cooperative kernels p2b_fused_moe /
+// p2b_fused_moe_mk / p2b_fused_moe_padded (csrc/p2b_moe.cu:643-2428), the
+// m <= 8 GEMV exl3_gemv (csrc/exl3_gemv.cu:23-63) and its row-chunk loop
+// exl3_gemm (csrc/exl3_gemm.cu:9-31).  The math is the reference's eager
+// loop apply_exl3_python_loop (src/vllm_exl3/exl3.py:2357-2413):
+//   per route (token t, local expert e, weight w):
+//     g = x_t W_gate,e ; u = x_t W_up,e ; a = fp16(silu(min(g,L)) * clamp(u,L))
+//     out_t += w * (a W_down,e)
+// computed in the rotated domain x W = ((x o suh) H / sqrt128) W~ (H / sqrt128) o svh.
+//
+// Kernels, in stream order (no host synchronisation, graph-capturable):
+//  1. prep     one CTA: map ids to local experts (expert_map, n_local
+//              sentinel; exl3.py:2332-2354), stable counting sort of routes
+//              by expert, each expert's rows padded to 16, work slots of <= 16
+//              rows, split-K counters cleared.
+//  2. rotate   fp16 H128(x o suh)/sqrt128 per (route, projection, 128-block),
+//              stored [proj][kblock][row][128] with a 16-byte XOR swizzle so a
+//              1-D bulk copy lands conflict-free for ldmatrix.
+//  3. gemv<2>  gate+up: work item = (slot, 128-column block, k split).  A
+//              producer thread streams the item's trellis rows and rotated
+//              inputs into a shared-memory ring with cp.async.bulk; 16 consumer
+//              warps (projection x 16-column tile) decode each 16x16 tile in
+//              registers straight into mma.m16n8k16 A fragments and
+//              accumulate in fp32.  Split-K partials are reduced in fixed order
+//              by the last CTA of the group (deterministic).  Epilogue: output
+//              FWHT o svh, SwiGLU (+clamp), fp16 round, down-input rotation
+//              o suh_down -> rotated down inputs.
+//  4. gemv<1>  down: same engine; epilogue FWHT o svh * route weight -> per-route rows.
+//  5. combine  out_t = sum over t's routes in top-k order (no atomics).
+#include <algorithm>
+
+#include "exl3_common.cuh"
+#include "exl3_internal.h"
+
+namespace exl3 {
+
+enum Epi : int { EPI_GATEUP = 0, EPI_DOWN = 1, EPI_LINEAR = 2 };
+enum Act : int { ACT_SILU = 0, ACT_SWIGLU_OAI = 3 };
+
+constexpr int kPrepThreads = 1024;
+constexpr int kMaxLocal = 2048;
+constexpr int kYsPitch = 132;  // fp32 pitch of the epilogue tile (conflict-free fragment stores)
+
+struct WsPtrs {
+    int* status;
+    int* nslots;
+    int4* slots;  // {expert, first sorted row, rows, 0}
+    int* route_pos;
+    int* sorted_tok;
+    int* sorted_exp;
+    float* sorted_w;
+    __half* xr;
+    __half* a2;
+    float* yd;
+    float* part1;
+    float* part2;
+    int* cnt1;
+    int* cnt2;
+};
+
+static WsPtrs ws_ptrs(const MoePlan& p, void* ws) {
+    char* b = static_cast<char*>(ws);
+    WsPtrs w;
+    w.status = reinterpret_cast<int*>(b + p.off_status);
+    w.nslots = reinterpret_cast<int*>(b + p.off_nslots);
+    w.slots = reinterpret_cast<int4*>(b + p.off_slots);
+    w.route_pos = reinterpret_cast<int*>(b + p.off_route_pos);
+    w.sorted_tok = reinterpret_cast<int*>(b + p.off_sorted_tok);
+    w.sorted_exp = reinterpret_cast<int*>(b + p.off_sorted_exp);
+    w.sorted_w = reinterpret_cast<float*>(b + p.off_sorted_w);
+    w.xr = reinterpret_cast<__half*>(b + p.off_xr);
+    w.a2 = reinterpret_cast<__half*>(b + p.off_a2);
+    w.yd = reinterpret_cast<float*>(b + p.off_yd);
+    w.part1 = reinterpret_cast<float*>(b + p.off_part1);
+    w.part2 = reinterpret_cast<float*>(b + p.off_part2);
+    w.cnt1 = reinterpret_cast<int*>(b + p.off_cnt1);
+    w.cnt2 = reinterpret_cast<int*>(b + p.off_cnt2);
+    return w;
+}
+
+// ---------------------------------------------------------------------------
+// 1. routing prep
+// ---------------------------------------------------------------------------
+struct PrepArgs {
+    const void* ids;
+    int ids_dtype;
+    const void* weights;
+    int w_dtype;
+    const int32_t* expert_map;
+    int64_t n_global;
+    const int32_t* n_valid;
+    int64_t t_max;
+    int topk;
+    int n_local;
+    int linear;
+    int cnt1_n;
+    int cnt2_n;
+    WsPtrs w;
+};
+
+__device__ __forceinline__ int local_expert(const PrepArgs& a, int64_t r) {
+    if (a.linear) return 0;
+    const int64_t g = load_id(a.ids, r, a.ids_dtype);
+    int64_t e = g;
+    if (a.expert_map) e = (g >= 0 && g < a.n_global) ? int64_t(a.expert_map[g]) : -1;
+    return (e >= 0 && e < a.n_local) ? int(e) : -1;
+}
+
+// Block-wide exclusive scan of one int per thread (kPrepThreads threads).
+__device__ int block_excl_scan(int v, int* total, int* sh32) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+    #pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) sh32[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int s = sh32[lane];
+        #pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += y;
+        }
+        sh32[lane] = s;
+    }
+    __syncthreads();
+    const int warp_prefix = warp ? sh32[warp - 1] : 0;
+    *total = sh32[31];
+    __syncthreads();
+    return warp_prefix + x - v;
+}
+
+__global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
+    __shared__ int cnt[kMaxLocal];
+    __shared__ int poff[kMaxLocal];
+    __shared__ int sh32[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int E = a.n_local;
+    int64_t T = a.t_max;
+    if (a.n_valid) T = min(T, int64_t(max(0, *a.n_valid)));
+    const int64_t R = T * a.topk, Rmax = a.t_max * a.topk;
+
+    for (int i = tid; i < a.cnt1_n; i += kPrepThreads) a.w.cnt1[i] = 0;
+    for (int i = tid; i < a.cnt2_n; i += kPrepThreads) a.w.cnt2[i] = 0;
+    for (int e = tid; e < E; e += kPrepThreads) cnt[e] = 0;
+    __syncthreads();
+    for (int64_t r = tid; r < R; r += kPrepThreads) {
+        const int e = local_expert(a, r);
+        if (e >= 0) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+
+    // padded row offsets and slot offsets
+    const int per = (E + kPrepThreads - 1) / kPrepThreads;
+    const int e0 = min(E, tid * per), e1 = min(E, e0 + per);
+    int sp = 0, ss = 0;
+    for (int e = e0; e < e1; ++e) {
+        sp += (cnt[e] + 15) & ~15;
+        ss += (cnt[e] + 15) >> 4;
+    }
+    int tot_p, tot_s;
+    int xp = block_excl_scan(sp, &tot_p, sh32);
+    int xs = block_excl_scan(ss, &tot_s, sh32);
+    for (int e = e0; e < e1; ++e) {
+        const int n = cnt[e];
+        poff[e] = xp;
+        for (int j = 0; j < ((n + 15) >> 4); ++j)
+            a.w.slots[xs + j] = make_int4(e, xp + 16 * j, min(16, n - 16 * j), 0);
+        for (int q = xp + n; q < xp + ((n + 15) & ~15); ++q) {
+            a.w.sorted_tok[q] = -1;
+            a.w.sorted_exp[q] = e;
+            a.w.sorted_w[q] = 0.f;
+        }
+        xp += (n + 15) & ~15;
+        xs += (n + 15) >> 4;
+    }
+    if (tid == 0) *a.w.nslots = tot_s;
+    __syncthreads();
+    for (int e = tid; e < E; e += kPrepThreads) cnt[e] = poff[e];  // running position
+    __syncthreads();
+
+    // stable placement: route order within each expert
+    for (int64_t base = 0; base < R; base += kPrepThreads) {
+        const int64_t r = base + tid;
+        const int e = r < R ? local_expert(a, r) : -1;
+        const unsigned mask = __match_any_sync(0xffffffffu, e);
+        const int rank = __popc(mask & ((1u << lane) - 1u));
+        const int leader = __ffs(mask) - 1;
+        int my_base = 0;
+        for (int w = 0; w < kPrepThreads / 32; ++w) {
+            if (warp == w && e >= 0 && lane == leader) {
+                my_base = cnt[e];
+                cnt[e] += __popc(mask);
+            }
+            __syncthreads();
+        }
+        my_base = __shfl_sync(0xffffffffu, my_base, leader);
+        if (e >= 0) {
+            const int p = my_base + rank;
+            a.w.route_pos[r] = p;
+            a.w.sorted_tok[p] = int(r / a.topk);
+            a.w.sorted_exp[p] = e;
+            a.w.sorted_w[p] = a.linear ? 1.f : load_as_float(a.weights, r, a.w_dtype);
+        } else if (r < Rmax) {
+            a.w.route_pos[r] = -1;
+        }
+    }
+    for (int64_t r = R + tid; r < Rmax; r += kPrepThreads) a.w.route_pos[r] = -1;
+}
+
+// ---------------------------------------------------------------------------
+// 2. input rotation
+// ---------------------------------------------------------------------------
+struct RotArgs {
+    const void* x;
+    int x_dtype;
+    int in_f;
+    int nproj;
+    ProjRef proj[2];
+    const int* nslots;
+    const int4* slots;
+    const int* sorted_tok;
+    __half* xr;
+    int64_t rpad;
+    int* status;
+};
+
+__device__ __forceinline__ const __half* proj_suh(const ProjRef& p, int e) {
+    return p.suh_tbl ? reinterpret_cast<const __half*>(p.suh_tbl[e]) : static_cast<const __half*>(p.suh);
+}
+__device__ __forceinline__ const __half* proj_svh(const ProjRef& p, int e) {
+    return p.svh_tbl ? reinterpret_cast<const __half*>(p.svh_tbl[e]) : static_cast<const __half*>(p.svh);
+}
+__device__ __forceinline__ const uint16_t* proj_trellis(const ProjRef& p, int e) {
+    return p.trellis_tbl ? reinterpret_cast<const uint16_t*>(p.trellis_tbl[e])
+                         : static_cast<const uint16_t*>(p.trellis);
+}
+__device__ __forceinline__ int proj_k(const ProjRef& p, int e) {
+    return p.k_tbl ? int(p.k_tbl[e]) : p.k_uniform;
+}
+
+// swizzled element offset of column c in a 128-wide fp16 row of sorted row p
+__device__ __forceinline__ int swz(int c, int64_t p) {
+    return ((((c >> 3) ^ int(p & 7))) << 3) | (c & 7);
+}
+
+__global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int nkb = a.in_f / 128;
+    const int64_t per_slot = int64_t(16) * a.nproj * nkb;
+    const int64_t total = int64_t(*a.nslots) * per_slot;
+    for (int64_t it = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; it < total;
+         it += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+        const int64_t s = it / per_slot;
+        const int rem = int(it % per_slot);
+        const int row = rem / (a.nproj * nkb);
+        const int pj = (rem / nkb) % a.nproj;
+        const int kb = rem % nkb;
+        const int4 sl = a.slots[s];
+        if (row >= sl.z) continue;
+        const int64_t p = sl.y + row;
+        const int tok = a.sorted_tok[p];
+        const __half* suh = proj_suh(a.proj[pj], sl.x);
+        if (suh == nullptr || tok < 0) {
+            if (lane == 0) set_status(a.status, suh == nullptr ? DEV_NULL_PTR : DEV_BAD_ROUTE);
+            continue;
+        }
+        float v[4];
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int c = kb * 128 + lane + 32 * i;
+            // the reference casts activations to fp16 first (exl3.py:2384, 2856)
+            const float xv = __half2float(__float2half_rn(load_as_float(a.x, int64_t(tok) * a.in_f + c, a.x_dtype)));
+            v[i] = xv * __half2float(suh[c]);
+        }
+        fwht128_warp(v, lane);
+        __half* dst = a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * 128;
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) dst[swz(lane + 32 * i, p)] = __float2half_rn(v[i] * kHadNorm);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 3/4. expert GEMV engine
+// ---------------------------------------------------------------------------
+struct GemvArgs {
+    int* status;
+    ProjRef proj[2];
+    int in_f, out_f, ncb, nsplit, ktps, stages, kmax;
+    const int* nslots;
+    const int4* slots;
+    const __half* xin;
+    int64_t rpad;
+    // EPI_GATEUP
+    ProjRef down;
+    __half* a2;
+    float limit;
+    int act;
+    // EPI_DOWN
+    const float* sorted_w;
+    float* yd;
+    // EPI_LINEAR
+    void* y;
+    int y_dtype;
+    const int* sorted_tok;
+    // split-K
+    float* part;
+    int* cnt;
+};
+
+struct GemvSmem {
+    uint64_t* full;
+    uint64_t* empty;
+    int* flags;  // [0] abort, [1] last-of-group
+    float* ys;   // [NPROJ][16][kYsPitch]
+    char* stages;
+};
+
+template <int NPROJ>
+__host__ __device__ constexpr int gemv_threads() {
+    return (8 * NPROJ + 1) * 32;
+}
+
+__host__ __device__ inline size_t gemv_stage_bytes(int nproj, int kmax) {
+    return size_t(nproj) * (kKtPerStage * 8 * 32 * kmax) + size_t(nproj) * 16 * 256;
+}
+
+__host__ __device__ inline size_t gemv_fixed_bytes(int nproj, int stages) {
+    const size_t bars = (size_t(stages) * 2 * 8 + 8 * 4 + 127) & ~size_t(127);
+    const size_t ys = (size_t(nproj) * 16 * kYsPitch * 4 + 127) & ~size_t(127);
+    return bars + ys;
+}
+
+__device__ __forceinline__ GemvSmem gemv_smem(char* base, int nproj, int stages) {
+    GemvSmem s;
+    s.full = reinterpret_cast<uint64_t*>(base);
+    s.empty = s.full + stages;
+    s.flags = reinterpret_cast<int*>(s.empty + stages);
+    const size_t bars = (size_t(stages) * 2 * 8 + 8 * 4 + 127) & ~size_t(127);
+    s.ys = reinterpret_cast<float*>(base + bars);
+    s.stages = base + gemv_fixed_bytes(nproj, stages);
+    return s;
+}
+
+struct ItemInfo {
+    int e, p0, rows, cb, sp, kt0, kt1, group;
+};
+
+__device__ __forceinline__ ItemInfo gemv_item(const GemvArgs& a, int64_t it) {
+    ItemInfo I;
+    const int per = a.ncb * a.nsplit;
+    const int64_t slot = it / per;
+    const int rem = int(it % per);
+    I.cb = rem / a.nsplit;
+    I.sp = rem % a.nsplit;
+    const int4 sl = a.slots[slot];
+    I.e = sl.x;
+    I.p0 = sl.y;
+    I.rows = sl.z;
+    I.kt0 = I.sp * a.ktps;
+    I.kt1 = min(I.kt0 + a.ktps, a.in_f / 16);
+    I.group = int(slot * a.ncb + I.cb);
+    return I;
+}
+
+// is projection usable for this expert (pointer present, aligned, K valid)?
+__device__ __forceinline__ bool proj_ok(const ProjRef& p, int e, int kmax, int* status, bool report) {
+    const int K = proj_k(p, e);
+    const uint16_t* t = proj_trellis(p, e);
+    if (K < 2 || K > kmax) {
+        if (report) set_status(status, DEV_BAD_K);
+        return false;
+    }
+    if (t == nullptr) {
+        if (report) set_status(status, DEV_NULL_PTR);
+        return false;
+    }
+    if (reinterpret_cast<uintptr_t>(t) & 15) {
+        if (report) set_status(status, DEV_BAD_ALIGN);
+        return false;
+    }
+    return true;
+}
+
+__device__ __forceinline__ bool guarded_wait(uint64_t* bar, uint32_t parity, int* status,
+                                             volatile int* abort_flag) {
+    if (*abort_flag) return false;
+    if (mbar_wait(bar, parity, status)) return true;
+    *abort_flag = 1;
+    return false;
+}
+
+template <int K, int CB>
+__device__ __forceinline__ void stage_mma(const uint32_t* __restrict__ trow0, int row_stride_words,
+                                          int nt, uint32_t xs_addr, int lane, bool two,
+                                          float (&acc)[2][4]) {
+    const int brow = (lane & 7) + ((lane >> 4) << 3);
+    const int bhalf = (lane >> 3) & 1;
+    #pragma unroll 2
+    for (int kk = 0; kk < kKtPerStage; ++kk) {
+        uint32_t af[4];
+        decode_tile_afrag<K, CB>(trow0 + kk * row_stride_words + nt * (8 * K), lane, af);
+        uint32_t b[4];
+        const int ch = 2 * kk + bhalf;
+        ldmatrix_x4(b, xs_addr + brow * 256 + ((ch ^ (brow & 7)) << 4));
+        mma_16816(acc[0], af, b[0], b[1]);
+        if (two) mma_16816(acc[1], af, b[2], b[3]);
+    }
+}
+
+template <int CB>
+__device__ __forceinline__ void stage_mma_k(int K, const uint32_t* trow0, int row_stride_words, int nt,
+                                            uint32_t xs_addr, int lane, bool two, float (&acc)[2][4]) {
+    switch (K) {
+        case 2: stage_mma<2, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
+        case 3: stage_mma<3, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
+        case 4: stage_mma<4, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
+        case 5: stage_mma<5, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
+        case 6: stage_mma<6, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
+        case 7: stage_mma<7, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
+        case 8: stage_mma<8, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
+        default: break;
+    }
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+
+template <int NPROJ, int EPI, int CB>
+__global__ void __launch_bounds__(gemv_threads<NPROJ>(), (NPROJ == 1 ? 2 : 1))
+gemv_kernel(const __grid_constant__ GemvArgs a) {
+    constexpr int NCW = 8 * NPROJ;  // consumer warps
+    constexpr int NCT = NCW * 32;
+    extern __shared__ __align__(128) char smem_raw[];
+    const int S = a.stages;
+    GemvSmem sm = gemv_smem(smem_raw, NPROJ, S);
+    const size_t stage_bytes = gemv_stage_bytes(NPROJ, a.kmax);
+    const int row_words = 8 * 8 * a.kmax;  // uint32 capacity of one k-tile row (8 tiles)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    volatile int* abort_flag = sm.flags;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], NCW);
+        }
+        sm.flags[0] = 0;
+        sm.flags[1] = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    const int64_t n_items = int64_t(*a.nslots) * a.ncb * a.nsplit;
+    const int nkb = a.in_f / 128;
+    const int ntiles_out = a.out_f / 16;
+
+    if (warp == NCW) {
+        // ------------------------------ producer ------------------------------
+        if (lane != 0) return;
+        uint32_t q = 0;
+        for (int64_t it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
+            const ItemInfo I = gemv_item(a, it);
+            bool ok[NPROJ];
+            int Kp[NPROJ];
+            const uint16_t* tp[NPROJ];
+            #pragma unroll
+            for (int p = 0; p < NPROJ; ++p) {
+                ok[p] = proj_ok(a.proj[p], I.e, a.kmax, a.status, true);
+                Kp[p] = proj_k(a.proj[p], I.e);
+                tp[p] = proj_trellis(a.proj[p], I.e);
+            }
+            for (int kt = I.kt0; kt < I.kt1; kt += kKtPerStage, ++q) {
+                const int s = int(q % uint32_t(S));
+                const uint32_t ph = (q / uint32_t(S)) & 1u;
+                if (!guarded_wait(&sm.empty[s], ph ^ 1u, a.status, abort_flag)) break;
+                char* st = sm.stages + size_t(s) * stage_bytes;
+                uint32_t bytes = NPROJ * 16 * 256;
+                #pragma unroll
+                for (int p = 0; p < NPROJ; ++p)
+                    if (ok[p]) bytes += kKtPerStage * 256 * Kp[p];
+                mbar_arrive_expect_tx(&sm.full[s], bytes);
+                #pragma unroll
+                for (int p = 0; p < NPROJ; ++p) {
+                    if (!ok[p]) continue;
+                    const int tw = 16 * Kp[p];  // int16 per tile
+                    for (int kk = 0; kk < kKtPerStage; ++kk) {
+                        const uint16_t* src = tp[p] + (int64_t(kt + kk) * ntiles_out + int64_t(I.cb) * 8) * tw;
+                        char* dst = st + (size_t(p) * kKtPerStage + kk) * row_words * 4;
+                        bulk_g2s(dst, src, uint32_t(256 * Kp[p]), &sm.full[s]);
+                    }
+                }
+                const int kb = kt / kKtPerStage;
+                #pragma unroll
+                for (int p = 0; p < NPROJ; ++p) {
+                    const __half* src = a.xin + ((int64_t(p) * nkb + kb) * a.rpad + I.p0) * 128;
+                    char* dst = st + size_t(NPROJ) * kKtPerStage * row_words * 4 + size_t(p) * 4096;
+                    bulk_g2s(dst, src, 4096u, &sm.full[s]);
+                }
+            }
+        }
+        // drain: every issued stage must land before the CTA exits
+        const uint32_t first = q > uint32_t(S) ? q - uint32_t(S) : 0u;
+        for (uint32_t r = first; r < q; ++r) {
+            const int s = int(r % uint32_t(S));
+            mbar_wait(&sm.full[s], (r / uint32_t(S)) & 1u, a.status);
+        }
+        return;
+    }
+
+    // ------------------------------ consumers ------------------------------
+    const int cw = warp;
+    const int pj = cw / 8, nt = cw % 8;
+    uint32_t q = 0;
+    for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+        const ItemInfo I = gemv_item(a, it);
+        const bool ok = proj_ok(a.proj[pj], I.e, a.kmax, a.status, false);
+        const int K = proj_k(a.proj[pj], I.e);
+        const bool two = I.rows > 8;
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        for (int kt = I.kt0; kt < I.kt1; kt += kKtPerStage, ++q) {
+            const int s = int(q % uint32_t(S));
+            const uint32_t ph = (q / uint32_t(S)) & 1u;
+            const bool landed = guarded_wait(&sm.full[s], ph, a.status, abort_flag);
+            if (landed && ok) {
+                const char* st = sm.stages + size_t(s) * stage_bytes;
+                const uint32_t* trow0 = reinterpret_cast<const uint32_t*>(st + size_t(pj) * kKtPerStage * row_words * 4);
+                const uint32_t xs = smem_u32(st + size_t(NPROJ) * kKtPerStage * row_words * 4 + size_t(pj) * 4096);
+                stage_mma_k<CB>(K, trow0, row_words, nt, xs, lane, two, acc);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[s]);
+        }
+
+        // ---- split-K: last CTA of the group reduces partials in split order
+        if (a.nsplit > 1) {
+            float* pp = a.part + ((int64_t(I.group) * a.nsplit + I.sp) * NCW + cw) * 256;
+            #pragma unroll
+            for (int i = 0; i < 8; ++i) __stcg(pp + i * 32 + lane, acc[i >> 2][i & 3]);
+            __threadfence();
+            named_bar_sync(1, NCT);
+            if (threadIdx.x == 0) {
+                const int old = atomicAdd(&a.cnt[I.group], 1);
+                const int last = old == a.nsplit - 1;
+                if (last) a.cnt[I.group] = 0;
+                sm.flags[1] = last;
+            }
+            named_bar_sync(1, NCT);
+            if (!sm.flags[1]) continue;
+            __threadfence();
+            #pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i >> 2][i & 3] = 0.f;
+            for (int sp = 0; sp < a.nsplit; ++sp) {
+                const float* rp = a.part + ((int64_t(I.group) * a.nsplit + sp) * NCW + cw) * 256;
+                #pragma unroll
+                for (int i = 0; i < 8; ++i) acc[i >> 2][i & 3] += __ldcg(rp + i * 32 + lane);
+            }
+        }
+
+        // ---- fragments -> [proj][token row][column] tile
+        float* ys = sm.ys + pj * 16 * kYsPitch;
+        #pragma unroll
+        for (int nb = 0; nb < 2; ++nb)
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int m = nt * 16 + (lane >> 2) + 8 * (i >> 1);
+                const int n = nb * 8 + 2 * (lane & 3) + (i & 1);
+                ys[n * kYsPitch + m] = acc[nb][i];
+            }
+        named_bar_sync(1, NCT);
+
+        // ---- output rotation o svh
+        for (int v = cw; v < NPROJ * I.rows; v += NCW) {
+            const int p = v / I.rows, r = v % I.rows;
+            float* row = sm.ys + (p * 16 + r) * kYsPitch;
+            float x[4];
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) x[i] = row[lane + 32 * i];
+            fwht128_warp(x, lane);
+            const __half* svh = proj_svh(a.proj[p], I.e);
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float sv = svh ? __half2float(svh[I.cb * 128 + lane + 32 * i]) : 0.f;
+                row[lane + 32 * i] = x[i] * kHadNorm * sv;
+            }
+        }
+        named_bar_sync(1, NCT);
+
+        if constexpr (EPI == EPI_GATEUP) {
+            const __half* dsuh = proj_suh(a.down, I.e);
+            for (int r = cw; r < I.rows; r += NCW) {
+                const float* gr = sm.ys + r * kYsPitch;
+                const float* ur = sm.ys + (16 + r) * kYsPitch;
+                float x[4];
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int c = lane + 32 * i;
+                    float g = gr[c], u = ur[c];
+                    if (a.limit > 0.f) {
+                        g = fminf(g, a.limit);
+                        u = fminf(fmaxf(u, -a.limit), a.limit);
+                    }
+                    float act;
+                    if (a.act == ACT_SWIGLU_OAI) act = (u + 1.0f) * g / (1.0f + expf(-1.702f * g));
+                    else act = silu_f(g) * u;
+                    const float h = __half2float(__float2half_rn(act));  // the reference's act.half()
+                    x[i] = h * (dsuh ? __half2float(dsuh[I.cb * 128 + c]) : 0.f);
+                }
+                fwht128_warp(x, lane);
+                const int64_t p = I.p0 + r;
+                __half* dst = a.a2 + (int64_t(I.cb) * a.rpad + p) * 128;
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) dst[swz(lane + 32 * i, p)] = __float2half_rn(x[i] * kHadNorm);
+            }
+        } else if constexpr (EPI == EPI_DOWN) {
+            for (int r = cw; r < I.rows; r += NCW) {
+                const float* row = sm.ys + r * kYsPitch;
+                const int64_t p = I.p0 + r;
+                const float w = a.sorted_w[p];
+                float* dst = a.yd + p * a.out_f + I.cb * 128;
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = row[lane + 32 * i] * w;
+            }
+        } else {
+            for (int r = cw; r < I.rows; r += NCW) {
+                const float* row = sm.ys + r * kYsPitch;
+                const int tok = a.sorted_tok[I.p0 + r];
+                if (tok < 0) continue;
+                #pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    store_from_float(a.y, int64_t(tok) * a.out_f + I.cb * 128 + lane + 32 * i, a.y_dtype,
+                                     row[lane + 32 * i]);
+            }
+        }
+        named_bar_sync(1, NCT);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 5. deterministic combine
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+combine_kernel(const int* __restrict__ route_pos, const float* __restrict__ yd, int64_t t_max, int topk,
+               int hidden, const int32_t* n_valid, void* out, int out_dtype) {
+    int64_t T = t_max;
+    if (n_valid) T = min(T, int64_t(max(0, *n_valid)));
+    const int h4 = hidden / 4;
+    const int64_t total = t_max * h4;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t t = i / h4;
+        const int c = int(i % h4) * 4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < T) {
+            for (int k = 0; k < topk; ++k) {
+                const int p = route_pos[t * topk + k];
+                if (p < 0) continue;
+                const float4 v = *reinterpret_cast<const float4*>(yd + int64_t(p) * hidden + c);
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+        }
+        const int64_t o = t * hidden + c;
+        store_from_float(out, o + 0, out_dtype, acc.x);
+        store_from_float(out, o + 1, out_dtype, acc.y);
+        store_from_float(out, o + 2, out_dtype, acc.z);
+        store_from_float(out, o + 3, out_dtype, acc.w);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host: planning and launch
+// ---------------------------------------------------------------------------
+static constexpr size_t kSmemBudget = 227 * 1024;
+
+static void pick_stages(int nproj, int kmax, int ctas_per_sm, int& stages, size_t& smem) {
+    const size_t per_cta = kSmemBudget / ctas_per_sm - (ctas_per_sm > 1 ? 1024 : 0);
+    const size_t sb = gemv_stage_bytes(nproj, kmax);
+    int s = 8;
+    while (s > 2 && gemv_fixed_bytes(nproj, s) + size_t(s) * sb > per_cta) --s;
+    stages = s;
+    smem = gemv_fixed_bytes(nproj, s) + size_t(s) * sb;
+}
+
+static void pick_split(int64_t groups_est, int grid, int nkt, int& nsplit, int& ktps) {
+    const int64_t target = 2 * int64_t(grid);
+    int ns = 1;
+    if (groups_est < target) ns = int((target + groups_est - 1) / groups_est);
+    ns = std::max(1, std::min(ns, nkt / kKtPerStage));
+    ktps = ((nkt + ns - 1) / ns + kKtPerStage - 1) / kKtPerStage * kKtPerStage;
+    nsplit = (nkt + ktps - 1) / ktps;
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_local, int kmax,
+              bool linear, int num_sms) {
+    if (t_max < 1 || topk < 1 || hidden < 128 || hidden % 128 || n_local < 1 || n_local > kMaxLocal)
+        return false;
+    if (!linear && (inter < 128 || inter % 128)) return false;
+    if (kmax < 2 || kmax > 8) return false;
+    p = MoePlan();
+    p.t_max = t_max;
+    p.topk = topk;
+    p.hidden = hidden;  // linear: in_features
+    p.inter = inter;    // linear: out_features
+    p.n_local = n_local;
+    p.kmax = kmax;
+    p.linear = linear;
+    p.routes = t_max * topk;
+    const int64_t act_max = std::min<int64_t>(p.routes, n_local);
+    p.smax = p.routes / 16 + act_max + 1;
+    p.rpad = p.smax * 16;
+
+    if (linear) {
+        // one projection: in = hidden, out = inter
+        p.ncb1 = inter / 128;
+        pick_stages(1, kmax, 2, p.stages1, p.smem1);
+        p.grid1 = num_sms * 2;
+        pick_split((t_max + 15) / 16 * p.ncb1, p.grid1, hidden / 16, p.nsplit1, p.ktps1);
+    } else {
+        p.ncb1 = inter / 128;
+        pick_stages(2, kmax, 1, p.stages1, p.smem1);
+        p.grid1 = num_sms;
+        pick_split(act_max * p.ncb1, p.grid1, hidden / 16, p.nsplit1, p.ktps1);
+        p.ncb2 = hidden / 128;
+        pick_stages(1, kmax, 2, p.stages2, p.smem2);
+        p.grid2 = num_sms * 2;
+        pick_split(act_max * p.ncb2, p.grid2, inter / 16, p.nsplit2, p.ktps2);
+    }
+
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o = align256(o + bytes);
+        return at;
+    };
+    p.off_status = take(64);
+    p.off_nslots = take(64);
+    p.off_slots = take(size_t(p.smax) * 16);
+    p.off_route_pos = take(size_t(p.routes) * 4);
+    p.off_sorted_tok = take(size_t(p.rpad) * 4);
+    p.off_sorted_exp = take(size_t(p.rpad) * 4);
+    p.off_sorted_w = take(size_t(p.rpad) * 4);
+    const int nproj1 = linear ? 1 : 2;
+    p.off_xr = take(size_t(nproj1) * p.rpad * hidden * 2);
+    p.off_a2 = take(linear ? 0 : size_t(p.rpad) * inter * 2);
+    p.off_yd = take(linear ? 0 : size_t(p.rpad) * hidden * 4);
+    const int ncw1 = 8 * nproj1;
+    p.off_part1 = take(p.nsplit1 > 1 ? size_t(p.smax) * p.ncb1 * p.nsplit1 * ncw1 * 256 * 4 : 0);
+    p.off_part2 = take(!linear && p.nsplit2 > 1 ? size_t(p.smax) * p.ncb2 * p.nsplit2 * 8 * 256 * 4 : 0);
+    p.off_cnt1 = take(size_t(p.smax) * p.ncb1 * 4);
+    p.off_cnt2 = take(linear ? 0 : size_t(p.smax) * p.ncb2 * 4);
+    p.total = o;
+    return true;
+}
+
+template <int NPROJ, int EPI>
+static cudaError_t launch_gemv(int cb, const GemvArgs& g, int grid, size_t smem, cudaStream_t s) {
+    void (*kern)(GemvArgs);
+    if (cb == CB_MCG) kern = gemv_kernel<NPROJ, EPI, CB_MCG>;
+    else if (cb == CB_MUL1) kern = gemv_kernel<NPROJ, EPI, CB_MUL1>;
+    else kern = gemv_kernel<NPROJ, EPI, CB_3INST>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    kern<<<grid, gemv_threads<NPROJ>(), smem, s>>>(g);
+    return cudaGetLastError();
+}
+
+cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s) {
+    const WsPtrs w = ws_ptrs(p, ws);
+    const int nsm = std::max(1, p.grid1 / (p.linear ? 2 : 1));
+
+    PrepArgs pa;
+    pa.ids = c.ids;
+    pa.ids_dtype = c.ids_dtype;
+    pa.weights = c.weights;
+    pa.w_dtype = c.w_dtype;
+    pa.expert_map = c.expert_map;
+    pa.n_global = c.n_global;
+    pa.n_valid = c.n_valid;
+    pa.t_max = p.t_max;
+    pa.topk = p.topk;
+    pa.n_local = p.n_local;
+    pa.linear = p.linear ? 1 : 0;
+    pa.cnt1_n = int(p.smax * p.ncb1);
+    pa.cnt2_n = p.linear ? 0 : int(p.smax * p.ncb2);
+    pa.w = w;
+    prep_kernel<<<1, kPrepThreads, 0, s>>>(pa);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+
+    RotArgs ra;
+    ra.x = c.x;
+    ra.x_dtype = c.x_dtype;
+    ra.in_f = p.hidden;
+    ra.nproj = p.linear ? 1 : 2;
+    ra.proj[0] = p.linear ? c.up : c.gate;
+    ra.proj[1] = c.up;
+    ra.nslots = w.nslots;
+    ra.slots = w.slots;
+    ra.sorted_tok = w.sorted_tok;
+    ra.xr = w.xr;
+    ra.rpad = p.rpad;
+    ra.status = w.status;
+    rotate_kernel<<<nsm * 8, 256, 0, s>>>(ra);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+
+    GemvArgs g;
+    g.status = w.status;
+    g.nslots = w.nslots;
+    g.slots = w.slots;
+    g.rpad = p.rpad;
+    g.kmax = p.kmax;
+    g.sorted_tok = w.sorted_tok;
+    g.sorted_w = w.sorted_w;
+    if (p.linear) {
+        g.proj[0] = c.up;
+        g.in_f = p.hidden;
+        g.out_f = p.inter;
+        g.ncb = p.ncb1;
+        g.nsplit = p.nsplit1;
+        g.ktps = p.ktps1;
+        g.stages = p.stages1;
+        g.xin = w.xr;
+        g.y = c.out;
+        g.y_dtype = c.out_dtype;
+        g.part = w.part1;
+        g.cnt = w.cnt1;
+        return launch_gemv<1, EPI_LINEAR>(c.cb, g, p.grid1, p.smem1, s);
+    }
+
+    g.proj[0] = c.gate;
+    g.proj[1] = c.up;
+    g.in_f = p.hidden;
+    g.out_f = p.inter;
+    g.ncb = p.ncb1;
+    g.nsplit = p.nsplit1;
+    g.ktps = p.ktps1;
+    g.stages = p.stages1;
+    g.xin = w.xr;
+    g.down = c.down;
+    g.a2 = w.a2;
+    g.limit = c.limit;
+    g.act = c.act;
+    g.part = w.part1;
+    g.cnt = w.cnt1;
+    if ((e = launch_gemv<2, EPI_GATEUP>(c.cb, g, p.grid1, p.smem1, s)) != cudaSuccess) return e;
+
+    GemvArgs d = g;
+    d.proj[0] = c.down;
+    d.proj[1] = ProjRef();
+    d.in_f = p.inter;
+    d.out_f = p.hidden;
+    d.ncb = p.ncb2;
+    d.nsplit = p.nsplit2;
+    d.ktps = p.ktps2;
+    d.stages = p.stages2;
+    d.xin = w.a2;
+    d.yd = w.yd;
+    d.part = w.part2;
+    d.cnt = w.cnt2;
+    if ((e = launch_gemv<1, EPI_DOWN>(c.cb, d, p.grid2, p.smem2, s)) != cudaSuccess) return e;
+
+    const int64_t total = p.t_max * (p.hidden / 4);
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, int64_t(nsm) * 16);
+    combine_kernel<<<unsigned(std::max<int64_t>(blocks, 1)), 256, 0, s>>>(
+        w.route_pos, w.yd, p.t_max, p.topk, p.hidden, c.n_valid, c.out, c.out_dtype);
+    return cudaGetLastError();
+}
+
+int num_sms_current() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+    return n;
+}
+
+}  // namespace exl3

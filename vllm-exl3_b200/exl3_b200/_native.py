@@ -1,0 +1,128 @@
+"""ctypes binding of ``libexl3_b200.so`` (the C ABI in ``include/exl3_b200.h``).
+
+There is no CPU fallback: if the library is missing or cannot load, every
+entry raises.  Tensors are passed as raw device pointers; the stream is
+torch's current stream of the tensors' device.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+from . import build as _build
+
+_lock = threading.Lock()
+_lib = None
+
+EXL3_OK, EXL3_ERR_ARG, EXL3_ERR_CUDA, EXL3_ERR_WORKSPACE = 0, 1, 2, 3
+DT_F32, DT_F16, DT_BF16, DT_I32, DT_I64 = 0, 1, 2, 3, 4
+CB_3INST, CB_MCG, CB_MUL1 = 0, 1, 2
+ACT_SILU, ACT_SWIGLU_OAI = 0, 3
+
+_DTYPE_CODE = {
+    torch.float32: DT_F32,
+    torch.float16: DT_F16,
+    torch.bfloat16: DT_BF16,
+    torch.int32: DT_I32,
+    torch.int64: DT_I64,
+}
+
+P = ctypes.c_void_p
+I32 = ctypes.c_int
+I64 = ctypes.c_int64
+SZ = ctypes.c_size_t
+F32 = ctypes.c_float
+
+# name -> (restype, argtypes); must cover every function in include/exl3_b200.h
+SIGNATURES = {
+    "exl3_abi_version": (I32, []),
+    "exl3_last_error": (ctypes.c_char_p, []),
+    "exl3_device_status": (I32, [P, I32, P, ctypes.POINTER(I32)]),
+    "exl3_reconstruct": (I32, [P, P, P, I64, I64, I32, I32, P, P]),
+    "exl3_decode_raw": (I32, [P, I64, I64, I32, I32, P, P]),
+    "exl3_had128": (I32, [P, P, I64, I64, P, P, F32, P]),
+    "exl3_linear_workspace_size": (SZ, [I64, I64, I64, I32]),
+    "exl3_linear": (I32, [P, I32, I64, P, P, P, I64, I64, I32, I32, P, I32, P, SZ, P]),
+    "exl3_moe_workspace_size": (SZ, [I64, I32, I64, I64, I32, I32]),
+    "exl3_moe_forward": (
+        I32,
+        [P, I32, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, I32, P, I32, I32, P, I64,
+         P, P, P, I32, I32, I32, I32, I32, F32, P, P, I32, P, SZ, P],
+    ),
+}
+
+
+def lib_path() -> str:
+    return _build.LIB_PATH
+
+
+def load():
+    """Load (building first if the sources are newer) and bind the library."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = _build.LIB_PATH
+        if not _build.up_to_date():
+            try:
+                _build.build()
+            except Exception as exc:  # no nvcc on this machine: use the shipped binary
+                if not os.path.exists(path):
+                    raise RuntimeError(f"EXL3 CUDA library unavailable: {exc}") from exc
+        lib = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    return load().exl3_last_error().decode(errors="replace")
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != EXL3_OK:
+        raise RuntimeError(last_error() or f"{what} failed with status {rc}")
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPE_CODE[t.dtype]
+    except KeyError:
+        raise RuntimeError(f"unsupported dtype {t.dtype}") from None
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def require_cuda(*tensors: torch.Tensor | None, who: str) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(f"{who} requires CUDA tensors (the B200 path has no CPU fallback)")
+
+
+_ws_cache: dict[tuple, torch.Tensor] = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """A cached, 256-byte aligned uint8 workspace of at least ``nbytes``.
+
+    Grown (never shrunk) per device; callers on one stream reuse it.
+    """
+    key = (device.type, device.index)
+    buf = _ws_cache.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _ws_cache[key] = buf
+    return buf
