@@ -105,6 +105,18 @@ int exl3_moe_forward(const void* x, int x_dtype, int64_t tokens, int64_t hidden,
                      const int32_t* n_valid, void* out, int out_dtype, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* Phase timing for benchmarks (no reference counterpart; the reference times
+ * its kernels with CUDA events in tools/bench_moe_decode.py:24-55).  While
+ * enabled, exl3_moe_forward and exl3_linear first launch a spin of
+ * `delay_cycles` GPU clocks (capped at 4e9) so every launch is queued before
+ * the GPU reaches it, then record a CUDA event before and after each kernel
+ * phase on the call's stream: MoE = prep, rotate, gate/up, down, combine;
+ * linear = prep, rotate, gemv.  exl3_profile_read waits for the last call's
+ * final event and returns each phase's milliseconds.  Process-global, not
+ * thread-safe, not for use inside CUDA-graph capture. */
+int exl3_profile_enable(int on, long long delay_cycles);
+int exl3_profile_read(float* ms, int max_phases, int* n_phases);
+
 #ifdef __cplusplus
 }
 #endif

@@ -76,7 +76,7 @@ def test_decode_config_shape_matches_eager_loop(native, cuda, tokens):
 def test_mixed_k_mul1_with_limit(native, cuda):
     import torch
     pack, layer, x, ids, w = _setup(cuda, "cfg3", seed=5, tokens=24, n_experts=12, hidden=512,
-                                    inter=384, k_choices=(2, 3, 4, 5))
+                                    inter=384, k_choices=(2, 3, 4, 5), k_probs=None)
     dense = _dense(pack)
     for limit in (None, 0.75):
         want = oracle.moe_eager(x, ids, w, dense, limit=limit)

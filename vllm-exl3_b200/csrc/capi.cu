@@ -219,4 +219,17 @@ int exl3_moe_forward(const void* x, int x_dtype, int64_t tokens, int64_t hidden,
     return e == cudaSuccess ? EXL3_OK : cuda_fail(e, "fused MoE launch");
 }
 
+int exl3_profile_enable(int on, long long delay_cycles) {
+    exl3::profile_enable(on != 0, delay_cycles);
+    return EXL3_OK;
+}
+
+int exl3_profile_read(float* ms, int max_phases, int* n_phases) {
+    if (!ms || !n_phases || max_phases < 1) return fail(EXL3_ERR_ARG, "exl3_profile_read: bad arguments");
+    const int n = exl3::profile_read(ms, max_phases);
+    if (n < 0) return fail(EXL3_ERR_CUDA, "exl3_profile_read: event query failed");
+    *n_phases = n;
+    return EXL3_OK;
+}
+
 }  // extern "C"

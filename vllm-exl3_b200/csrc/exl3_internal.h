@@ -81,5 +81,7 @@ cudaError_t run_had128(const void* x, void* y, int64_t rows, int64_t n, const vo
                        const void* post, float scale, cudaStream_t s);
 
 int num_sms_current();
+void profile_enable(bool on, long long delay_cycles);
+int profile_read(float* ms, int max_phases);
 
 }  // namespace exl3

@@ -773,6 +773,59 @@ static cudaError_t launch_gemv(int cb, const GemvArgs& g, int grid, size_t smem,
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// phase timing for benchmarks (exl3_profile_*): events around each kernel
+// phase, preceded by a bounded spin so the host has queued every launch
+// before the GPU reaches the first event.  Not thread-safe; benchmark use only.
+// ---------------------------------------------------------------------------
+struct PhaseProfiler {
+    bool on = false;
+    long long delay_cycles = 0;
+    int dev = -1;
+    cudaEvent_t ev[8] = {};
+    int n = 0;  // events recorded by the last call
+};
+static PhaseProfiler g_prof;
+
+__global__ void spin_kernel(long long cycles) {
+    const long long t0 = clock64();
+    while (clock64() - t0 < cycles) {
+    }
+}
+
+static void prof_begin(cudaStream_t s) {
+    g_prof.n = 0;
+    if (!g_prof.on) return;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (g_prof.dev != dev) {
+        for (auto& e : g_prof.ev)
+            if (e) cudaEventDestroy(e);
+        for (auto& e : g_prof.ev) cudaEventCreate(&e);
+        g_prof.dev = dev;
+    }
+    if (g_prof.delay_cycles > 0) spin_kernel<<<1, 1, 0, s>>>(g_prof.delay_cycles);
+    cudaEventRecord(g_prof.ev[g_prof.n++], s);
+}
+
+static void prof_mark(cudaStream_t s) {
+    if (g_prof.on && g_prof.n < 8) cudaEventRecord(g_prof.ev[g_prof.n++], s);
+}
+
+void profile_enable(bool on, long long delay_cycles) {
+    g_prof.on = on;
+    g_prof.delay_cycles = delay_cycles < 0 ? 0 : (delay_cycles > 4000000000LL ? 4000000000LL : delay_cycles);
+}
+
+int profile_read(float* ms, int max_phases) {
+    const int n = g_prof.n - 1;
+    if (n <= 0) return 0;
+    if (cudaEventSynchronize(g_prof.ev[g_prof.n - 1]) != cudaSuccess) return -1;
+    for (int i = 0; i < n && i < max_phases; ++i)
+        if (cudaEventElapsedTime(&ms[i], g_prof.ev[i], g_prof.ev[i + 1]) != cudaSuccess) return -1;
+    return n;
+}
+
 cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s) {
     const WsPtrs w = ws_ptrs(p, ws);
     const int nsm = std::max(1, p.grid1 / (p.linear ? 2 : 1));
@@ -792,9 +845,11 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     pa.cnt1_n = int(p.smax * p.ncb1);
     pa.cnt2_n = p.linear ? 0 : int(p.smax * p.ncb2);
     pa.w = w;
+    prof_begin(s);
     prep_kernel<<<1, kPrepThreads, 0, s>>>(pa);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    prof_mark(s);
 
     RotArgs ra;
     ra.x = c.x;
@@ -811,6 +866,7 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     ra.status = w.status;
     rotate_kernel<<<nsm * 8, 256, 0, s>>>(ra);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    prof_mark(s);
 
     GemvArgs g;
     g.status = w.status;
@@ -833,7 +889,9 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
         g.y_dtype = c.out_dtype;
         g.part = w.part1;
         g.cnt = w.cnt1;
-        return launch_gemv<1, EPI_LINEAR>(c.cb, g, p.grid1, p.smem1, s);
+        e = launch_gemv<1, EPI_LINEAR>(c.cb, g, p.grid1, p.smem1, s);
+        prof_mark(s);
+        return e;
     }
 
     g.proj[0] = c.gate;
@@ -852,6 +910,7 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     g.part = w.part1;
     g.cnt = w.cnt1;
     if ((e = launch_gemv<2, EPI_GATEUP>(c.cb, g, p.grid1, p.smem1, s)) != cudaSuccess) return e;
+    prof_mark(s);
 
     GemvArgs d = g;
     d.proj[0] = c.down;
@@ -867,12 +926,15 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     d.part = w.part2;
     d.cnt = w.cnt2;
     if ((e = launch_gemv<1, EPI_DOWN>(c.cb, d, p.grid2, p.smem2, s)) != cudaSuccess) return e;
+    prof_mark(s);
 
     const int64_t total = p.t_max * (p.hidden / 4);
     const int64_t blocks = std::min<int64_t>((total + 255) / 256, int64_t(nsm) * 16);
     combine_kernel<<<unsigned(std::max<int64_t>(blocks, 1)), 256, 0, s>>>(
         w.route_pos, w.yd, p.t_max, p.topk, p.hidden, c.n_valid, c.out, c.out_dtype);
-    return cudaGetLastError();
+    e = cudaGetLastError();
+    prof_mark(s);
+    return e;
 }
 
 int num_sms_current() {

@@ -53,6 +53,8 @@ SIGNATURES = {
         [P, I32, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, I32, P, I32, I32, P, I64,
          P, P, P, I32, I32, I32, I32, I32, F32, P, P, I32, P, SZ, P],
     ),
+    "exl3_profile_enable": (I32, [I32, ctypes.c_longlong]),
+    "exl3_profile_read": (I32, [ctypes.POINTER(F32), I32, ctypes.POINTER(I32)]),
 }
 
 
@@ -110,6 +112,18 @@ def require_cuda(*tensors: torch.Tensor | None, who: str) -> None:
     for t in tensors:
         if t is not None and not t.is_cuda:
             raise RuntimeError(f"{who} requires CUDA tensors (the B200 path has no CPU fallback)")
+
+
+def profile_enable(on: bool, delay_cycles: int = 0) -> None:
+    check(load().exl3_profile_enable(int(bool(on)), int(delay_cycles)))
+
+
+def profile_read(max_phases: int = 8) -> list[float]:
+    """Milliseconds of each kernel phase of the last profiled call."""
+    buf = (F32 * max_phases)()
+    n = I32(0)
+    check(load().exl3_profile_read(buf, max_phases, ctypes.byref(n)))
+    return [float(buf[i]) for i in range(n.value)]
 
 
 _ws_cache: dict[tuple, torch.Tensor] = {}
