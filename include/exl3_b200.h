@@ -105,6 +105,32 @@ int exl3_moe_forward(const void* x, int x_dtype, int64_t tokens, int64_t hidden,
                      const int32_t* n_valid, void* out, int out_dtype, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* Replaces p2b_gemv_batched (csrc/bindings.cpp:149-156, csrc/p2b_batched.cu:341-368):
+ * one shared input x [m][in] against the experts listed in expert_indices
+ * (int32 device [n_active], entries indexing the tables [n_table]);
+ * y [n_active][m][out] with y[j] = x W_{expert_indices[j]}.  Entries outside
+ * [0, n_table) leave their rows untouched.  The reference fixes out = 2048
+ * and K in 2..4; here out is any multiple of 128 and K is 2..8. */
+size_t exl3_batched_linear_workspace_size(int64_t m, int n_active, int64_t in_features,
+                                          int64_t out_features, int n_table, int K);
+int exl3_batched_linear(const void* x, int x_dtype, int64_t m, const int64_t* trellis_ptrs,
+                        const int64_t* suh_ptrs, const int64_t* svh_ptrs, int n_table,
+                        const int32_t* expert_indices, int n_active, int64_t in_features,
+                        int64_t out_features, int K, int codebook, void* y, int y_dtype,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Replaces exl3_fat_gemm / exl3_fat_gemm_scatter (csrc/exl3_fat_gemm.cu:266-305):
+ * `a` fp16 [m][in] is already input-rotated (had_r_128 of the activations
+ * with suh); out fp32 = (a W~) H / sqrt(128) o svh.  Without token_idx it
+ * writes out [m][out]; with token_idx (int64 [m]) and route_weight (fp16 [m])
+ * it adds route_weight[r] * row r into out[token_idx[r]] -- a plain
+ * read-modify-write, race-free only when no two rows of one call share a
+ * token, the reference's contract (exl3_fat_gemm.cu:182-189).  Any K 2..8
+ * and codebook (the reference: K4 MCG only).  Workspace: exl3_linear_workspace_size. */
+int exl3_fat_gemm(const void* a, int64_t m, const void* packed, const void* svh, int64_t in_features,
+                  int64_t out_features, int K, int codebook, float* out, const int64_t* token_idx,
+                  const void* route_weight, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Phase timing for benchmarks (no reference counterpart; the reference times
  * its kernels with CUDA events in tools/bench_moe_decode.py:24-55).  While
  * enabled, exl3_moe_forward and exl3_linear first launch a spin of

@@ -49,7 +49,8 @@ def test_arg_validation_happens_on_host():
 def test_dropin_module_surface():
     import vllm_exl3_c as m
     for name in ("dequant_trellis", "exl3_gemv", "exl3_gemm", "p2b_fused_moe", "p2b_fused_moe_mk",
-                 "p2b_fused_moe_padded", "had_r_128", "exl3_reconstruct", "exl3_linear", "exl3_moe"):
+                 "p2b_fused_moe_padded", "had_r_128", "exl3_reconstruct", "exl3_linear", "exl3_moe",
+                 "p2b_gemv_batched", "exl3_fat_gemm", "exl3_fat_gemm_scatter"):
         assert callable(getattr(m, name)), name
     assert m.P2B_MOE_ABI_VERSION >= 4 and m.P2B_MOE_MIXED_K and m.P2B_MOE_PADDED
 

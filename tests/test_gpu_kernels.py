@@ -133,3 +133,46 @@ def test_gemv_and_gemm_entries(native, cuda):
     x2 = rng.normal(0, 1, (2, 33, 256)).astype(np.float16)
     y2 = native.exl3_gemm(dev(x2), dev(t), dev(u), dev(v), 4, True)
     _close(y2.float().cpu().numpy().reshape(-1, 256), x2.reshape(-1, 256).astype(np.float32) @ w)
+
+
+def test_p2b_gemv_batched(native, cuda):
+    import torch
+    rng = np.random.default_rng(21)
+    E_tab, in_f, out_f, K = 5, 256, 2048, 3
+    packs = [_rand_packed(rng, in_f, out_f, K) for _ in range(E_tab)]
+    dev = [tuple(torch.from_numpy(a).to(cuda) for a in p) for p in packs]
+    tabs = [torch.tensor([d[i].data_ptr() for d in dev], dtype=torch.int64, device=cuda) for i in range(3)]
+    idx = torch.tensor([3, 0, 3, 4], dtype=torch.int32, device=cuda)
+    x = rng.normal(0, 1, (3, in_f)).astype(np.float16)
+    y = native.p2b_gemv_batched(torch.from_numpy(x).to(cuda), *tabs, idx, K, True)
+    assert y.shape == (4, 3, out_f) and y.dtype == torch.float16
+    for j, e in enumerate([3, 0, 3, 4]):
+        w = oracle.dequant(*packs[e], K, True).astype(np.float32)
+        _close(y[j].float().cpu().numpy(), x.astype(np.float32) @ w)
+
+
+@pytest.mark.parametrize("K,mcg,mul1", [(4, True, False), (2, False, True), (3, True, False)])
+def test_fat_gemm_and_scatter(native, cuda, K, mcg, mul1):
+    import torch
+    rng = np.random.default_rng(31 + K)
+    in_f, out_f, M, T = 384, 256, 70, 90
+    t, u, v = _rand_packed(rng, in_f, out_f, K)
+    cb = 1 if mcg else 2
+    h = rng.normal(0, 1, (M, in_f)).astype(np.float16)
+    ht = torch.from_numpy(h).to(cuda)
+    a = torch.empty_like(ht)
+    native.had_r_128(ht, a, torch.from_numpy(u).to(cuda), None, 1.0)  # the reference's input rotation
+    w = oracle.dequant(t, u, v, K, cb=cb).astype(np.float32)
+    want = h.astype(np.float32) @ w
+    out = torch.empty((M, out_f), dtype=torch.float32, device=cuda)
+    native.exl3_fat_gemm(a, torch.from_numpy(t).to(cuda), out, torch.from_numpy(v).to(cuda), K, mcg, mul1)
+    _close(out.cpu().numpy(), want)
+    tok = torch.from_numpy(rng.permutation(T)[:M].astype(np.int64)).to(cuda)
+    rw = torch.from_numpy(rng.uniform(0.1, 1, M).astype(np.float16)).to(cuda)
+    acc0 = rng.normal(0, 1, (T, out_f)).astype(np.float32)
+    acc = torch.from_numpy(acc0).to(cuda)
+    native.exl3_fat_gemm_scatter(a, torch.from_numpy(t).to(cuda), acc, torch.from_numpy(v).to(cuda),
+                                 tok, rw, K, mcg, mul1)
+    exp = acc0.copy()
+    exp[tok.cpu().numpy()] += want * rw.float().cpu().numpy()[:, None]
+    _close(acc.cpu().numpy(), exp)

@@ -219,6 +219,85 @@ int exl3_moe_forward(const void* x, int x_dtype, int64_t tokens, int64_t hidden,
     return e == cudaSuccess ? EXL3_OK : cuda_fail(e, "fused MoE launch");
 }
 
+size_t exl3_batched_linear_workspace_size(int64_t m, int n_active, int64_t in_f, int64_t out_f,
+                                          int n_table, int K) {
+    exl3::MoePlan p;
+    if (m < 1 || n_active < 1 || in_f > INT32_MAX || out_f > INT32_MAX) return 0;
+    if (!exl3::plan_moe(p, m, n_active, int(in_f), int(out_f), n_table, K < 2 ? 8 : K, true,
+                        exl3::num_sms_current()))
+        return 0;
+    return p.total;
+}
+
+int exl3_batched_linear(const void* x, int x_dtype, int64_t m, const int64_t* trellis_ptrs,
+                        const int64_t* suh_ptrs, const int64_t* svh_ptrs, int n_table,
+                        const int32_t* expert_indices, int n_active, int64_t in_f, int64_t out_f, int K,
+                        int cb, void* y, int y_dtype, void* ws, size_t ws_bytes, void* stream) {
+    const char* who = "batched GEMV";
+    if (!x || !y || !trellis_ptrs || !suh_ptrs || !svh_ptrs || !expert_indices)
+        return fail(EXL3_ERR_ARG, "%s: null argument", who);
+    if (!float_dtype(x_dtype) || !float_dtype(y_dtype))
+        return fail(EXL3_ERR_ARG, "%s: x/y dtype must be fp32, fp16 or bf16", who);
+    if (K < 2 || K > 8) return fail(EXL3_ERR_ARG, "%s supports K in 2..8", who);
+    if (cb < 0 || cb > 2) return fail(EXL3_ERR_ARG, "%s: codebook must be 0, 1 or 2", who);
+    if (in_f <= 0 || out_f <= 0 || in_f % 128 || out_f % 128 || in_f > INT32_MAX || out_f > INT32_MAX)
+        return fail(EXL3_ERR_ARG, "%s: in/out features must be positive multiples of 128", who);
+    if (n_table < 1 || n_table > 2048) return fail(EXL3_ERR_ARG, "%s: table length must be in 1..2048", who);
+    if (n_active < 1 || m < 1) return fail(EXL3_ERR_ARG, "%s: need m >= 1 and at least one expert", who);
+    exl3::MoePlan p;
+    if (!exl3::plan_moe(p, m, n_active, int(in_f), int(out_f), n_table, K, true, exl3::num_sms_current()))
+        return fail(EXL3_ERR_ARG, "%s: unsupported geometry", who);
+    if (!ws || ws_bytes < p.total)
+        return fail(EXL3_ERR_WORKSPACE, "%s: workspace of %zu bytes required (got %zu)", who, p.total, ws_bytes);
+    if (!aligned(ws, 256)) return fail(EXL3_ERR_WORKSPACE, "%s: workspace must be 256-byte aligned", who);
+    exl3::MoeCall c;
+    c.x = x;
+    c.x_dtype = x_dtype;
+    c.ids = expert_indices;
+    c.ids_dtype = EXL3_DT_I32;
+    c.up = {trellis_ptrs, suh_ptrs, svh_ptrs, nullptr, nullptr, nullptr, nullptr, K};
+    c.cb = cb;
+    c.out = y;
+    c.out_dtype = y_dtype;
+    c.batched = true;
+    cudaError_t e = exl3::run_moe(p, c, ws, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, who);
+}
+
+int exl3_fat_gemm(const void* a, int64_t m, const void* packed, const void* svh, int64_t in_f,
+                  int64_t out_f, int K, int cb, float* out, const int64_t* token_idx,
+                  const void* route_weight, void* ws, size_t ws_bytes, void* stream) {
+    static const uint16_t one = 0x3c00;  // the input is pre-rotated: no suh is read
+    if (int rc = check_packed("exl3_fat_gemm", packed, &one, svh, in_f, out_f, K, cb)) return rc;
+    if (!a || !out) return fail(EXL3_ERR_ARG, "exl3_fat_gemm: null a/out");
+    if ((token_idx == nullptr) != (route_weight == nullptr))
+        return fail(EXL3_ERR_ARG, "exl3_fat_gemm: token_idx and route_weight go together");
+    if (m < 0) return fail(EXL3_ERR_ARG, "exl3_fat_gemm: m must be >= 0");
+    if (m == 0) return EXL3_OK;
+    exl3::MoePlan p;
+    if (in_f > INT32_MAX || out_f > INT32_MAX ||
+        !exl3::plan_moe(p, m, 1, int(in_f), int(out_f), 1, K, true, exl3::num_sms_current()))
+        return fail(EXL3_ERR_ARG, "exl3_fat_gemm: unsupported geometry");
+    if (!ws || ws_bytes < p.total)
+        return fail(EXL3_ERR_WORKSPACE, "exl3_fat_gemm: workspace of %zu bytes required (got %zu)", p.total,
+                    ws_bytes);
+    if (!aligned(ws, 256)) return fail(EXL3_ERR_WORKSPACE, "exl3_fat_gemm: workspace must be 256-byte aligned");
+    exl3::MoeCall c;
+    c.x = a;
+    c.x_dtype = EXL3_DT_F16;
+    c.up.trellis = packed;
+    c.up.svh = svh;
+    c.up.k_uniform = K;
+    c.cb = cb;
+    c.out = out;
+    c.out_dtype = EXL3_DT_F32;
+    c.prerotated = true;
+    c.scatter_idx = token_idx;
+    c.scatter_w = route_weight;
+    cudaError_t e = exl3::run_moe(p, c, ws, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, "exl3_fat_gemm");
+}
+
 int exl3_profile_enable(int on, long long delay_cycles) {
     exl3::profile_enable(on != 0, delay_cycles);
     return EXL3_OK;

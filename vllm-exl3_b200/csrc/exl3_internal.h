@@ -35,7 +35,7 @@ struct MoePlan {
     int inter = 0;
     int n_local = 0;
     int kmax = 8;
-    bool linear = false;  // dense linear: one expert, topk 1, no activation
+    bool linear = false;  // one projection (dense linear, batched expert linear): no activation
     int64_t routes = 0;   // t_max * topk
     int64_t rpad = 0;     // sorted rows incl. per-expert padding to 16
     int64_t smax = 0;     // max work slots
@@ -45,6 +45,7 @@ struct MoePlan {
     size_t smem1 = 0, smem2 = 0;
     // offsets
     size_t off_status = 0, off_nslots = 0, off_slots = 0, off_route_pos = 0, off_sorted_tok = 0,
+           off_sorted_route = 0,
            off_sorted_exp = 0, off_sorted_w = 0, off_xr = 0, off_a2 = 0, off_yd = 0,
            off_part1 = 0, off_part2 = 0, off_cnt1 = 0, off_cnt2 = 0;
     size_t total = 0;
@@ -71,6 +72,11 @@ struct MoeCall {
     void* out = nullptr;
     int out_dtype = 0;
     bool gateless = false;
+    // single-projection variants (plan.linear)
+    bool batched = false;              // ids = expert list shared by all rows; out [n_active][m][out]
+    bool prerotated = false;           // x already carries H(x o suh)/sqrt128 (fat GEMM input)
+    const int64_t* scatter_idx = nullptr;  // out[scatter_idx[row]] += scatter_w[row] * y[row]
+    const void* scatter_w = nullptr;       // fp16
 };
 
 cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s);

@@ -37,7 +37,7 @@
 
 namespace exl3 {
 
-enum Epi : int { EPI_GATEUP = 0, EPI_DOWN = 1, EPI_LINEAR = 2 };
+enum Epi : int { EPI_GATEUP = 0, EPI_DOWN = 1, EPI_LINEAR = 2, EPI_ROUTE = 3 };
 enum Act : int { ACT_SILU = 0, ACT_SWIGLU_OAI = 3 };
 
 constexpr int kPrepThreads = 1024;
@@ -50,6 +50,7 @@ struct WsPtrs {
     int4* slots;  // {expert, first sorted row, rows, 0}
     int* route_pos;
     int* sorted_tok;
+    int* sorted_route;
     int* sorted_exp;
     float* sorted_w;
     __half* xr;
@@ -69,6 +70,7 @@ static WsPtrs ws_ptrs(const MoePlan& p, void* ws) {
     w.slots = reinterpret_cast<int4*>(b + p.off_slots);
     w.route_pos = reinterpret_cast<int*>(b + p.off_route_pos);
     w.sorted_tok = reinterpret_cast<int*>(b + p.off_sorted_tok);
+    w.sorted_route = reinterpret_cast<int*>(b + p.off_sorted_route);
     w.sorted_exp = reinterpret_cast<int*>(b + p.off_sorted_exp);
     w.sorted_w = reinterpret_cast<float*>(b + p.off_sorted_w);
     w.xr = reinterpret_cast<__half*>(b + p.off_xr);
@@ -95,7 +97,8 @@ struct PrepArgs {
     int64_t t_max;
     int topk;
     int n_local;
-    int linear;
+    int linear;   // one expert, every row routed to it with weight 1
+    int batched;  // ids is one expert list shared by every row: route r -> ids[r % topk]
     int cnt1_n;
     int cnt2_n;
     WsPtrs w;
@@ -103,7 +106,7 @@ struct PrepArgs {
 
 __device__ __forceinline__ int local_expert(const PrepArgs& a, int64_t r) {
     if (a.linear) return 0;
-    const int64_t g = load_id(a.ids, r, a.ids_dtype);
+    const int64_t g = load_id(a.ids, a.batched ? r % a.topk : r, a.ids_dtype);
     int64_t e = g;
     if (a.expert_map) e = (g >= 0 && g < a.n_global) ? int64_t(a.expert_map[g]) : -1;
     return (e >= 0 && e < a.n_local) ? int(e) : -1;
@@ -174,6 +177,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
             a.w.slots[xs + j] = make_int4(e, xp + 16 * j, min(16, n - 16 * j), 0);
         for (int q = xp + n; q < xp + ((n + 15) & ~15); ++q) {
             a.w.sorted_tok[q] = -1;
+            a.w.sorted_route[q] = -1;
             a.w.sorted_exp[q] = e;
             a.w.sorted_w[q] = 0.f;
         }
@@ -205,8 +209,9 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
             const int p = my_base + rank;
             a.w.route_pos[r] = p;
             a.w.sorted_tok[p] = int(r / a.topk);
+            a.w.sorted_route[p] = int(r);
             a.w.sorted_exp[p] = e;
-            a.w.sorted_w[p] = a.linear ? 1.f : load_as_float(a.weights, r, a.w_dtype);
+            a.w.sorted_w[p] = (a.linear || a.batched) ? 1.f : load_as_float(a.weights, r, a.w_dtype);
         } else if (r < Rmax) {
             a.w.route_pos[r] = -1;
         }
@@ -229,6 +234,7 @@ struct RotArgs {
     __half* xr;
     int64_t rpad;
     int* status;
+    int prerotated;  // x already rotated (fp16): copy into the swizzled layout only
 };
 
 __device__ __forceinline__ const __half* proj_suh(const ProjRef& p, int e) {
@@ -266,8 +272,8 @@ __global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a) {
         if (row >= sl.z) continue;
         const int64_t p = sl.y + row;
         const int tok = a.sorted_tok[p];
-        const __half* suh = proj_suh(a.proj[pj], sl.x);
-        if (suh == nullptr || tok < 0) {
+        const __half* suh = a.prerotated ? nullptr : proj_suh(a.proj[pj], sl.x);
+        if ((suh == nullptr && !a.prerotated) || tok < 0) {
             if (lane == 0) set_status(a.status, suh == nullptr ? DEV_NULL_PTR : DEV_BAD_ROUTE);
             continue;
         }
@@ -277,10 +283,15 @@ __global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a) {
             const int c = kb * 128 + lane + 32 * i;
             // the reference casts activations to fp16 first (exl3.py:2384, 2856)
             const float xv = __half2float(__float2half_rn(load_as_float(a.x, int64_t(tok) * a.in_f + c, a.x_dtype)));
-            v[i] = xv * __half2float(suh[c]);
+            v[i] = a.prerotated ? xv : xv * __half2float(suh[c]);
+        }
+        __half* dst = a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * 128;
+        if (a.prerotated) {
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) dst[swz(lane + 32 * i, p)] = __float2half_rn(v[i]);
+            continue;
         }
         fwht128_warp(v, lane);
-        __half* dst = a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * 128;
         #pragma unroll
         for (int i = 0; i < 4; ++i) dst[swz(lane + 32 * i, p)] = __float2half_rn(v[i] * kHadNorm);
     }
@@ -305,10 +316,15 @@ struct GemvArgs {
     // EPI_DOWN
     const float* sorted_w;
     float* yd;
-    // EPI_LINEAR
+    // EPI_LINEAR / EPI_ROUTE
     void* y;
     int y_dtype;
     const int* sorted_tok;
+    const int* sorted_route;
+    const int64_t* scatter_idx;  // EPI_LINEAR: y[scatter_idx[row]] += scatter_w[row] * v
+    const __half* scatter_w;
+    int64_t t_max;
+    int topk;
     // split-K
     float* part;
     int* cnt;
@@ -625,14 +641,34 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 #pragma unroll
                 for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = row[lane + 32 * i] * w;
             }
-        } else {
+        } else if constexpr (EPI == EPI_LINEAR) {
             for (int r = cw; r < I.rows; r += NCW) {
                 const float* row = sm.ys + r * kYsPitch;
                 const int tok = a.sorted_tok[I.p0 + r];
                 if (tok < 0) continue;
+                if (a.scatter_idx) {
+                    // one route per destination row per call: plain read-modify-write
+                    float* dst = static_cast<float*>(a.y) + a.scatter_idx[tok] * a.out_f + I.cb * 128;
+                    const float w = __half2float(a.scatter_w[tok]);
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] += w * row[lane + 32 * i];
+                    continue;
+                }
                 #pragma unroll
                 for (int i = 0; i < 4; ++i)
                     store_from_float(a.y, int64_t(tok) * a.out_f + I.cb * 128 + lane + 32 * i, a.y_dtype,
+                                     row[lane + 32 * i]);
+            }
+        } else {
+            // EPI_ROUTE: route r = t * topk + j -> output row j * t_max + t
+            for (int r = cw; r < I.rows; r += NCW) {
+                const float* row = sm.ys + r * kYsPitch;
+                const int rt = a.sorted_route[I.p0 + r];
+                if (rt < 0) continue;
+                const int64_t orow = int64_t(rt % a.topk) * a.t_max + rt / a.topk;
+                #pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    store_from_float(a.y, orow * a.out_f + I.cb * 128 + lane + 32 * i, a.y_dtype,
                                      row[lane + 32 * i]);
             }
         }
@@ -723,7 +759,7 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
         p.ncb1 = inter / 128;
         pick_stages(1, kmax, 2, p.stages1, p.smem1);
         p.grid1 = num_sms * 2;
-        pick_split((t_max + 15) / 16 * p.ncb1, p.grid1, hidden / 16, p.nsplit1, p.ktps1);
+        pick_split(p.smax * p.ncb1, p.grid1, hidden / 16, p.nsplit1, p.ktps1);
     } else {
         p.ncb1 = inter / 128;
         pick_stages(2, kmax, 1, p.stages1, p.smem1);
@@ -746,6 +782,7 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     p.off_slots = take(size_t(p.smax) * 16);
     p.off_route_pos = take(size_t(p.routes) * 4);
     p.off_sorted_tok = take(size_t(p.rpad) * 4);
+    p.off_sorted_route = take(size_t(p.rpad) * 4);
     p.off_sorted_exp = take(size_t(p.rpad) * 4);
     p.off_sorted_w = take(size_t(p.rpad) * 4);
     const int nproj1 = linear ? 1 : 2;
@@ -841,7 +878,8 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     pa.t_max = p.t_max;
     pa.topk = p.topk;
     pa.n_local = p.n_local;
-    pa.linear = p.linear ? 1 : 0;
+    pa.linear = (p.linear && !c.batched) ? 1 : 0;
+    pa.batched = c.batched ? 1 : 0;
     pa.cnt1_n = int(p.smax * p.ncb1);
     pa.cnt2_n = p.linear ? 0 : int(p.smax * p.ncb2);
     pa.w = w;
@@ -864,6 +902,7 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     ra.xr = w.xr;
     ra.rpad = p.rpad;
     ra.status = w.status;
+    ra.prerotated = c.prerotated ? 1 : 0;
     rotate_kernel<<<nsm * 8, 256, 0, s>>>(ra);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     prof_mark(s);
@@ -875,7 +914,12 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     g.rpad = p.rpad;
     g.kmax = p.kmax;
     g.sorted_tok = w.sorted_tok;
+    g.sorted_route = w.sorted_route;
     g.sorted_w = w.sorted_w;
+    g.scatter_idx = c.scatter_idx;
+    g.scatter_w = static_cast<const __half*>(c.scatter_w);
+    g.t_max = p.t_max;
+    g.topk = p.topk;
     if (p.linear) {
         g.proj[0] = c.up;
         g.in_f = p.hidden;
@@ -889,7 +933,8 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
         g.y_dtype = c.out_dtype;
         g.part = w.part1;
         g.cnt = w.cnt1;
-        e = launch_gemv<1, EPI_LINEAR>(c.cb, g, p.grid1, p.smem1, s);
+        e = c.batched ? launch_gemv<1, EPI_ROUTE>(c.cb, g, p.grid1, p.smem1, s)
+                      : launch_gemv<1, EPI_LINEAR>(c.cb, g, p.grid1, p.smem1, s);
         prof_mark(s);
         return e;
     }

@@ -151,6 +151,113 @@ def exl3_gemm(x, trellis, suh, svh, K, mcg):
     return exl3_linear(x2, trellis, suh, svh, K, _cb(mcg))
 
 
+def p2b_gemv_batched(x, trellis_ptrs, suh_ptrs, svh_ptrs, expert_indices, K, mcg, mmode=1,
+                     out_features=2048):
+    """Batched MoE EXL3 GEMV (csrc/bindings.cpp:149-156): one shared input
+    x [m, in] against each listed expert; returns [n_active, m, out_features]
+    (the reference fixes out_features = 2048)."""
+    if not x.is_cuda or x.dtype != torch.float16:
+        raise RuntimeError("batched GEMV requires CUDA fp16")
+    for t in (trellis_ptrs, suh_ptrs, svh_ptrs, expert_indices):
+        if not t.is_cuda:
+            raise RuntimeError("batched GEMV requires CUDA tensors")
+    if int(K) not in range(2, 9):
+        raise RuntimeError("batched GEMV supports K in 2..8")
+    if int(mmode) not in (0, 1):
+        raise RuntimeError("mmode must be 0 or 1")
+    x2 = x.contiguous().view(-1, x.size(-1))
+    m, in_f = int(x2.size(0)), int(x2.size(1))
+    idx = expert_indices.to(torch.int32).contiguous().view(-1)
+    n_active = int(idx.numel())
+    tabs = [t.contiguous() for t in (trellis_ptrs, suh_ptrs, svh_ptrs)]
+    y = torch.zeros((n_active, m, int(out_features)), dtype=torch.float16, device=x.device)
+    if n_active == 0:
+        return y
+    lib = _n.load()
+    with torch.cuda.device(x.device):
+        need = lib.exl3_batched_linear_workspace_size(m, n_active, in_f, int(out_features),
+                                                      int(tabs[0].numel()), int(K))
+        if need == 0:
+            raise RuntimeError("batched GEMV: unsupported geometry")
+        ws = _n.workspace(x.device, need)
+        _n.check(lib.exl3_batched_linear(
+            x2.data_ptr(), _n.DT_F16, m, tabs[0].data_ptr(), tabs[1].data_ptr(), tabs[2].data_ptr(),
+            int(tabs[0].numel()), idx.data_ptr(), n_active, in_f, int(out_features), int(K), _cb(mcg),
+            y.data_ptr(), _n.DT_F16, ws.data_ptr(), ws.numel(), _n.stream_of(x)), "batched GEMV")
+    return y
+
+
+def _fat_checks(a, packed, out, svh, K, mcg, mul1):
+    if not (a.is_cuda and packed.is_cuda and out.is_cuda and svh.is_cuda):
+        raise RuntimeError("exl3_fat_gemm tensors must be CUDA tensors")
+    if not (a.is_contiguous() and packed.is_contiguous() and out.is_contiguous() and svh.is_contiguous()):
+        raise RuntimeError("exl3_fat_gemm tensors must be contiguous")
+    if a.dtype != torch.float16:
+        raise RuntimeError("a must be float16")
+    if packed.dtype != torch.int16:
+        raise RuntimeError("packed must be int16")
+    if out.dtype != torch.float32:
+        raise RuntimeError("out must be float32")
+    if svh.dtype != torch.float16:
+        raise RuntimeError("svh must be float16")
+    if a.dim() != 2 or packed.dim() != 3 or out.dim() != 2 or svh.dim() != 1:
+        raise RuntimeError("exl3_fat_gemm expects rank-2/rank-3 tensors")
+    if bool(mcg) and bool(mul1):
+        raise RuntimeError("exl3_fat_gemm: mcg and mul1 are exclusive")
+    if a.size(1) != packed.size(0) * 16:
+        raise RuntimeError("a K dimension does not match packed tensor")
+    if svh.numel() != packed.size(1) * 16:
+        raise RuntimeError("svh N dimension does not match packed tensor")
+    if svh.numel() % 128:
+        raise RuntimeError("output dimension must be divisible by 128")
+    if packed.size(2) != 16 * int(K):
+        raise RuntimeError("packed block width must be 16*K int16 words")
+    if len({a.device, packed.device, out.device, svh.device}) != 1:
+        raise RuntimeError("exl3_fat_gemm tensors must share a device")
+    return _n.CB_MCG if mcg else (_n.CB_MUL1 if mul1 else _n.CB_3INST)
+
+
+def _fat_call(a, packed, out, svh, K, cb, token_idx=None, route_weight=None):
+    m, in_f, n = int(a.size(0)), int(a.size(1)), int(svh.numel())
+    lib = _n.load()
+    with torch.cuda.device(a.device):
+        need = lib.exl3_linear_workspace_size(max(m, 1), in_f, n, int(K))
+        ws = _n.workspace(a.device, need)
+        _n.check(lib.exl3_fat_gemm(a.data_ptr(), m, packed.data_ptr(), svh.data_ptr(), in_f, n, int(K),
+                                   int(cb), out.data_ptr(), _n.ptr(token_idx), _n.ptr(route_weight),
+                                   ws.data_ptr(), ws.numel(), _n.stream_of(a)), "exl3_fat_gemm")
+
+
+def exl3_fat_gemm(a, packed, out, svh, K, mcg, mul1):
+    """Prefill GEMM on a pre-rotated input (csrc/exl3_fat_gemm.cu:266-278):
+    out [M, N] fp32 = (a W~) H/sqrt(128) o svh."""
+    cb = _fat_checks(a, packed, out, svh, K, mcg, mul1)
+    if out.size(0) != a.size(0) or out.size(1) != svh.numel():
+        raise RuntimeError("out shape must be [M, N]")
+    _fat_call(a, packed, out, svh, K, cb)
+
+
+def exl3_fat_gemm_scatter(a, packed, out, svh, token_idx, route_weight, K, mcg, mul1):
+    """Scatter variant (csrc/exl3_fat_gemm.cu:281-305): out[token_idx[r]] +=
+    route_weight[r] * row r; rows of one call must target distinct tokens."""
+    cb = _fat_checks(a, packed, out, svh, K, mcg, mul1)
+    if out.size(1) != svh.numel():
+        raise RuntimeError("out N dimension mismatch")
+    if not (token_idx.is_cuda and route_weight.is_cuda):
+        raise RuntimeError("routing tensors must be CUDA tensors")
+    if not (token_idx.is_contiguous() and route_weight.is_contiguous()):
+        raise RuntimeError("routing tensors must be contiguous")
+    if token_idx.dtype != torch.int64:
+        raise RuntimeError("token_idx must be int64")
+    if route_weight.dtype != torch.float16:
+        raise RuntimeError("route_weight must be float16")
+    if token_idx.numel() != a.size(0) or route_weight.numel() != a.size(0):
+        raise RuntimeError("routing tensors must have M elements")
+    if token_idx.device != a.device or route_weight.device != a.device:
+        raise RuntimeError("routing tensors must share a device with a")
+    _fat_call(a, packed, out, svh, K, cb, token_idx, route_weight)
+
+
 # ---------------------------------------------------------------------------
 # routed-expert MoE
 # ---------------------------------------------------------------------------
