@@ -131,6 +131,23 @@ int exl3_fat_gemm(const void* a, int64_t m, const void* packed, const void* svh,
                   int64_t out_features, int K, int codebook, float* out, const int64_t* token_idx,
                   const void* route_weight, void* workspace, size_t workspace_bytes, void* stream);
 
+/* exl3_linear for callers that cannot allocate device memory when they run
+ * a projection (no counterpart in the reference): e.g. a serving engine that
+ * has already given all free HBM to its KV cache, or a C/FFI host with no
+ * caching allocator, where every cudaMalloc/cudaFree would also synchronise.
+ * Same arguments and result as exl3_linear minus the workspace: the work
+ * buffers live in one file-scope device array of
+ * EXL3_LINEAR_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds
+ * until exit.  Calls needing more scratch are rejected (EXL3_ERR_ARG) before
+ * anything is launched.  The first call on a device looks up the array's
+ * address with that device current; make it before any stream capture.
+ * All calls share the array: calls whose GPU work overlaps race.  The call
+ * itself allocates nothing (no cudaMalloc, cudaFree or allocating library). */
+#define EXL3_LINEAR_NOALLOC_SCRATCH_BYTES (16u << 20)
+int exl3_linear_noalloc(const void* x, int x_dtype, int64_t m, const void* trellis, const void* suh,
+                        const void* svh, int64_t in_features, int64_t out_features, int K,
+                        int codebook, void* y, int y_dtype, void* stream);
+
 /* Phase timing for benchmarks (no reference counterpart; the reference times
  * its kernels with CUDA events in tools/bench_moe_decode.py:24-55).  While
  * enabled, exl3_moe_forward and exl3_linear first launch a spin of

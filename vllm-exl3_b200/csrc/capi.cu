@@ -49,6 +49,11 @@ int check_packed(const char* who, const void* trellis, const void* suh, const vo
 
 }  // namespace
 
+namespace exl3 {
+// lets other translation units of the library report through exl3_last_error
+void set_last_error(const char* msg) { g_last_error = msg; }
+}  // namespace exl3
+
 extern "C" {
 
 int exl3_abi_version(void) { return EXL3_B200_ABI_VERSION; }

@@ -17,7 +17,7 @@ ROOT = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(ROOT, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libexl3_b200.so")
 
-SOURCES = ["capi.cu", "moe.cu", "reconstruct.cu"]
+SOURCES = ["capi.cu", "moe.cu", "reconstruct.cu", "noalloc.cu"]
 HEADERS = ["exl3_common.cuh", "exl3_internal.h"]
 
 NVCC_FLAGS = [
