@@ -76,10 +76,16 @@ __device__ __forceinline__ uint32_t decode_pair(uint32_t wa, uint32_t wb) {
             xa = wa * 89226354u + 64248484u;
             xb = wb * 89226354u + 64248484u;
         }
-        const uint32_t lo = (__byte_perm(xa, xb, 0x5410) & 0x8fff8fffu) ^ 0x3b603b60u;
-        const uint32_t hi = (__byte_perm(xa, xb, 0x7632) & 0x8fff8fffu) ^ 0x3b603b60u;
+        xa = (xa & 0x8fff8fffu) ^ 0x3b603b60u;
+        xb = (xb & 0x8fff8fffu) ^ 0x3b603b60u;
+        // lo + hi of each word as one f16 add, then pack the two sums
+        // (measured cheaper than pairing the halves with byte permutes first)
         uint32_t r;
-        asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(lo), "r"(hi));
+        asm("{\n .reg .f16 a0, a1, b0, b1, sa, sb;\n"
+            " mov.b32 {a0, a1}, %1;\n mov.b32 {b0, b1}, %2;\n"
+            " add.rn.f16 sa, a0, a1;\n add.rn.f16 sb, b0, b1;\n"
+            " mov.b32 %0, {sa, sb};\n}\n"
+            : "=r"(r) : "r"(xa), "r"(xb));
         return r;
     }
 }
@@ -103,18 +109,21 @@ __device__ __forceinline__ void tile_windows(const uint32_t* __restrict__ tile, 
                                              uint32_t (&w)[8]) {
     constexpr int N32 = 8 * K;  // uint32 words per tile
     if constexpr (K == 4) {
-        // b0 = 32l - 12 (mod 1024): unit 2l - 1, o0 = 4.  The 48 stream bits
-        // are the low half of word l-1 followed by word l.
+        // b0 = 32l - 12 (mod 1024): with S = word(l-1):word(l) (64 bits, MSB
+        // first), window j sits at S offset 20 + 4j, i.e. (S >> (28 - 4j)) &
+        // 0xffff.  Byte-aligned windows are one byte permute; the odd-nibble
+        // ones share one funnel shift q = S >> 12.
         const uint32_t wa = tile[(lane + N32 - 1) & (N32 - 1)];
         const uint32_t wb = tile[lane];
-        const uint32_t r0 = __byte_perm(wb, wa, 0x5432);  // (wa.lo << 16) | wb.hi
-        w[0] = (r0 << 4) >> 16;
-        w[1] = __byte_perm(r0, 0u, 0x4421);  // o = 8: (r0 << 8) >> 16
-        w[2] = (r0 << 12) >> 16;
-        w[3] = r0 & 0xffffu;
-        w[4] = (wb << 4) >> 16;
+        const uint32_t r0 = __byte_perm(wb, wa, 0x5432);  // S >> 16
+        const uint32_t q = __funnelshift_r(wb, wa, 12);    // S >> 12
+        w[0] = q >> 16;
+        w[1] = __byte_perm(r0, 0u, 0x4421);
+        w[2] = __byte_perm(q, 0u, 0x4421);
+        w[3] = wb >> 16;
+        w[4] = q & 0xffffu;
         w[5] = __byte_perm(wb, 0u, 0x4421);
-        w[6] = (wb << 12) >> 16;
+        w[6] = (wb >> 4) & 0xffffu;
         w[7] = wb & 0xffffu;
     } else {
         constexpr int UNITS = 16 * K;  // 16-bit units per tile

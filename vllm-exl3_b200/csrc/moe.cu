@@ -1,5 +1,6 @@
 // moe.cu -- routed-expert EXL3 MoE forward (all tokens of a step in one
-// pass) and the dense EXL3 linear, for sm_100a.
+// pass) and the single-projection variants (dense linear, batched expert
+// linear, fat GEMM), for sm_100a.
 //
 // Replaces the reference's per-token cooperative kernels p2b_fused_moe /
 // p2b_fused_moe_mk / p2b_fused_moe_padded (csrc/p2b_moe.cu:643-2428), the
@@ -17,17 +18,17 @@
 //              by expert, each expert's rows padded to 16, work slots of <= 16
 //              rows, split-K counters cleared.
 //  2. rotate   fp16 H128(x o suh)/sqrt128 per (route, projection, 128-block),
-//              stored [proj][kblock][row][128] with a 16-byte XOR swizzle so a
-//              1-D bulk copy lands conflict-free for ldmatrix.
+//              stored [proj][kblock][row][136] (rows padded to 272 bytes so a
+//              1-D bulk copy lands ldmatrix-conflict-free).
 //  3. gemv<2>  gate+up: work item = (slot, 128-column block, k split).  A
 //              producer thread streams the item's trellis rows and rotated
-//              inputs into a shared-memory ring with cp.async.bulk; 16 consumer
-//              warps (projection x 16-column tile) decode each 16x16 tile in
-//              registers straight into mma.m16n8k16 A fragments and
-//              accumulate in fp32.  Split-K partials are reduced in fixed order
-//              by the last CTA of the group (deterministic).  Epilogue: output
-//              FWHT o svh, SwiGLU (+clamp), fp16 round, down-input rotation
-//              o suh_down -> rotated down inputs.
+//              inputs into a shared-memory ring with cp.async.bulk; 8 consumer
+//              warps (one 16-column tile each, gate and up together) decode
+//              each 16x16 tile in registers straight into mma.m16n8k16 A
+//              fragments and accumulate in fp32.  Split-K partials are reduced
+//              in fixed order by the last CTA of the group (deterministic).
+//              Epilogue: output FWHT o svh, SwiGLU (+clamp), fp16 round,
+//              down-input rotation o suh_down -> rotated down inputs.
 //  4. gemv<1>  down: same engine; epilogue FWHT o svh * route weight -> per-route rows.
 //  5. combine  out_t = sum over t's routes in top-k order (no atomics).
 #include <algorithm>
@@ -42,7 +43,12 @@ enum Act : int { ACT_SILU = 0, ACT_SWIGLU_OAI = 3 };
 
 constexpr int kPrepThreads = 1024;
 constexpr int kMaxLocal = 2048;
-constexpr int kYsPitch = 132;  // fp32 pitch of the epilogue tile (conflict-free fragment stores)
+constexpr int kFastRankExperts = 256;  // per-warp histogram ranking up to this many experts
+constexpr int kYsPitch = 132;          // fp32 pitch of the epilogue tile (conflict-free fragment stores)
+constexpr int kXPitch = 136;           // fp16 pitch of a rotated-input row (272 B: ldmatrix conflict-free)
+constexpr int kXSlice = 16 * kXPitch * 2;  // bytes of one 16-row x 128-column input slice
+constexpr int kCW = 8;                 // consumer warps: one per 16-column tile of a 128-column block
+constexpr int kGemvThreads = (kCW + 1) * 32;
 
 struct WsPtrs {
     int* status;
@@ -142,6 +148,7 @@ __device__ int block_excl_scan(int v, int* total, int* sh32) {
 __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
     __shared__ int cnt[kMaxLocal];
     __shared__ int poff[kMaxLocal];
+    __shared__ unsigned short wcnt[kPrepThreads / 32][kFastRankExperts];
     __shared__ int sh32[32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int E = a.n_local;
@@ -186,27 +193,51 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
     }
     if (tid == 0) *a.w.nslots = tot_s;
     __syncthreads();
-    for (int e = tid; e < E; e += kPrepThreads) cnt[e] = poff[e];  // running position
+    for (int e = tid; e < E; e += kPrepThreads) cnt[e] = poff[e];  // running position (general path)
     __syncthreads();
 
-    // stable placement: route order within each expert
+    // stable placement: route order within each expert.  Running start of
+    // each expert: poff[e] (fast path) or cnt[e] (general path).
+    const bool fast = E <= kFastRankExperts;
     for (int64_t base = 0; base < R; base += kPrepThreads) {
         const int64_t r = base + tid;
         const int e = r < R ? local_expert(a, r) : -1;
         const unsigned mask = __match_any_sync(0xffffffffu, e);
         const int rank = __popc(mask & ((1u << lane) - 1u));
         const int leader = __ffs(mask) - 1;
-        int my_base = 0;
-        for (int w = 0; w < kPrepThreads / 32; ++w) {
-            if (warp == w && e >= 0 && lane == leader) {
-                my_base = cnt[e];
-                cnt[e] += __popc(mask);
+        int p = -1;
+        if (fast) {
+            // per-warp counts -> exclusive prefix over warps per expert (in
+            // wcnt), chunk totals in cnt; three barriers per 1024 routes
+            for (int i = tid; i < (kPrepThreads / 32) * kFastRankExperts; i += kPrepThreads)
+                (&wcnt[0][0])[i] = 0;
+            __syncthreads();
+            if (e >= 0 && lane == leader) wcnt[warp][e] = (unsigned short)__popc(mask);
+            __syncthreads();
+            for (int x = tid; x < E; x += kPrepThreads) {
+                int run = 0;
+                for (int w = 0; w < kPrepThreads / 32; ++w) {
+                    const int c = wcnt[w][x];
+                    wcnt[w][x] = (unsigned short)run;
+                    run += c;
+                }
+                cnt[x] = run;
             }
             __syncthreads();
+            if (e >= 0) p = poff[e] + int(wcnt[warp][e]) + rank;
+        } else {
+            int my_base = 0;
+            for (int w = 0; w < kPrepThreads / 32; ++w) {
+                if (warp == w && e >= 0 && lane == leader) {
+                    my_base = cnt[e];
+                    cnt[e] += __popc(mask);
+                }
+                __syncthreads();
+            }
+            my_base = __shfl_sync(0xffffffffu, my_base, leader);
+            if (e >= 0) p = my_base + rank;
         }
-        my_base = __shfl_sync(0xffffffffu, my_base, leader);
         if (e >= 0) {
-            const int p = my_base + rank;
             a.w.route_pos[r] = p;
             a.w.sorted_tok[p] = int(r / a.topk);
             a.w.sorted_route[p] = int(r);
@@ -214,6 +245,11 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
             a.w.sorted_w[p] = (a.linear || a.batched) ? 1.f : load_as_float(a.weights, r, a.w_dtype);
         } else if (r < Rmax) {
             a.w.route_pos[r] = -1;
+        }
+        if (fast) {
+            __syncthreads();
+            for (int x = tid; x < E; x += kPrepThreads) poff[x] += cnt[x];
+            __syncthreads();
         }
     }
     for (int64_t r = R + tid; r < Rmax; r += kPrepThreads) a.w.route_pos[r] = -1;
@@ -234,7 +270,7 @@ struct RotArgs {
     __half* xr;
     int64_t rpad;
     int* status;
-    int prerotated;  // x already rotated (fp16): copy into the swizzled layout only
+    int prerotated;  // x already rotated (fp16): copy into the padded layout only
 };
 
 __device__ __forceinline__ const __half* proj_suh(const ProjRef& p, int e) {
@@ -251,12 +287,8 @@ __device__ __forceinline__ int proj_k(const ProjRef& p, int e) {
     return p.k_tbl ? int(p.k_tbl[e]) : p.k_uniform;
 }
 
-// swizzled element offset of column c in a 128-wide fp16 row of sorted row p
-__device__ __forceinline__ int swz(int c, int64_t p) {
-    return ((((c >> 3) ^ int(p & 7))) << 3) | (c & 7);
-}
-
 __global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a) {
+    // one warp per (sorted row, projection, 128-block)
     const int lane = threadIdx.x & 31;
     const int nkb = a.in_f / 128;
     const int64_t per_slot = int64_t(16) * a.nproj * nkb;
@@ -274,7 +306,7 @@ __global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a) {
         const int tok = a.sorted_tok[p];
         const __half* suh = a.prerotated ? nullptr : proj_suh(a.proj[pj], sl.x);
         if ((suh == nullptr && !a.prerotated) || tok < 0) {
-            if (lane == 0) set_status(a.status, suh == nullptr ? DEV_NULL_PTR : DEV_BAD_ROUTE);
+            if (lane == 0) set_status(a.status, tok < 0 ? DEV_BAD_ROUTE : DEV_NULL_PTR);
             continue;
         }
         float v[4];
@@ -285,15 +317,14 @@ __global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a) {
             const float xv = __half2float(__float2half_rn(load_as_float(a.x, int64_t(tok) * a.in_f + c, a.x_dtype)));
             v[i] = a.prerotated ? xv : xv * __half2float(suh[c]);
         }
-        __half* dst = a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * 128;
-        if (a.prerotated) {
+        __half* dst = a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * kXPitch;
+        if (!a.prerotated) {
+            fwht128_warp(v, lane);
             #pragma unroll
-            for (int i = 0; i < 4; ++i) dst[swz(lane + 32 * i, p)] = __float2half_rn(v[i]);
-            continue;
+            for (int i = 0; i < 4; ++i) v[i] *= kHadNorm;
         }
-        fwht128_warp(v, lane);
         #pragma unroll
-        for (int i = 0; i < 4; ++i) dst[swz(lane + 32 * i, p)] = __float2half_rn(v[i] * kHadNorm);
+        for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2half_rn(v[i]);
     }
 }
 
@@ -338,15 +369,14 @@ struct GemvSmem {
     char* stages;
 };
 
-template <int NPROJ>
-__host__ __device__ constexpr int gemv_threads() {
-    return (8 * NPROJ + 1) * 32;
+// stage = trellis region (NPROJ x 8 k-tile rows x 8 tiles, packed at each
+// projection's own K, capacity kmax) + NPROJ rotated-input slices
+__host__ __device__ inline size_t gemv_trellis_bytes(int nproj, int kmax) {
+    return size_t(nproj) * kKtPerStage * 256 * kmax;
 }
-
 __host__ __device__ inline size_t gemv_stage_bytes(int nproj, int kmax) {
-    return size_t(nproj) * (kKtPerStage * 8 * 32 * kmax) + size_t(nproj) * 16 * 256;
+    return (gemv_trellis_bytes(nproj, kmax) + size_t(nproj) * kXSlice + 127) & ~size_t(127);
 }
-
 __host__ __device__ inline size_t gemv_fixed_bytes(int nproj, int stages) {
     const size_t bars = (size_t(stages) * 2 * 8 + 8 * 4 + 127) & ~size_t(127);
     const size_t ys = (size_t(nproj) * 16 * kYsPitch * 4 + 127) & ~size_t(127);
@@ -412,35 +442,42 @@ __device__ __forceinline__ bool guarded_wait(uint64_t* bar, uint32_t parity, int
     return false;
 }
 
-template <int K, int CB>
-__device__ __forceinline__ void stage_mma(const uint32_t* __restrict__ trow0, int row_stride_words,
-                                          int nt, uint32_t xs_addr, int lane, bool two,
-                                          float (&acc)[2][4]) {
-    const int brow = (lane & 7) + ((lane >> 4) << 3);
-    const int bhalf = (lane >> 3) & 1;
-    #pragma unroll 2
+// One stage for NP projections that share one K: per k-tile, every
+// projection's tile of this warp's 16 columns is decoded (independent chains
+// for the scheduler) and multiplied by the 16-row input slice.
+//   tiles: trellis region of the stage + this warp's tile offset (uint32 words)
+//   xs:    per-lane ldmatrix address of projection 0's input slice
+template <int K, int CB, int NP>
+__device__ __forceinline__ void stage_mma(const uint32_t* __restrict__ tiles, uint32_t xs, int lane,
+                                          bool two, float (&acc)[NP][2][4]) {
+    constexpr int ROW = 64 * K;                // words per k-tile row (8 tiles of 8K words)
+    constexpr int REGION = kKtPerStage * ROW;  // words per projection region
+    #pragma unroll
     for (int kk = 0; kk < kKtPerStage; ++kk) {
-        uint32_t af[4];
-        decode_tile_afrag<K, CB>(trow0 + kk * row_stride_words + nt * (8 * K), lane, af);
-        uint32_t b[4];
-        const int ch = 2 * kk + bhalf;
-        ldmatrix_x4(b, xs_addr + brow * 256 + ((ch ^ (brow & 7)) << 4));
-        mma_16816(acc[0], af, b[0], b[1]);
-        if (two) mma_16816(acc[1], af, b[2], b[3]);
+        uint32_t af[NP][4];
+        #pragma unroll
+        for (int p = 0; p < NP; ++p) decode_tile_afrag<K, CB>(tiles + p * REGION + kk * ROW, lane, af[p]);
+        #pragma unroll
+        for (int p = 0; p < NP; ++p) {
+            uint32_t b[4];
+            ldmatrix_x4(b, xs + p * kXSlice + kk * 32);
+            mma_16816(acc[p][0], af[p], b[0], b[1]);
+            if (two) mma_16816(acc[p][1], af[p], b[2], b[3]);
+        }
     }
 }
 
-template <int CB>
-__device__ __forceinline__ void stage_mma_k(int K, const uint32_t* trow0, int row_stride_words, int nt,
-                                            uint32_t xs_addr, int lane, bool two, float (&acc)[2][4]) {
+template <int CB, int NP>
+__device__ __forceinline__ void stage_mma_k(int K, const uint32_t* tiles, uint32_t xs, int lane, bool two,
+                                            float (&acc)[NP][2][4]) {
     switch (K) {
-        case 2: stage_mma<2, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
-        case 3: stage_mma<3, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
-        case 4: stage_mma<4, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
-        case 5: stage_mma<5, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
-        case 6: stage_mma<6, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
-        case 7: stage_mma<7, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
-        case 8: stage_mma<8, CB>(trow0, row_stride_words, nt, xs_addr, lane, two, acc); break;
+        case 2: stage_mma<2, CB, NP>(tiles, xs, lane, two, acc); break;
+        case 3: stage_mma<3, CB, NP>(tiles, xs, lane, two, acc); break;
+        case 4: stage_mma<4, CB, NP>(tiles, xs, lane, two, acc); break;
+        case 5: stage_mma<5, CB, NP>(tiles, xs, lane, two, acc); break;
+        case 6: stage_mma<6, CB, NP>(tiles, xs, lane, two, acc); break;
+        case 7: stage_mma<7, CB, NP>(tiles, xs, lane, two, acc); break;
+        case 8: stage_mma<8, CB, NP>(tiles, xs, lane, two, acc); break;
         default: break;
     }
 }
@@ -448,22 +485,21 @@ __device__ __forceinline__ void stage_mma_k(int K, const uint32_t* trow0, int ro
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
 template <int NPROJ, int EPI, int CB>
-__global__ void __launch_bounds__(gemv_threads<NPROJ>(), (NPROJ == 1 ? 2 : 1))
+__global__ void __launch_bounds__(kGemvThreads, 2)
 gemv_kernel(const __grid_constant__ GemvArgs a) {
-    constexpr int NCW = 8 * NPROJ;  // consumer warps
-    constexpr int NCT = NCW * 32;
+    constexpr int NCT = kCW * 32;
     extern __shared__ __align__(128) char smem_raw[];
     const int S = a.stages;
     GemvSmem sm = gemv_smem(smem_raw, NPROJ, S);
     const size_t stage_bytes = gemv_stage_bytes(NPROJ, a.kmax);
-    const int row_words = 8 * 8 * a.kmax;  // uint32 capacity of one k-tile row (8 tiles)
+    const size_t xs_off = gemv_trellis_bytes(NPROJ, a.kmax);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     volatile int* abort_flag = sm.flags;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&sm.full[s], 1);
-            mbar_init(&sm.empty[s], NCW);
+            mbar_init(&sm.empty[s], kCW);
         }
         sm.flags[0] = 0;
         sm.flags[1] = 0;
@@ -475,7 +511,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
     const int nkb = a.in_f / 128;
     const int ntiles_out = a.out_f / 16;
 
-    if (warp == NCW) {
+    if (warp == kCW) {
         // ------------------------------ producer ------------------------------
         if (lane != 0) return;
         uint32_t q = 0;
@@ -495,27 +531,29 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 const uint32_t ph = (q / uint32_t(S)) & 1u;
                 if (!guarded_wait(&sm.empty[s], ph ^ 1u, a.status, abort_flag)) break;
                 char* st = sm.stages + size_t(s) * stage_bytes;
-                uint32_t bytes = NPROJ * 16 * 256;
+                uint32_t bytes = NPROJ * kXSlice;
                 #pragma unroll
                 for (int p = 0; p < NPROJ; ++p)
                     if (ok[p]) bytes += kKtPerStage * 256 * Kp[p];
                 mbar_arrive_expect_tx(&sm.full[s], bytes);
+                size_t region = 0;
                 #pragma unroll
                 for (int p = 0; p < NPROJ; ++p) {
-                    if (!ok[p]) continue;
-                    const int tw = 16 * Kp[p];  // int16 per tile
-                    for (int kk = 0; kk < kKtPerStage; ++kk) {
-                        const uint16_t* src = tp[p] + (int64_t(kt + kk) * ntiles_out + int64_t(I.cb) * 8) * tw;
-                        char* dst = st + (size_t(p) * kKtPerStage + kk) * row_words * 4;
-                        bulk_g2s(dst, src, uint32_t(256 * Kp[p]), &sm.full[s]);
+                    const int rowb = 256 * Kp[p];  // bytes of 8 tiles
+                    if (ok[p]) {
+                        const int tw = 16 * Kp[p];  // int16 per tile
+                        for (int kk = 0; kk < kKtPerStage; ++kk) {
+                            const uint16_t* src = tp[p] + (int64_t(kt + kk) * ntiles_out + int64_t(I.cb) * 8) * tw;
+                            bulk_g2s(st + region + size_t(kk) * rowb, src, uint32_t(rowb), &sm.full[s]);
+                        }
                     }
+                    region += size_t(kKtPerStage) * (ok[p] ? rowb : 0);
                 }
                 const int kb = kt / kKtPerStage;
                 #pragma unroll
                 for (int p = 0; p < NPROJ; ++p) {
-                    const __half* src = a.xin + ((int64_t(p) * nkb + kb) * a.rpad + I.p0) * 128;
-                    char* dst = st + size_t(NPROJ) * kKtPerStage * row_words * 4 + size_t(p) * 4096;
-                    bulk_g2s(dst, src, 4096u, &sm.full[s]);
+                    const __half* src = a.xin + ((int64_t(p) * nkb + kb) * a.rpad + I.p0) * kXPitch;
+                    bulk_g2s(st + xs_off + size_t(p) * kXSlice, src, uint32_t(kXSlice), &sm.full[s]);
                 }
             }
         }
@@ -529,24 +567,52 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
     }
 
     // ------------------------------ consumers ------------------------------
-    const int cw = warp;
-    const int pj = cw / 8, nt = cw % 8;
+    const int cw = warp;  // 16-column tile of the 128-column block
+    // per-lane ldmatrix row address inside an input slice (rows padded to 272 B)
+    const int brow = (lane & 7) + ((lane >> 4) << 3);
+    const uint32_t xs_lane = uint32_t(brow * kXPitch * 2 + ((lane >> 3) & 1) * 16);
     uint32_t q = 0;
     for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
         const ItemInfo I = gemv_item(a, it);
-        const bool ok = proj_ok(a.proj[pj], I.e, a.kmax, a.status, false);
-        const int K = proj_k(a.proj[pj], I.e);
+        bool ok[NPROJ];
+        int Kp[NPROJ];
+        #pragma unroll
+        for (int p = 0; p < NPROJ; ++p) {
+            ok[p] = proj_ok(a.proj[p], I.e, a.kmax, a.status, false);
+            Kp[p] = proj_k(a.proj[p], I.e);
+        }
+        bool same = ok[0];
+        #pragma unroll
+        for (int p = 1; p < NPROJ; ++p) same = same && ok[p] && Kp[p] == Kp[0];
         const bool two = I.rows > 8;
-        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        float acc[NPROJ][2][4];
+        #pragma unroll
+        for (int p = 0; p < NPROJ; ++p)
+            #pragma unroll
+            for (int i = 0; i < 8; ++i) acc[p][i >> 2][i & 3] = 0.f;
         for (int kt = I.kt0; kt < I.kt1; kt += kKtPerStage, ++q) {
             const int s = int(q % uint32_t(S));
             const uint32_t ph = (q / uint32_t(S)) & 1u;
             const bool landed = guarded_wait(&sm.full[s], ph, a.status, abort_flag);
-            if (landed && ok) {
+            if (landed) {
                 const char* st = sm.stages + size_t(s) * stage_bytes;
-                const uint32_t* trow0 = reinterpret_cast<const uint32_t*>(st + size_t(pj) * kKtPerStage * row_words * 4);
-                const uint32_t xs = smem_u32(st + size_t(NPROJ) * kKtPerStage * row_words * 4 + size_t(pj) * 4096);
-                stage_mma_k<CB>(K, trow0, row_words, nt, xs, lane, two, acc);
+                const uint32_t xs = smem_u32(st + xs_off) + xs_lane;
+                if (same) {
+                    const uint32_t* tiles = reinterpret_cast<const uint32_t*>(st) + cw * 8 * Kp[0];
+                    stage_mma_k<CB, NPROJ>(Kp[0], tiles, xs, lane, two, acc);
+                } else {
+                    size_t region = 0;
+                    #pragma unroll
+                    for (int p = 0; p < NPROJ; ++p) {
+                        if (ok[p]) {
+                            const uint32_t* tiles =
+                                reinterpret_cast<const uint32_t*>(st + region) + cw * 8 * Kp[p];
+                            float (&accp)[1][2][4] = *reinterpret_cast<float (*)[1][2][4]>(&acc[p]);
+                            stage_mma_k<CB, 1>(Kp[p], tiles, xs + p * kXSlice, lane, two, accp);
+                            region += size_t(kKtPerStage) * 256 * Kp[p];
+                        }
+                    }
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.empty[s]);
@@ -554,9 +620,11 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
 
         // ---- split-K: last CTA of the group reduces partials in split order
         if (a.nsplit > 1) {
-            float* pp = a.part + ((int64_t(I.group) * a.nsplit + I.sp) * NCW + cw) * 256;
+            float* pp = a.part + ((int64_t(I.group) * a.nsplit + I.sp) * kCW + cw) * (NPROJ * 256);
             #pragma unroll
-            for (int i = 0; i < 8; ++i) __stcg(pp + i * 32 + lane, acc[i >> 2][i & 3]);
+            for (int p = 0; p < NPROJ; ++p)
+                #pragma unroll
+                for (int i = 0; i < 8; ++i) __stcg(pp + (p * 8 + i) * 32 + lane, acc[p][i >> 2][i & 3]);
             __threadfence();
             named_bar_sync(1, NCT);
             if (threadIdx.x == 0) {
@@ -569,28 +637,35 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             if (!sm.flags[1]) continue;
             __threadfence();
             #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i >> 2][i & 3] = 0.f;
-            for (int sp = 0; sp < a.nsplit; ++sp) {
-                const float* rp = a.part + ((int64_t(I.group) * a.nsplit + sp) * NCW + cw) * 256;
+            for (int p = 0; p < NPROJ; ++p)
                 #pragma unroll
-                for (int i = 0; i < 8; ++i) acc[i >> 2][i & 3] += __ldcg(rp + i * 32 + lane);
+                for (int i = 0; i < 8; ++i) acc[p][i >> 2][i & 3] = 0.f;
+            for (int sp = 0; sp < a.nsplit; ++sp) {
+                const float* rp = a.part + ((int64_t(I.group) * a.nsplit + sp) * kCW + cw) * (NPROJ * 256);
+                #pragma unroll
+                for (int p = 0; p < NPROJ; ++p)
+                    #pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[p][i >> 2][i & 3] += __ldcg(rp + (p * 8 + i) * 32 + lane);
             }
         }
 
         // ---- fragments -> [proj][token row][column] tile
-        float* ys = sm.ys + pj * 16 * kYsPitch;
         #pragma unroll
-        for (int nb = 0; nb < 2; ++nb)
+        for (int p = 0; p < NPROJ; ++p) {
+            float* ys = sm.ys + p * 16 * kYsPitch;
             #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int m = nt * 16 + (lane >> 2) + 8 * (i >> 1);
-                const int n = nb * 8 + 2 * (lane & 3) + (i & 1);
-                ys[n * kYsPitch + m] = acc[nb][i];
-            }
+            for (int nb = 0; nb < 2; ++nb)
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int m = cw * 16 + (lane >> 2) + 8 * (i >> 1);
+                    const int n = nb * 8 + 2 * (lane & 3) + (i & 1);
+                    ys[n * kYsPitch + m] = acc[p][nb][i];
+                }
+        }
         named_bar_sync(1, NCT);
 
         // ---- output rotation o svh
-        for (int v = cw; v < NPROJ * I.rows; v += NCW) {
+        for (int v = cw; v < NPROJ * I.rows; v += kCW) {
             const int p = v / I.rows, r = v % I.rows;
             float* row = sm.ys + (p * 16 + r) * kYsPitch;
             float x[4];
@@ -608,7 +683,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
 
         if constexpr (EPI == EPI_GATEUP) {
             const __half* dsuh = proj_suh(a.down, I.e);
-            for (int r = cw; r < I.rows; r += NCW) {
+            for (int r = cw; r < I.rows; r += kCW) {
                 const float* gr = sm.ys + r * kYsPitch;
                 const float* ur = sm.ys + (16 + r) * kYsPitch;
                 float x[4];
@@ -628,12 +703,12 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 }
                 fwht128_warp(x, lane);
                 const int64_t p = I.p0 + r;
-                __half* dst = a.a2 + (int64_t(I.cb) * a.rpad + p) * 128;
+                __half* dst = a.a2 + (int64_t(I.cb) * a.rpad + p) * kXPitch;
                 #pragma unroll
-                for (int i = 0; i < 4; ++i) dst[swz(lane + 32 * i, p)] = __float2half_rn(x[i] * kHadNorm);
+                for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2half_rn(x[i] * kHadNorm);
             }
         } else if constexpr (EPI == EPI_DOWN) {
-            for (int r = cw; r < I.rows; r += NCW) {
+            for (int r = cw; r < I.rows; r += kCW) {
                 const float* row = sm.ys + r * kYsPitch;
                 const int64_t p = I.p0 + r;
                 const float w = a.sorted_w[p];
@@ -642,7 +717,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = row[lane + 32 * i] * w;
             }
         } else if constexpr (EPI == EPI_LINEAR) {
-            for (int r = cw; r < I.rows; r += NCW) {
+            for (int r = cw; r < I.rows; r += kCW) {
                 const float* row = sm.ys + r * kYsPitch;
                 const int tok = a.sorted_tok[I.p0 + r];
                 if (tok < 0) continue;
@@ -661,7 +736,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             }
         } else {
             // EPI_ROUTE: route r = t * topk + j -> output row j * t_max + t
-            for (int r = cw; r < I.rows; r += NCW) {
+            for (int r = cw; r < I.rows; r += kCW) {
                 const float* row = sm.ys + r * kYsPitch;
                 const int rt = a.sorted_route[I.p0 + r];
                 if (rt < 0) continue;
@@ -713,10 +788,11 @@ combine_kernel(const int* __restrict__ route_pos, const float* __restrict__ yd, 
 // ---------------------------------------------------------------------------
 // host: planning and launch
 // ---------------------------------------------------------------------------
-static constexpr size_t kSmemBudget = 227 * 1024;
+static constexpr size_t kSmemPerSm = 228 * 1024;
+static constexpr int kCtasPerSm = 2;
 
-static void pick_stages(int nproj, int kmax, int ctas_per_sm, int& stages, size_t& smem) {
-    const size_t per_cta = kSmemBudget / ctas_per_sm - (ctas_per_sm > 1 ? 1024 : 0);
+static void pick_stages(int nproj, int kmax, int& stages, size_t& smem) {
+    const size_t per_cta = kSmemPerSm / kCtasPerSm - 1024;
     const size_t sb = gemv_stage_bytes(nproj, kmax);
     int s = 8;
     while (s > 2 && gemv_fixed_bytes(nproj, s) + size_t(s) * sb > per_cta) --s;
@@ -739,13 +815,13 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
               bool linear, int num_sms) {
     if (t_max < 1 || topk < 1 || hidden < 128 || hidden % 128 || n_local < 1 || n_local > kMaxLocal)
         return false;
-    if (!linear && (inter < 128 || inter % 128)) return false;
+    if (inter < 128 || inter % 128) return false;
     if (kmax < 2 || kmax > 8) return false;
     p = MoePlan();
     p.t_max = t_max;
     p.topk = topk;
-    p.hidden = hidden;  // linear: in_features
-    p.inter = inter;    // linear: out_features
+    p.hidden = hidden;  // single projection: in_features
+    p.inter = inter;    // single projection: out_features
     p.n_local = n_local;
     p.kmax = kmax;
     p.linear = linear;
@@ -754,21 +830,16 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     p.smax = p.routes / 16 + act_max + 1;
     p.rpad = p.smax * 16;
 
-    if (linear) {
-        // one projection: in = hidden, out = inter
-        p.ncb1 = inter / 128;
-        pick_stages(1, kmax, 2, p.stages1, p.smem1);
-        p.grid1 = num_sms * 2;
-        pick_split(p.smax * p.ncb1, p.grid1, hidden / 16, p.nsplit1, p.ktps1);
-    } else {
-        p.ncb1 = inter / 128;
-        pick_stages(2, kmax, 1, p.stages1, p.smem1);
-        p.grid1 = num_sms;
-        pick_split(act_max * p.ncb1, p.grid1, hidden / 16, p.nsplit1, p.ktps1);
+    const int grid = num_sms * kCtasPerSm;
+    p.ncb1 = inter / 128;
+    pick_stages(linear ? 1 : 2, kmax, p.stages1, p.smem1);
+    p.grid1 = grid;
+    pick_split(p.smax * p.ncb1, grid, hidden / 16, p.nsplit1, p.ktps1);
+    if (!linear) {
         p.ncb2 = hidden / 128;
-        pick_stages(1, kmax, 2, p.stages2, p.smem2);
-        p.grid2 = num_sms * 2;
-        pick_split(act_max * p.ncb2, p.grid2, inter / 16, p.nsplit2, p.ktps2);
+        pick_stages(1, kmax, p.stages2, p.smem2);
+        p.grid2 = grid;
+        pick_split(act_max * p.ncb2, grid, inter / 16, p.nsplit2, p.ktps2);
     }
 
     size_t o = 0;
@@ -786,12 +857,11 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     p.off_sorted_exp = take(size_t(p.rpad) * 4);
     p.off_sorted_w = take(size_t(p.rpad) * 4);
     const int nproj1 = linear ? 1 : 2;
-    p.off_xr = take(size_t(nproj1) * p.rpad * hidden * 2);
-    p.off_a2 = take(linear ? 0 : size_t(p.rpad) * inter * 2);
+    p.off_xr = take(size_t(nproj1) * (hidden / 128) * p.rpad * kXPitch * 2);
+    p.off_a2 = take(linear ? 0 : size_t(inter / 128) * p.rpad * kXPitch * 2);
     p.off_yd = take(linear ? 0 : size_t(p.rpad) * hidden * 4);
-    const int ncw1 = 8 * nproj1;
-    p.off_part1 = take(p.nsplit1 > 1 ? size_t(p.smax) * p.ncb1 * p.nsplit1 * ncw1 * 256 * 4 : 0);
-    p.off_part2 = take(!linear && p.nsplit2 > 1 ? size_t(p.smax) * p.ncb2 * p.nsplit2 * 8 * 256 * 4 : 0);
+    p.off_part1 = take(p.nsplit1 > 1 ? size_t(p.smax) * p.ncb1 * p.nsplit1 * kCW * nproj1 * 256 * 4 : 0);
+    p.off_part2 = take(!linear && p.nsplit2 > 1 ? size_t(p.smax) * p.ncb2 * p.nsplit2 * kCW * 256 * 4 : 0);
     p.off_cnt1 = take(size_t(p.smax) * p.ncb1 * 4);
     p.off_cnt2 = take(linear ? 0 : size_t(p.smax) * p.ncb2 * 4);
     p.total = o;
@@ -806,7 +876,7 @@ static cudaError_t launch_gemv(int cb, const GemvArgs& g, int grid, size_t smem,
     else kern = gemv_kernel<NPROJ, EPI, CB_3INST>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
-    kern<<<grid, gemv_threads<NPROJ>(), smem, s>>>(g);
+    kern<<<grid, kGemvThreads, smem, s>>>(g);
     return cudaGetLastError();
 }
 
@@ -865,7 +935,7 @@ int profile_read(float* ms, int max_phases) {
 
 cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s) {
     const WsPtrs w = ws_ptrs(p, ws);
-    const int nsm = std::max(1, p.grid1 / (p.linear ? 2 : 1));
+    const int nsm = std::max(1, p.grid1 / kCtasPerSm);
 
     PrepArgs pa;
     pa.ids = c.ids;
