@@ -1,5 +1,8 @@
 """GPU parity of the decode kernels against the CPU oracle, through the C ABI.
 
+Rows >= 32 per projection take the tcgen05 grouped-GEMM path, fewer the
+decode GEMV; both are covered.
+
 * exl3_reconstruct (dequant_trellis): bit-exact with the oracle and with the
   reference fixtures, K 2..8 x codebooks 3INST/MCG/mul1;
 * exl3_decode_raw: bit-exact W~;
@@ -102,7 +105,7 @@ def test_had_r_128(native, cuda):
     np.testing.assert_allclose(y.cpu().numpy().astype(np.float64), want, rtol=2e-3, atol=2e-3)
 
 
-@pytest.mark.parametrize("m", [1, 5, 8, 16, 17, 40])
+@pytest.mark.parametrize("m", [1, 5, 8, 16, 17, 40, 128, 300])
 @pytest.mark.parametrize("K,cb", [(2, 1), (3, 1), (4, 1), (3, 2), (4, 2), (8, 1)])
 def test_linear_matches_dense(native, cuda, m, K, cb):
     import torch

@@ -73,6 +73,26 @@ def test_decode_config_shape_matches_eager_loop(native, cuda, tokens):
     _close(_run(layer, cuda, x, ids, w, dtype=torch.float32), want)
 
 
+@pytest.mark.parametrize("tokens", [96, 300])
+def test_prefill_gemm_path_uniform_k(native, cuda, tokens):
+    """>= 32 routes per expert: the tcgen05 grouped GEMM path."""
+    import torch
+    pack, layer, x, ids, w = _setup(cuda, "cfg2", seed=40 + tokens, tokens=tokens, n_experts=16,
+                                    hidden=512, inter=256)
+    want = oracle.moe_eager(x, ids, w, _dense(pack))
+    _close(_run(layer, cuda, x, ids, w, dtype=torch.float32), want)
+
+
+def test_prefill_gemm_path_mixed_k_mul1_limit(native, cuda):
+    import torch
+    pack, layer, x, ids, w = _setup(cuda, "cfg3", seed=77, tokens=256, n_experts=10, hidden=384,
+                                    inter=256, k_choices=(2, 3, 4), k_probs=None)
+    dense = _dense(pack)
+    for limit in (None, 0.75):
+        want = oracle.moe_eager(x, ids, w, dense, limit=limit)
+        _close(_run(layer, cuda, x, ids, w, dtype=torch.float32, limit=limit), want)
+
+
 def test_mixed_k_mul1_with_limit(native, cuda):
     import torch
     pack, layer, x, ids, w = _setup(cuda, "cfg3", seed=5, tokens=24, n_experts=12, hidden=512,

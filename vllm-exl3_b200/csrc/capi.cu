@@ -229,7 +229,7 @@ size_t exl3_batched_linear_workspace_size(int64_t m, int n_active, int64_t in_f,
     exl3::MoePlan p;
     if (m < 1 || n_active < 1 || in_f > INT32_MAX || out_f > INT32_MAX) return 0;
     if (!exl3::plan_moe(p, m, n_active, int(in_f), int(out_f), n_table, K < 2 ? 8 : K, true,
-                        exl3::num_sms_current()))
+                        exl3::num_sms_current(), false))
         return 0;
     return p.total;
 }
@@ -250,7 +250,7 @@ int exl3_batched_linear(const void* x, int x_dtype, int64_t m, const int64_t* tr
     if (n_table < 1 || n_table > 2048) return fail(EXL3_ERR_ARG, "%s: table length must be in 1..2048", who);
     if (n_active < 1 || m < 1) return fail(EXL3_ERR_ARG, "%s: need m >= 1 and at least one expert", who);
     exl3::MoePlan p;
-    if (!exl3::plan_moe(p, m, n_active, int(in_f), int(out_f), n_table, K, true, exl3::num_sms_current()))
+    if (!exl3::plan_moe(p, m, n_active, int(in_f), int(out_f), n_table, K, true, exl3::num_sms_current(), false))
         return fail(EXL3_ERR_ARG, "%s: unsupported geometry", who);
     if (!ws || ws_bytes < p.total)
         return fail(EXL3_ERR_WORKSPACE, "%s: workspace of %zu bytes required (got %zu)", who, p.total, ws_bytes);

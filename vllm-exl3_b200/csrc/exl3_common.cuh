@@ -21,6 +21,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "exl3_internal.h"
+
 namespace exl3 {
 
 enum Codebook : int { CB_3INST = 0, CB_MCG = 1, CB_MUL1 = 2 };
@@ -314,6 +316,21 @@ __device__ __forceinline__ void store_from_float(void* p, int64_t i, int dt, flo
 __device__ __forceinline__ int64_t load_id(const void* p, int64_t i, int dt) {
     return dt == DT_I64 ? static_cast<const int64_t*>(p)[i]
                         : static_cast<int64_t>(static_cast<const int32_t*>(p)[i]);
+}
+
+// Per-expert pointers of one projection family (tables) or a dense projection.
+__device__ __forceinline__ const __half* proj_suh(const ProjRef& p, int e) {
+    return p.suh_tbl ? reinterpret_cast<const __half*>(p.suh_tbl[e]) : static_cast<const __half*>(p.suh);
+}
+__device__ __forceinline__ const __half* proj_svh(const ProjRef& p, int e) {
+    return p.svh_tbl ? reinterpret_cast<const __half*>(p.svh_tbl[e]) : static_cast<const __half*>(p.svh);
+}
+__device__ __forceinline__ const uint16_t* proj_trellis(const ProjRef& p, int e) {
+    return p.trellis_tbl ? reinterpret_cast<const uint16_t*>(p.trellis_tbl[e])
+                         : static_cast<const uint16_t*>(p.trellis);
+}
+__device__ __forceinline__ int proj_k(const ProjRef& p, int e) {
+    return p.k_tbl ? int(p.k_tbl[e]) : p.k_uniform;
 }
 
 }  // namespace exl3

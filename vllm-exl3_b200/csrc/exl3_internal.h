@@ -43,9 +43,14 @@ struct MoePlan {
     int ncb1 = 0, nsplit1 = 1, ktps1 = 0, grid1 = 0, stages1 = 0;
     int ncb2 = 0, nsplit2 = 1, ktps2 = 0, grid2 = 0, stages2 = 0;
     size_t smem1 = 0, smem2 = 0;
+    // prefill path: tcgen05 grouped GEMM over 128-row expert tiles
+    bool gemm = false;
+    int64_t t128max = 0;
+    int tc_stages = 0;
+    size_t tc_smem = 0;
     // offsets
     size_t off_status = 0, off_nslots = 0, off_slots = 0, off_route_pos = 0, off_sorted_tok = 0,
-           off_sorted_route = 0,
+           off_sorted_route = 0, off_ntiles128 = 0, off_tiles128 = 0, off_g = 0, off_u = 0, off_x2 = 0,
            off_sorted_exp = 0, off_sorted_w = 0, off_xr = 0, off_a2 = 0, off_yd = 0,
            off_part1 = 0, off_part2 = 0, off_cnt1 = 0, off_cnt2 = 0;
     size_t total = 0;
@@ -53,7 +58,7 @@ struct MoePlan {
 
 // Fill a plan; returns false if the geometry is unsupported.
 bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_local, int kmax,
-              bool linear, int num_sms);
+              bool linear, int num_sms, bool allow_gemm = true);
 
 struct MoeCall {
     const void* x = nullptr;
@@ -87,6 +92,7 @@ cudaError_t run_had128(const void* x, void* y, int64_t rows, int64_t n, const vo
                        const void* post, float scale, cudaStream_t s);
 
 int num_sms_current();
+void tc_pick_stages(int kmax, int& stages, size_t& smem);
 void profile_enable(bool on, long long delay_cycles);
 int profile_read(float* ms, int max_phases);
 

@@ -35,6 +35,7 @@
 
 #include "exl3_common.cuh"
 #include "exl3_internal.h"
+#include "tc_gemm.h"
 
 namespace exl3 {
 
@@ -66,6 +67,11 @@ struct WsPtrs {
     float* part2;
     int* cnt1;
     int* cnt2;
+    int* ntiles128;
+    int4* tiles128;  // {expert, first sorted row, rows <= 128, 0}: the GEMM path's work tiles
+    float* g;
+    float* u;
+    __half* x2;
 };
 
 static WsPtrs ws_ptrs(const MoePlan& p, void* ws) {
@@ -86,6 +92,11 @@ static WsPtrs ws_ptrs(const MoePlan& p, void* ws) {
     w.part2 = reinterpret_cast<float*>(b + p.off_part2);
     w.cnt1 = reinterpret_cast<int*>(b + p.off_cnt1);
     w.cnt2 = reinterpret_cast<int*>(b + p.off_cnt2);
+    w.ntiles128 = reinterpret_cast<int*>(b + p.off_ntiles128);
+    w.tiles128 = reinterpret_cast<int4*>(b + p.off_tiles128);
+    w.g = reinterpret_cast<float*>(b + p.off_g);
+    w.u = reinterpret_cast<float*>(b + p.off_u);
+    w.x2 = reinterpret_cast<__half*>(b + p.off_x2);
     return w;
 }
 
@@ -169,19 +180,25 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
     // padded row offsets and slot offsets
     const int per = (E + kPrepThreads - 1) / kPrepThreads;
     const int e0 = min(E, tid * per), e1 = min(E, e0 + per);
-    int sp = 0, ss = 0;
+    int sp = 0, ss = 0, st = 0;
     for (int e = e0; e < e1; ++e) {
         sp += (cnt[e] + 15) & ~15;
         ss += (cnt[e] + 15) >> 4;
+        st += (cnt[e] + 127) >> 7;
     }
-    int tot_p, tot_s;
+    int tot_p, tot_s, tot_t;
     int xp = block_excl_scan(sp, &tot_p, sh32);
     int xs = block_excl_scan(ss, &tot_s, sh32);
+    int xt = block_excl_scan(st, &tot_t, sh32);
     for (int e = e0; e < e1; ++e) {
         const int n = cnt[e];
         poff[e] = xp;
         for (int j = 0; j < ((n + 15) >> 4); ++j)
             a.w.slots[xs + j] = make_int4(e, xp + 16 * j, min(16, n - 16 * j), 0);
+        if (a.w.tiles128)
+            for (int j = 0; j < ((n + 127) >> 7); ++j)
+                a.w.tiles128[xt + j] = make_int4(e, xp + 128 * j, min(128, n - 128 * j), 0);
+        xt += (n + 127) >> 7;
         for (int q = xp + n; q < xp + ((n + 15) & ~15); ++q) {
             a.w.sorted_tok[q] = -1;
             a.w.sorted_route[q] = -1;
@@ -191,7 +208,10 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
         xp += (n + 15) & ~15;
         xs += (n + 15) >> 4;
     }
-    if (tid == 0) *a.w.nslots = tot_s;
+    if (tid == 0) {
+        *a.w.nslots = tot_s;
+        if (a.w.ntiles128) *a.w.ntiles128 = tot_t;
+    }
     __syncthreads();
     for (int e = tid; e < E; e += kPrepThreads) cnt[e] = poff[e];  // running position (general path)
     __syncthreads();
@@ -271,21 +291,9 @@ struct RotArgs {
     int64_t rpad;
     int* status;
     int prerotated;  // x already rotated (fp16): copy into the padded layout only
+    int rowmajor;    // GEMM path: [proj][row][in] fp16, no padding
 };
 
-__device__ __forceinline__ const __half* proj_suh(const ProjRef& p, int e) {
-    return p.suh_tbl ? reinterpret_cast<const __half*>(p.suh_tbl[e]) : static_cast<const __half*>(p.suh);
-}
-__device__ __forceinline__ const __half* proj_svh(const ProjRef& p, int e) {
-    return p.svh_tbl ? reinterpret_cast<const __half*>(p.svh_tbl[e]) : static_cast<const __half*>(p.svh);
-}
-__device__ __forceinline__ const uint16_t* proj_trellis(const ProjRef& p, int e) {
-    return p.trellis_tbl ? reinterpret_cast<const uint16_t*>(p.trellis_tbl[e])
-                         : static_cast<const uint16_t*>(p.trellis);
-}
-__device__ __forceinline__ int proj_k(const ProjRef& p, int e) {
-    return p.k_tbl ? int(p.k_tbl[e]) : p.k_uniform;
-}
 
 __global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a) {
     // one warp per (sorted row, projection, 128-block)
@@ -317,7 +325,8 @@ __global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a) {
             const float xv = __half2float(__float2half_rn(load_as_float(a.x, int64_t(tok) * a.in_f + c, a.x_dtype)));
             v[i] = a.prerotated ? xv : xv * __half2float(suh[c]);
         }
-        __half* dst = a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * kXPitch;
+        __half* dst = a.rowmajor ? a.xr + (int64_t(pj) * a.rpad + p) * a.in_f + kb * 128
+                                 : a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * kXPitch;
         if (!a.prerotated) {
             fwht128_warp(v, lane);
             #pragma unroll
@@ -812,7 +821,7 @@ static void pick_split(int64_t groups_est, int grid, int nkt, int& nsplit, int& 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_local, int kmax,
-              bool linear, int num_sms) {
+              bool linear, int num_sms, bool allow_gemm) {
     if (t_max < 1 || topk < 1 || hidden < 128 || hidden % 128 || n_local < 1 || n_local > kMaxLocal)
         return false;
     if (inter < 128 || inter % 128) return false;
@@ -842,6 +851,12 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
         pick_split(act_max * p.ncb2, grid, inter / 16, p.nsplit2, p.ktps2);
     }
 
+    // prefill-sized batches (>= 32 rows per active expert on average) take the
+    // tcgen05 GEMM path, which decodes each weight tile once per 128 rows
+    p.gemm = allow_gemm && p.routes >= 32 * act_max;
+    p.t128max = p.routes / 128 + act_max + 1;
+    tc_pick_stages(kmax, p.tc_stages, p.tc_smem);
+
     size_t o = 0;
     auto take = [&](size_t bytes) {
         const size_t at = o;
@@ -857,13 +872,27 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     p.off_sorted_exp = take(size_t(p.rpad) * 4);
     p.off_sorted_w = take(size_t(p.rpad) * 4);
     const int nproj1 = linear ? 1 : 2;
-    p.off_xr = take(size_t(nproj1) * (hidden / 128) * p.rpad * kXPitch * 2);
-    p.off_a2 = take(linear ? 0 : size_t(inter / 128) * p.rpad * kXPitch * 2);
-    p.off_yd = take(linear ? 0 : size_t(p.rpad) * hidden * 4);
-    p.off_part1 = take(p.nsplit1 > 1 ? size_t(p.smax) * p.ncb1 * p.nsplit1 * kCW * nproj1 * 256 * 4 : 0);
-    p.off_part2 = take(!linear && p.nsplit2 > 1 ? size_t(p.smax) * p.ncb2 * p.nsplit2 * kCW * 256 * 4 : 0);
-    p.off_cnt1 = take(size_t(p.smax) * p.ncb1 * 4);
-    p.off_cnt2 = take(linear ? 0 : size_t(p.smax) * p.ncb2 * 4);
+    p.off_ntiles128 = take(p.gemm ? 64 : 0);
+    p.off_tiles128 = take(p.gemm ? size_t(p.t128max) * 16 : 0);
+    if (p.gemm) {
+        p.off_xr = take(size_t(nproj1) * p.rpad * hidden * 2);
+        p.off_g = take(linear ? 0 : size_t(p.rpad) * inter * 4);
+        p.off_u = take(linear ? 0 : size_t(p.rpad) * inter * 4);
+        p.off_x2 = take(linear ? 0 : size_t(p.rpad) * inter * 2);
+        p.off_yd = take(linear ? 0 : size_t(p.rpad) * hidden * 4);
+        p.off_a2 = p.off_part1 = p.off_part2 = take(0);
+        p.off_cnt1 = p.off_cnt2 = take(0);
+        p.nsplit1 = p.nsplit2 = 1;
+    } else {
+        p.off_xr = take(size_t(nproj1) * (hidden / 128) * p.rpad * kXPitch * 2);
+        p.off_a2 = take(linear ? 0 : size_t(inter / 128) * p.rpad * kXPitch * 2);
+        p.off_yd = take(linear ? 0 : size_t(p.rpad) * hidden * 4);
+        p.off_part1 = take(p.nsplit1 > 1 ? size_t(p.smax) * p.ncb1 * p.nsplit1 * kCW * nproj1 * 256 * 4 : 0);
+        p.off_part2 = take(!linear && p.nsplit2 > 1 ? size_t(p.smax) * p.ncb2 * p.nsplit2 * kCW * 256 * 4 : 0);
+        p.off_cnt1 = take(size_t(p.smax) * p.ncb1 * 4);
+        p.off_cnt2 = take(linear ? 0 : size_t(p.smax) * p.ncb2 * 4);
+        p.off_g = p.off_u = p.off_x2 = take(0);
+    }
     p.total = o;
     return true;
 }
@@ -933,8 +962,82 @@ int profile_read(float* ms, int max_phases) {
     return n;
 }
 
+// prefill path: tcgen05 grouped GEMM (tc_gemm.cu) over 128-row expert tiles
+static cudaError_t run_moe_gemm(const MoePlan& p, const MoeCall& c, const WsPtrs& w, int nsm, cudaStream_t s) {
+    TcArgs t{};
+    t.status = w.status;
+    t.kmax = p.kmax;
+    t.stages = p.tc_stages;
+    t.ntiles = w.ntiles128;
+    t.tiles = w.tiles128;
+    t.sorted_w = w.sorted_w;
+    t.sorted_tok = w.sorted_tok;
+    t.scatter_idx = c.scatter_idx;
+    t.scatter_w = static_cast<const __half*>(c.scatter_w);
+    cudaError_t e;
+    if (p.linear) {
+        if (c.batched) return cudaErrorNotSupported;  // callers route batched linears to the GEMV path
+        t.proj = c.up;
+        t.in_f = p.hidden;
+        t.out_f = p.inter;
+        t.ncb = p.inter / 128;
+        t.epi = TC_EPI_LINEAR;
+        t.y = c.out;
+        t.y_dtype = c.out_dtype;
+        e = run_tc_gemm(c.cb, t, w.xr, p.rpad, p.t128max * t.ncb, p.tc_smem, s);
+        prof_mark(s);
+        return e;
+    }
+    // gate and up rows (fp32, after the output rotation o svh)
+    t.in_f = p.hidden;
+    t.out_f = p.inter;
+    t.ncb = p.inter / 128;
+    t.epi = TC_EPI_ROWS;
+    t.proj = c.gate;
+    t.yrows = w.g;
+    if ((e = run_tc_gemm(c.cb, t, w.xr, p.rpad, p.t128max * t.ncb, p.tc_smem, s)) != cudaSuccess) return e;
+    t.proj = c.up;
+    t.yrows = w.u;
+    if ((e = run_tc_gemm(c.cb, t, w.xr + size_t(p.rpad) * p.hidden, p.rpad, p.t128max * t.ncb, p.tc_smem, s)) !=
+        cudaSuccess)
+        return e;
+    prof_mark(s);
+    ActArgs aa{};
+    aa.g = w.g;
+    aa.u = w.u;
+    aa.x2 = w.x2;
+    aa.down = c.down;
+    aa.ntiles = w.ntiles128;
+    aa.tiles = w.tiles128;
+    aa.inter = p.inter;
+    aa.limit = c.limit;
+    aa.act = c.act;
+    aa.status = w.status;
+    if ((e = run_tc_act(aa, nsm * 8, s)) != cudaSuccess) return e;
+    prof_mark(s);
+    t.proj = c.down;
+    t.in_f = p.inter;
+    t.out_f = p.hidden;
+    t.ncb = p.hidden / 128;
+    t.epi = TC_EPI_DOWN;
+    t.yrows = w.yd;
+    if ((e = run_tc_gemm(c.cb, t, w.x2, p.rpad, p.t128max * t.ncb, p.tc_smem, s)) != cudaSuccess) return e;
+    prof_mark(s);
+    const int64_t total = p.t_max * (p.hidden / 4);
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, int64_t(nsm) * 16);
+    combine_kernel<<<unsigned(std::max<int64_t>(blocks, 1)), 256, 0, s>>>(
+        w.route_pos, w.yd, p.t_max, p.topk, p.hidden, c.n_valid, c.out, c.out_dtype);
+    e = cudaGetLastError();
+    prof_mark(s);
+    return e;
+}
+
 cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s) {
-    const WsPtrs w = ws_ptrs(p, ws);
+    WsPtrs w = ws_ptrs(p, ws);
+    if (!p.gemm) {
+        w.ntiles128 = nullptr;
+        w.tiles128 = nullptr;
+    }
     const int nsm = std::max(1, p.grid1 / kCtasPerSm);
 
     PrepArgs pa;
@@ -950,8 +1053,8 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     pa.n_local = p.n_local;
     pa.linear = (p.linear && !c.batched) ? 1 : 0;
     pa.batched = c.batched ? 1 : 0;
-    pa.cnt1_n = int(p.smax * p.ncb1);
-    pa.cnt2_n = p.linear ? 0 : int(p.smax * p.ncb2);
+    pa.cnt1_n = p.gemm ? 0 : int(p.smax * p.ncb1);
+    pa.cnt2_n = (p.linear || p.gemm) ? 0 : int(p.smax * p.ncb2);
     pa.w = w;
     prof_begin(s);
     prep_kernel<<<1, kPrepThreads, 0, s>>>(pa);
@@ -973,9 +1076,11 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     ra.rpad = p.rpad;
     ra.status = w.status;
     ra.prerotated = c.prerotated ? 1 : 0;
+    ra.rowmajor = p.gemm ? 1 : 0;
     rotate_kernel<<<nsm * 8, 256, 0, s>>>(ra);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     prof_mark(s);
+    if (p.gemm) return run_moe_gemm(p, c, w, nsm, s);
 
     GemvArgs g;
     g.status = w.status;

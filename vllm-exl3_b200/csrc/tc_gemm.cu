@@ -1,0 +1,346 @@
+// tc_gemm.cu -- routed grouped GEMM for prefill-sized batches on sm_100a:
+// tcgen05 tensor cores with TMEM accumulators, TMA-fed activations and
+// weights decoded from the trellis into shared memory.
+//
+// Replaces the reference's prefill tiers: ExLlamaV3 exl3_moe / exl3_moe_mixedk
+// (expert-batched, src/vllm_exl3/exl3.py:3275-3579) and the fat-expert tier
+// exl3_fat_gemm(_scatter) (csrc/exl3_fat_gemm.cu:65-305: 128x128 mma.sync
+// tiles, K4 MCG only).
+//
+// One CTA computes one 128-row x 128-column output tile of one expert
+// (rows = that expert's routes, sorted and padded by the prep kernel; columns =
+// one 128-point Hadamard block), looping over K in stages of 64:
+//   warp 0   producer: TMA 2-D load of the 128x64 activation tile (128-byte
+//            swizzle) + 1-D bulk copy of the 4 k-tile rows of compressed trellis
+//   warp 1   TMEM allocator and the single MMA-issuing thread:
+//            tcgen05.mma kind::f16 M128 N128 K16 x4 per stage, fp32 in TMEM;
+//            tcgen05.commit frees the stage
+//   warps 2-9 decoders: each decodes its 16-column slice of the stage's 4 x 8
+//            tiles in registers and stores fp16 pairs straight into the
+//            K-major 128-byte-swizzled layout UMMA reads (conflict-free)
+//   warps 2-5 epilogue: tcgen05.ld one accumulator row per thread, in-thread
+//            128-point FWHT, * 1/sqrt128 * svh, store (fp32 rows, * route
+//            weight, or the caller's dtype / scatter)
+// Every mbarrier wait is bounded; no multicast anywhere.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "exl3_common.cuh"
+#include "exl3_internal.h"
+#include "tc_common.cuh"
+#include "tc_gemm.h"
+
+namespace exl3 {
+
+constexpr int kTcThreads = 320;
+constexpr int kTcM = 128, kTcN = 128, kTcK = 64;
+constexpr int kTcKt = kTcK / 16;            // k-tiles per stage
+constexpr int kTcABytes = kTcM * kTcK * 2;  // 16 KB
+constexpr int kTcBBytes = kTcN * kTcK * 2;  // 16 KB
+
+__host__ __device__ inline size_t tc_raw_bytes(int kmax) { return size_t(kTcKt) * 256 * kmax; }
+__host__ __device__ inline size_t tc_stage_bytes(int kmax) {
+    return (size_t(kTcABytes + kTcBBytes) + tc_raw_bytes(kmax) + 1023) & ~size_t(1023);
+}
+
+template <int K, int CB>
+__device__ __forceinline__ void tc_decode_slice(const char* raw, char* bsm, int d, int lane) {
+    // k-tiles kk of this stage, 16-column tile d: values j of lane l sit at
+    // n = 16d + l/4 (+8 for j >= 4), k = 16kk + 2(l%4) (+1 for odd j, +8 for j&2)
+    const int g = lane >> 2, t = lane & 3;
+    #pragma unroll
+    for (int kk = 0; kk < kTcKt; ++kk) {
+        const uint32_t* tile = reinterpret_cast<const uint32_t*>(raw) + (kk * 8 + d) * (8 * K);
+        uint32_t v[4];
+        decode_tile_pairs<K, CB>(tile, lane, v);
+        const int n0 = 16 * d + g, k0 = 16 * kk + 2 * t;
+        *reinterpret_cast<uint32_t*>(bsm + sw128_offset(n0, k0)) = v[0];
+        *reinterpret_cast<uint32_t*>(bsm + sw128_offset(n0, k0 + 8)) = v[1];
+        *reinterpret_cast<uint32_t*>(bsm + sw128_offset(n0 + 8, k0)) = v[2];
+        *reinterpret_cast<uint32_t*>(bsm + sw128_offset(n0 + 8, k0 + 8)) = v[3];
+    }
+}
+
+template <int CB>
+__device__ __forceinline__ void tc_decode_slice_k(int K, const char* raw, char* bsm, int d, int lane) {
+    switch (K) {
+        case 2: tc_decode_slice<2, CB>(raw, bsm, d, lane); break;
+        case 3: tc_decode_slice<3, CB>(raw, bsm, d, lane); break;
+        case 4: tc_decode_slice<4, CB>(raw, bsm, d, lane); break;
+        case 5: tc_decode_slice<5, CB>(raw, bsm, d, lane); break;
+        case 6: tc_decode_slice<6, CB>(raw, bsm, d, lane); break;
+        case 7: tc_decode_slice<7, CB>(raw, bsm, d, lane); break;
+        case 8: tc_decode_slice<8, CB>(raw, bsm, d, lane); break;
+        default: break;
+    }
+}
+
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* status, volatile int* abort_flag) {
+    if (*abort_flag) return false;
+    if (mbar_wait(bar, parity, status)) return true;
+    *abort_flag = 1;
+    return false;
+}
+
+template <int CB>
+__global__ void __launch_bounds__(kTcThreads, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ TcArgs a) {
+    extern __shared__ __align__(1024) char tc_smem_raw[];
+    char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    const int S = a.stages;
+    const size_t stage_bytes = tc_stage_bytes(a.kmax);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(S) * stage_bytes);
+    uint64_t* dec = full + S;
+    uint64_t* empty = dec + S;
+    uint64_t* accf = empty + S;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int64_t n_items = int64_t(*a.ntiles) * a.ncb;
+    const int64_t item = blockIdx.x;
+    if (item >= n_items) return;  // whole CTA, before any barrier
+    const int4 T = a.tiles[item / a.ncb];
+    const int cb = int(item % a.ncb);
+    const int e = T.x, p0 = T.y, rows = T.z;
+    const int K = proj_k(a.proj, e);
+    const uint16_t* trellis = proj_trellis(a.proj, e);
+    const bool ok = K >= 2 && K <= a.kmax && trellis != nullptr && (reinterpret_cast<uintptr_t>(trellis) & 15) == 0;
+    const int nst = a.in_f / kTcK;
+    const int ntiles_out = a.out_f / 16;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&dec[s], 8);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accf, 1);
+        *abort_flag = 0;
+        if (!ok) set_status(a.status, K < 2 || K > a.kmax ? DEV_BAD_K : (trellis ? DEV_BAD_ALIGN : DEV_NULL_PTR));
+        mbar_fence_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, kTcN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t taddr = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int ks = 0; ks < nst; ++ks) {
+                const int s = ks % S;
+                const uint32_t ph = uint32_t(ks / S) & 1u;
+                if (!tc_wait(&empty[s], ph ^ 1u, a.status, abort_flag)) break;
+                char* st = smem + size_t(s) * stage_bytes;
+                const uint32_t rawb = ok ? uint32_t(kTcKt * 256 * K) : 0u;
+                mbar_arrive_expect_tx(&full[s], uint32_t(kTcABytes) + rawb);
+                tma_load_2d(st, &amap, ks * kTcK, p0, &full[s]);
+                if (ok) {
+                    const int tw = 16 * K;
+                    for (int kk = 0; kk < kTcKt; ++kk) {
+                        const uint16_t* src =
+                            trellis + (int64_t(ks * kTcKt + kk) * ntiles_out + int64_t(cb) * 8) * tw;
+                        bulk_g2s(st + kTcABytes + kTcBBytes + size_t(kk) * 256 * K, src, uint32_t(256 * K), &full[s]);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_f16_f32(kTcM, kTcN);
+            for (int ks = 0; ks < nst; ++ks) {
+                const int s = ks % S;
+                const uint32_t ph = uint32_t(ks / S) & 1u;
+                if (!tc_wait(&full[s], ph, a.status, abort_flag)) break;
+                if (!tc_wait(&dec[s], ph, a.status, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t abase = smem_u32(smem + size_t(s) * stage_bytes);
+                const uint32_t bbase = abase + kTcABytes;
+                #pragma unroll
+                for (int k4 = 0; k4 < kTcK / 16; ++k4) {
+                    umma_f16(taddr, umma_desc_k_sw128(abase + 32 * k4), umma_desc_k_sw128(bbase + 32 * k4), idesc,
+                             (ks | k4) != 0);
+                }
+                umma_commit(&empty[s]);
+            }
+            umma_commit(accf);  // also covers the no-MMA case: arrives at once
+        }
+    } else {
+        const int d = warp - 2;  // 16-column tile of the 128-column block
+        for (int ks = 0; ks < nst; ++ks) {
+            const int s = ks % S;
+            const uint32_t ph = uint32_t(ks / S) & 1u;
+            const bool landed = tc_wait(&full[s], ph, a.status, abort_flag);
+            char* st = smem + size_t(s) * stage_bytes;
+            char* bsm = st + kTcABytes;
+            if (landed && ok) {
+                tc_decode_slice_k<CB>(K, st + kTcABytes + kTcBBytes, bsm, d, lane);
+            } else {
+                // zero weights: the MMA then adds nothing for this stage
+                for (int i = lane; i < 16 * kTcK / 2; i += 32) {
+                    const int n = 16 * d + i / (kTcK / 2), k = 2 * (i % (kTcK / 2));
+                    *reinterpret_cast<uint32_t*>(bsm + sw128_offset(n, k)) = 0u;
+                }
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&dec[s]);
+        }
+
+        if (warp < 6) {
+            // ---------------------------- epilogue ----------------------------
+            // on an abort still wait (bounded) for issued MMAs before TMEM is read or freed
+            if (!tc_wait(accf, 0u, a.status, abort_flag)) mbar_wait(accf, 0u, a.status);
+            tc_fence_after();
+            const int q = warp & 3;  // TMEM lane quarter this warp may access
+            const int row = 32 * q + lane;
+            float v[128];
+            #pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) {
+                float part[32];
+                tmem_ld32(taddr + (uint32_t(32 * q) << 16) + uint32_t(32 * c4), part);
+                #pragma unroll
+                for (int i = 0; i < 32; ++i) v[32 * c4 + i] = part[i];
+            }
+            fwht128_thread(v);
+            if (row < rows) {
+                const int64_t p = p0 + row;
+                const __half* svh = proj_svh(a.proj, e) + cb * 128;
+                float wmul = 1.f;
+                if (a.epi == TC_EPI_DOWN) wmul = a.sorted_w[p];
+                #pragma unroll
+                for (int c = 0; c < 128; ++c) v[c] = v[c] * kHadNorm * __half2float(svh[c]) * wmul;
+                if (a.epi == TC_EPI_LINEAR) {
+                    const int tok = a.sorted_tok[p];
+                    if (tok >= 0) {
+                        if (a.scatter_idx) {
+                            float* dst = static_cast<float*>(a.y) + a.scatter_idx[tok] * a.out_f + cb * 128;
+                            const float w = __half2float(a.scatter_w[tok]);
+                            #pragma unroll
+                            for (int c = 0; c < 128; ++c) dst[c] += w * v[c];
+                        } else {
+                            #pragma unroll
+                            for (int c = 0; c < 128; ++c)
+                                store_from_float(a.y, int64_t(tok) * a.out_f + cb * 128 + c, a.y_dtype, v[c]);
+                        }
+                    }
+                } else {
+                    float4* dst = reinterpret_cast<float4*>(a.yrows + p * a.out_f + cb * 128);
+                    #pragma unroll
+                    for (int c = 0; c < 32; ++c) dst[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+                }
+            }
+            tc_fence_before();
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(taddr, kTcN);
+    }
+}
+
+// gate/up rows -> SwiGLU (+clamp) -> fp16 -> o suh_down -> H128/sqrt128 ->
+// fp16 row-major down input; one warp per (tile row, 128-block)
+__global__ void __launch_bounds__(256) tc_act_kernel(const ActArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int nkb = a.inter / 128;
+    const int64_t total = int64_t(*a.ntiles) * 128 * nkb;
+    for (int64_t it = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; it < total;
+         it += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+        const int64_t t = it / (128 * nkb);
+        const int rem = int(it % (128 * nkb));
+        const int row = rem / nkb, kb = rem % nkb;
+        const int4 T = a.tiles[t];
+        if (row >= T.z) continue;
+        const int64_t p = T.y + row;
+        const __half* suh = reinterpret_cast<const __half*>(a.down.suh_tbl ? a.down.suh_tbl[T.x] : 0);
+        float x[4];
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int c = kb * 128 + lane + 32 * i;
+            float g = a.g[p * a.inter + c], u = a.u[p * a.inter + c];
+            if (a.limit > 0.f) {
+                g = fminf(g, a.limit);
+                u = fminf(fmaxf(u, -a.limit), a.limit);
+            }
+            float act;
+            if (a.act == 3) act = (u + 1.0f) * g / (1.0f + expf(-1.702f * g));
+            else act = g / (1.0f + expf(-g)) * u;
+            x[i] = __half2float(__float2half_rn(act)) * (suh ? __half2float(suh[c]) : 0.f);
+        }
+        fwht128_warp(x, lane);
+        #pragma unroll
+        for (int i = 0; i < 4; ++i)
+            a.x2[p * a.inter + kb * 128 + lane + 32 * i] = __float2half_rn(x[i] * kHadNorm);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// fp16 row-major [rows][cols] -> 128 x 64 boxes, 128-byte swizzle
+static cudaError_t make_act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+    const cuuint64_t strides[1] = {cuuint64_t(cols) * 2};
+    const cuuint32_t box[2] = {kTcK, kTcM};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+void tc_pick_stages(int kmax, int& stages, size_t& smem) {
+    const size_t budget = 227 * 1024 - 1024 /* alignment slack */ - 256 /* barriers */;
+    const size_t sb = tc_stage_bytes(kmax);
+    int s = int(std::min<size_t>(6, budget / sb));
+    if (s < 2) s = 2;
+    stages = s;
+    smem = size_t(s) * sb + 1024 + 256;
+}
+
+cudaError_t run_tc_gemm(int cb, const TcArgs& a, const void* act, int64_t act_rows, int64_t grid,
+                        size_t smem, cudaStream_t s) {
+    CUtensorMap map;
+    cudaError_t e = make_act_map(&map, act, act_rows, a.in_f);
+    if (e != cudaSuccess) return e;
+    void (*kern)(CUtensorMap, TcArgs);
+    if (cb == CB_MCG) kern = tc_gemm_kernel<CB_MCG>;
+    else if (cb == CB_MUL1) kern = tc_gemm_kernel<CB_MUL1>;
+    else kern = tc_gemm_kernel<CB_3INST>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    if (grid <= 0) return cudaSuccess;
+    kern<<<unsigned(grid), kTcThreads, smem, s>>>(map, a);
+    return cudaGetLastError();
+}
+
+cudaError_t run_tc_act(const ActArgs& a, int grid, cudaStream_t s) {
+    tc_act_kernel<<<grid, 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace exl3
