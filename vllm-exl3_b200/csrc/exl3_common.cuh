@@ -212,6 +212,29 @@ __device__ __forceinline__ void fwht128_warp(float (&v)[4], int lane) {
     }
 }
 
+// Same transform with element 4*lane + i in v[i] (contiguous lanes, for
+// vectorised row loads and stores).  Only the GEMV/GEMM activation paths use
+// it; the bit-exact reconstruction keeps fwht128_warp.
+__device__ __forceinline__ void fwht128_warp_contig(float (&v)[4], int lane) {
+    {
+        const float a0 = v[0], b0 = v[1], a1 = v[2], b1 = v[3];
+        v[0] = a0 + b0; v[1] = a0 - b0; v[2] = a1 + b1; v[3] = a1 - b1;
+    }
+    {
+        const float a0 = v[0], b0 = v[2], a1 = v[1], b1 = v[3];
+        v[0] = a0 + b0; v[2] = a0 - b0; v[1] = a1 + b1; v[3] = a1 - b1;
+    }
+    #pragma unroll
+    for (int s = 1; s < 32; s <<= 1) {
+        const bool upper = (lane & s) != 0;
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float p = __shfl_xor_sync(0xffffffffu, v[i], s);
+            v[i] = upper ? p - v[i] : v[i] + p;
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Tensor-core fragments (register-fed mma.sync; the operands are decoded in
 // registers, so no shared-memory round trip is needed for the weights).

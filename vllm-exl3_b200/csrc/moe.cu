@@ -209,7 +209,8 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
         xs += (n + 15) >> 4;
     }
     if (tid == 0) {
-        *a.w.nslots = tot_s;
+        a.w.nslots[0] = tot_s;
+        a.w.nslots[1] = tot_p;  // sorted rows in use (each expert padded to 16); rows past it are stale
         if (a.w.ntiles128) *a.w.ntiles128 = tot_t;
     }
     __syncthreads();
@@ -334,6 +335,50 @@ __global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a) {
         }
         #pragma unroll
         for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2half_rn(v[i]);
+    }
+}
+
+// GEMM path: one warp per (sorted row, projection), all 128-blocks of the row,
+// lanes holding 4 consecutive features; output fp16 row-major [proj][row][in].
+__global__ void __launch_bounds__(256) rotate_rows_kernel(const RotArgs a, const int* __restrict__ sorted_exp) {
+    const int lane = threadIdx.x & 31;
+    const int nkb = a.in_f / 128;
+    const int64_t total = min(int64_t(a.nslots[1]), int64_t(a.rpad)) * a.nproj;  // rows in use only
+    for (int64_t it = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; it < total;
+         it += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+        const int64_t p = it / a.nproj;
+        const int pj = int(it % a.nproj);
+        const int tok = a.sorted_tok[p];
+        if (tok < 0) continue;  // padding row
+        const __half* suh = a.prerotated ? nullptr : proj_suh(a.proj[pj], sorted_exp[p]);
+        if (suh == nullptr && !a.prerotated) {
+            if (lane == 0) set_status(a.status, DEV_NULL_PTR);
+            continue;
+        }
+        const int64_t xrow = int64_t(tok) * a.in_f;
+        __half* dst = a.xr + (int64_t(pj) * a.rpad + p) * a.in_f;
+        #pragma unroll 4
+        for (int kb = 0; kb < nkb; ++kb) {
+            const int c0 = kb * 128 + 4 * lane;
+            float v[4];
+            #pragma unroll
+            for (int i = 0; i < 4; ++i)
+                v[i] = __half2float(__float2half_rn(load_as_float(a.x, xrow + c0 + i, a.x_dtype)));
+            if (!a.prerotated) {
+                // suh comes from the caller's tables: only 2-byte alignment is guaranteed
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] *= __half2float(suh[c0 + i]);
+                fwht128_warp_contig(v, lane);
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] *= kHadNorm;
+            }
+            const __half2 h01 = __floats2half2_rn(v[0], v[1]);
+            const __half2 h23 = __floats2half2_rn(v[2], v[3]);
+            uint2 o;
+            o.x = *reinterpret_cast<const uint32_t*>(&h01);
+            o.y = *reinterpret_cast<const uint32_t*>(&h23);
+            *reinterpret_cast<uint2*>(dst + c0) = o;
+        }
     }
 }
 
@@ -1013,6 +1058,10 @@ static cudaError_t run_moe_gemm(const MoePlan& p, const MoeCall& c, const WsPtrs
     aa.limit = c.limit;
     aa.act = c.act;
     aa.status = w.status;
+    aa.rpad = p.rpad;
+    aa.nrows = w.nslots + 1;
+    aa.sorted_tok = w.sorted_tok;
+    aa.sorted_exp = w.sorted_exp;
     if ((e = run_tc_act(aa, nsm * 8, s)) != cudaSuccess) return e;
     prof_mark(s);
     t.proj = c.down;
@@ -1077,7 +1126,8 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     ra.status = w.status;
     ra.prerotated = c.prerotated ? 1 : 0;
     ra.rowmajor = p.gemm ? 1 : 0;
-    rotate_kernel<<<nsm * 8, 256, 0, s>>>(ra);
+    if (p.gemm) rotate_rows_kernel<<<nsm * 8, 256, 0, s>>>(ra, w.sorted_exp);
+    else rotate_kernel<<<nsm * 8, 256, 0, s>>>(ra);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     prof_mark(s);
     if (p.gemm) return run_moe_gemm(p, c, w, nsm, s);

@@ -18,10 +18,14 @@
 //   warps 2-9 decoders: each decodes its 16-column slice of the stage's 4 x 8
 //            tiles in registers and stores fp16 pairs straight into the
 //            K-major 128-byte-swizzled layout UMMA reads (conflict-free)
-//   warps 2-5 epilogue: tcgen05.ld one accumulator row per thread, in-thread
-//            128-point FWHT, * 1/sqrt128 * svh, store (fp32 rows, * route
-//            weight, or the caller's dtype / scatter)
-// Every mbarrier wait is bounded; no multicast anywhere.
+//   epilogue warps 2-5 move the accumulator (tcgen05.ld, one row per thread)
+//            into the now idle stage memory; warps 2-9 then run a warp-wide
+//            128-point FWHT per row, * 1/sqrt128 * svh, and store rows
+//            coalesced (fp32 rows, * route weight, or the caller's dtype /
+//            scatter)
+// Two CTAs per SM, so one CTA's prologue/epilogue overlaps the other's main
+// loop and 16 decoder warps share the SM.  Every mbarrier wait is bounded; no
+// multicast anywhere.
 #include <cuda.h>
 
 #include <algorithm>
@@ -84,8 +88,10 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* sta
     return false;
 }
 
+constexpr int kTcEpiPitch = 129;  // fp32 pitch of the epilogue tile (conflict-free row and column sweeps)
+
 template <int CB>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, 2)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ TcArgs a) {
     extern __shared__ __align__(1024) char tc_smem_raw[];
     char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -190,50 +196,58 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
             if (lane == 0) mbar_arrive(&dec[s]);
         }
 
+        // ---------------------------- epilogue ----------------------------
+        // the stage memory is free once every MMA has completed (accf)
+        float* ep = reinterpret_cast<float*>(smem);  // [128][kTcEpiPitch]
         if (warp < 6) {
-            // ---------------------------- epilogue ----------------------------
             // on an abort still wait (bounded) for issued MMAs before TMEM is read or freed
             if (!tc_wait(accf, 0u, a.status, abort_flag)) mbar_wait(accf, 0u, a.status);
             tc_fence_after();
             const int q = warp & 3;  // TMEM lane quarter this warp may access
             const int row = 32 * q + lane;
-            float v[128];
-            #pragma unroll
+            #pragma unroll 1
             for (int c4 = 0; c4 < 4; ++c4) {
                 float part[32];
                 tmem_ld32(taddr + (uint32_t(32 * q) << 16) + uint32_t(32 * c4), part);
                 #pragma unroll
-                for (int i = 0; i < 32; ++i) v[32 * c4 + i] = part[i];
-            }
-            fwht128_thread(v);
-            if (row < rows) {
-                const int64_t p = p0 + row;
-                const __half* svh = proj_svh(a.proj, e) + cb * 128;
-                float wmul = 1.f;
-                if (a.epi == TC_EPI_DOWN) wmul = a.sorted_w[p];
-                #pragma unroll
-                for (int c = 0; c < 128; ++c) v[c] = v[c] * kHadNorm * __half2float(svh[c]) * wmul;
-                if (a.epi == TC_EPI_LINEAR) {
-                    const int tok = a.sorted_tok[p];
-                    if (tok >= 0) {
-                        if (a.scatter_idx) {
-                            float* dst = static_cast<float*>(a.y) + a.scatter_idx[tok] * a.out_f + cb * 128;
-                            const float w = __half2float(a.scatter_w[tok]);
-                            #pragma unroll
-                            for (int c = 0; c < 128; ++c) dst[c] += w * v[c];
-                        } else {
-                            #pragma unroll
-                            for (int c = 0; c < 128; ++c)
-                                store_from_float(a.y, int64_t(tok) * a.out_f + cb * 128 + c, a.y_dtype, v[c]);
-                        }
-                    }
-                } else {
-                    float4* dst = reinterpret_cast<float4*>(a.yrows + p * a.out_f + cb * 128);
-                    #pragma unroll
-                    for (int c = 0; c < 32; ++c) dst[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-                }
+                for (int i = 0; i < 32; ++i) ep[row * kTcEpiPitch + 32 * c4 + i] = part[i];
             }
             tc_fence_before();
+        }
+        named_bar_sync(1, 8 * 32);
+        const __half* svh = proj_svh(a.proj, e) + cb * 128;
+        float sv[4];
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) sv[i] = __half2float(svh[lane + 32 * i]) * kHadNorm;
+        for (int r = d; r < rows; r += 8) {
+            float x[4];
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) x[i] = ep[r * kTcEpiPitch + lane + 32 * i];
+            fwht128_warp(x, lane);
+            const int64_t p = p0 + r;
+            float wmul = 1.f;
+            if (a.epi == TC_EPI_DOWN) wmul = a.sorted_w[p];
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) x[i] *= sv[i] * wmul;
+            if (a.epi == TC_EPI_LINEAR) {
+                const int tok = a.sorted_tok[p];
+                if (tok < 0) continue;
+                if (a.scatter_idx) {
+                    // one route per destination row per call: plain read-modify-write
+                    float* dst = static_cast<float*>(a.y) + a.scatter_idx[tok] * a.out_f + cb * 128;
+                    const float w = __half2float(a.scatter_w[tok]);
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] += w * x[i];
+                } else {
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        store_from_float(a.y, int64_t(tok) * a.out_f + cb * 128 + lane + 32 * i, a.y_dtype, x[i]);
+                }
+            } else {
+                float* dst = a.yrows + p * a.out_f + cb * 128;
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = x[i];
+            }
         }
     }
     __syncthreads();
@@ -246,36 +260,45 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
 // gate/up rows -> SwiGLU (+clamp) -> fp16 -> o suh_down -> H128/sqrt128 ->
 // fp16 row-major down input; one warp per (tile row, 128-block)
 __global__ void __launch_bounds__(256) tc_act_kernel(const ActArgs a) {
+    // one warp per sorted row, lanes holding 4 consecutive features
     const int lane = threadIdx.x & 31;
     const int nkb = a.inter / 128;
-    const int64_t total = int64_t(*a.ntiles) * 128 * nkb;
-    for (int64_t it = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; it < total;
-         it += (int64_t(gridDim.x) * blockDim.x) >> 5) {
-        const int64_t t = it / (128 * nkb);
-        const int rem = int(it % (128 * nkb));
-        const int row = rem / nkb, kb = rem % nkb;
-        const int4 T = a.tiles[t];
-        if (row >= T.z) continue;
-        const int64_t p = T.y + row;
-        const __half* suh = reinterpret_cast<const __half*>(a.down.suh_tbl ? a.down.suh_tbl[T.x] : 0);
-        float x[4];
-        #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int c = kb * 128 + lane + 32 * i;
-            float g = a.g[p * a.inter + c], u = a.u[p * a.inter + c];
-            if (a.limit > 0.f) {
-                g = fminf(g, a.limit);
-                u = fminf(fmaxf(u, -a.limit), a.limit);
+    const int64_t nrows = min(int64_t(*a.nrows), int64_t(a.rpad));  // rows past it are stale
+    for (int64_t p = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; p < nrows;
+         p += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+        if (a.sorted_tok[p] < 0) continue;  // padding row
+        const int64_t eid = a.sorted_exp[p];
+        const __half* suh = reinterpret_cast<const __half*>(a.down.suh_tbl ? a.down.suh_tbl[eid] : 0);
+        const float* gr = a.g + p * a.inter;
+        const float* ur = a.u + p * a.inter;
+        __half* dst = a.x2 + p * a.inter;
+        #pragma unroll 2
+        for (int kb = 0; kb < nkb; ++kb) {
+            const int c0 = kb * 128 + 4 * lane;
+            const float4 g4 = *reinterpret_cast<const float4*>(gr + c0);
+            const float4 u4 = *reinterpret_cast<const float4*>(ur + c0);
+            const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
+            float x[4];
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float g = gv[i], u = uv[i];
+                if (a.limit > 0.f) {
+                    g = fminf(g, a.limit);
+                    u = fminf(fmaxf(u, -a.limit), a.limit);
+                }
+                float act;
+                if (a.act == 3) act = (u + 1.0f) * g / (1.0f + expf(-1.702f * g));
+                else act = g / (1.0f + expf(-g)) * u;
+                x[i] = __half2float(__float2half_rn(act)) * (suh ? __half2float(suh[c0 + i]) : 0.f);
             }
-            float act;
-            if (a.act == 3) act = (u + 1.0f) * g / (1.0f + expf(-1.702f * g));
-            else act = g / (1.0f + expf(-g)) * u;
-            x[i] = __half2float(__float2half_rn(act)) * (suh ? __half2float(suh[c]) : 0.f);
+            fwht128_warp_contig(x, lane);
+            const __half2 h01 = __floats2half2_rn(x[0] * kHadNorm, x[1] * kHadNorm);
+            const __half2 h23 = __floats2half2_rn(x[2] * kHadNorm, x[3] * kHadNorm);
+            uint2 o;
+            o.x = *reinterpret_cast<const uint32_t*>(&h01);
+            o.y = *reinterpret_cast<const uint32_t*>(&h23);
+            *reinterpret_cast<uint2*>(dst + c0) = o;
         }
-        fwht128_warp(x, lane);
-        #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            a.x2[p * a.inter + kb * 128 + lane + 32 * i] = __float2half_rn(x[i] * kHadNorm);
     }
 }
 
@@ -314,10 +337,13 @@ static cudaError_t make_act_map(CUtensorMap* m, const void* base, int64_t rows, 
 }
 
 void tc_pick_stages(int kmax, int& stages, size_t& smem) {
-    const size_t budget = 227 * 1024 - 1024 /* alignment slack */ - 256 /* barriers */;
+    // two CTAs per SM; the epilogue tile [128][129] fp32 reuses the stages
+    const size_t budget = (228 * 1024) / 2 - 1024 /* per-CTA reserve */ - 1024 /* alignment */ - 256;
     const size_t sb = tc_stage_bytes(kmax);
     int s = int(std::min<size_t>(6, budget / sb));
     if (s < 2) s = 2;
+    const size_t epi = size_t(128) * kTcEpiPitch * 4;
+    if (size_t(s) * sb < epi) s = int((epi + sb - 1) / sb);
     stages = s;
     smem = size_t(s) * sb + 1024 + 256;
 }

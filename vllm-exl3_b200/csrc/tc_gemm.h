@@ -37,6 +37,10 @@ struct ActArgs {
     float limit;
     int act;
     int* status;
+    int64_t rpad;
+    const int* nrows;  // sorted rows in use (written by the prep kernel)
+    const int* sorted_tok;
+    const int* sorted_exp;
 };
 
 // act: fp16 row-major [act_rows][in_f] activations (TMA source); grid: upper
