@@ -17,8 +17,13 @@ layer, inputs resident in HBM).  `e2e` = the same metric through the public
 API (exl3_b200.moe.Exl3RoutedExperts.apply, eager) with pinned-host inputs
 copied in and the output copied back inside the timed region.
 
-N > 1: every rank runs its own replica of the layer (replicas; expert-parallel
-dispatch/combine is exl3_b200.ep).  --impl reference: rank 0 times the
+N > 1: expert parallelism (exl3_b200.ep): rank g holds experts
+[g*128/N, (g+1)*128/N) and T tokens of its own (weak scaling); a step is
+dispatch, NCCL all-to-all, the local fused forward, all-to-all back and the
+per-token combine, timed per step and taken as the max over ranks.
+--workload ep: configs[4] (256 experts, H7168 I2048, 8192 tokens split over
+the ranks: strong scaling), same EP step at any N.  --workload prefill:
+configs[2] on one GPU (tcgen05 grouped GEMM path).  --impl reference: rank 0 times the
 reference's CPU path (dequant_trellis compiled from the reference's own
 csrc/bindings.cpp, oracle/_ref; else the oracle port) on a bounded sample of
 each step's experts, scaled to the step.
@@ -51,6 +56,9 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep"],
+                    help="decode = configs[1] (the default, reported line); prefill = configs[2]; "
+                         "ep = configs[4]")
     return ap.parse_args()
 
 
@@ -399,6 +407,296 @@ def run_b200(args, rank, local_rank, world):
     return result
 
 
+PREFILL = {
+    # GLM-class mixed-K prefill, mul1, K in {2,3}
+    "prefill": dict(cfg="cfg3", E=160, topk=8, H=5120, I=1536, tokens=2048,
+                    name="configs[2] mixed-K prefill: 160 experts top-8, H5120 I1536, K2/3 mul1"),
+}
+
+# expert-parallel workloads: experts sharded evenly over the ranks, NCCL
+# all-to-all dispatch/combine (exl3_b200.ep, fixed-capacity exchange)
+EP_WORKLOADS = {
+    # configs[1] decode layer at N > 1: T tokens per rank (weak scaling)
+    "decode": dict(E=128, topk=8, H=2048, I=768, cb=1, k=(4,), kp=None, router="softmax", sigma=1.0,
+                   name="configs[1] decode layer, 128 experts top-8, H2048 I768, K4 MCG, expert-parallel"),
+    # 8192 tokens split over the ranks (strong scaling)
+    "ep": dict(E=256, topk=8, H=7168, I=2048, cb=1, k=(2, 3, 4), kp=(0.3, 0.5, 0.2), router="sigmoid_zipf",
+               tokens=8192, name="configs[4] EP layer: 256 experts top-8 sigmoid+Zipf, H7168 I2048, K2/3/4 MCG"),
+}
+
+
+def run_ep(args, rank, local_rank, world, which):
+    """One expert-parallel layer step per rank: dispatch, all-to-all, local
+    fused forward, all-to-all back, combine (fixed-capacity exchange, no host
+    synchronisation inside a step)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from exl3_b200 import _native, moe, synthetic
+    from exl3_b200.ep import Exl3ExpertParallel
+
+    c = EP_WORKLOADS[which]
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    E_, H_, I_, k = c["E"], c["H"], c["I"], c["topk"]
+    if which == "decode":
+        Tr, scaling = args.tokens, "weak"
+        Tt = Tr * world
+    else:
+        Tt = c["tokens"] if args.tokens == 64 else args.tokens
+        Tr, scaling = Tt // world, "strong"
+    epr = E_ // world
+    lo, hi = rank * epr, (rank + 1) * epr
+    pack = synthetic.make_moe_pack_slice(0, E_, H_, I_, c["cb"], c["k"], c["kp"], lo, hi)
+    kbits = [e["gate"].K for e in pack.experts]
+    layer = moe.layer_from_pack(pack, dev)
+    del pack
+    ep = Exl3ExpertParallel(layer, E_, combine_dtype=torch.bfloat16, capacity=Tr)
+    NB = 4 if which == "decode" else 2
+    batches, local_routes, local_experts = [], [], []
+    for b in range(NB):
+        rng = np.random.default_rng([900 + b])  # routing of all tokens: identical on every rank
+        if c["router"] == "softmax":
+            ids, w = synthetic.softmax_topk(rng, Tt, E_, k, c["sigma"])
+        else:
+            ids, w = synthetic.sigmoid_zipf_topk(rng, Tt, E_, k)
+        mine = (ids >= lo) & (ids < hi)
+        local_routes.append(int(mine.sum()))
+        local_experts.append(len(np.unique(ids[mine])))
+        x = synthetic.activations(np.random.default_rng([900 + b, rank]), Tr, H_)
+        sl = slice(rank * Tr, (rank + 1) * Tr)
+        batches.append((torch.from_numpy(x).to(torch.bfloat16).to(dev), torch.from_numpy(ids[sl]).to(dev),
+                        torch.from_numpy(w[sl]).to(dev)))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = torch.empty(Tr, H_, dtype=torch.bfloat16, device=dev)
+
+    def step(i):
+        x, ids, w = batches[i % NB]
+        ep(x, w, ids, out=out)
+
+    def timed(n):
+        evs = []
+        for i in range(n):
+            flush.zero_()
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record()
+            step(i)
+            a1.record()
+            evs.append((a0, a1))
+        return evs
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    timed(args.warmup)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local_rank) as clk:
+        evs = timed(args.steps)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    total_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs))
+    step_s = total_ms / args.steps / 1e3
+
+    # per-phase times: the EP step (CUDA events between phases) and, inside
+    # the local forward, the library's kernel phases
+    ep.profile = True
+    ep_ph = []
+    for i in range(4):
+        step(i)
+        ep_ph.append(ep.phase_ms())
+    ep.profile = False
+    _native.profile_enable(True, 2_000_000)
+    loc = []
+    for i in range(4):
+        step(i)
+        torch.cuda.synchronize(dev)
+        loc.append(_native.profile_read())
+    _native.profile_enable(False)
+    eph = {n: statistics.median(p[n] for p in ep_ph[1:]) * 1e3 for n in ep.PHASES}
+    nloc = len(loc[0])
+    names = ["prep", "rotate", "gate_up", "act", "down", "combine"] if nloc == 6 else \
+        ["prep", "rotate", "gate_up", "down", "combine"]
+    lph = {n: statistics.median(p[j] for p in loc[1:]) * 1e3 for j, n in enumerate(names)}
+
+    peak_b, kind_b = peaks()
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tpk, kind_t = float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        tpk, kind_t = 1590.0, "fallback"
+    gu_s = lph["gate_up"] / 1e6
+    routes = float(np.mean(local_routes))
+    if which == "ep":
+        flops = routes * 4.0 * H_ * I_
+        roof = {"kernel": "tc_gemm_kernel x2 (gate, up) of the local forward, rank %d" % rank,
+                "bound": "tensor", "unit": "TFLOP/s", "achieved": flops / gu_s / 1e12, "peak": tpk,
+                "peak_kind": kind_t, "frac": flops / gu_s / 1e12 / tpk, "flops_per_launch": flops,
+                "us_per_launch": lph["gate_up"], "traffic": None}
+    else:
+        kb = float(np.mean(kbits))
+        per_e = 2 * (H_ // 16) * (I_ // 16) * kb * 32 + 2 * (H_ + I_) * 2
+        byts = float(np.mean(local_experts)) * per_e + routes * 2 * H_ * 2
+        roof = {"kernel": "gate+up phase of the local forward, rank %d" % rank, "bound": "hbm", "unit": "GB/s",
+                "achieved": byts / gu_s / 1e9, "peak": peak_b, "peak_kind": kind_b,
+                "frac": byts / gu_s / 1e9 / peak_b, "bytes_per_launch": byts, "us_per_launch": lph["gate_up"],
+                "traffic": None}
+
+    # e2e through the public API with pinned host buffers
+    hb = [tuple(t.cpu().pin_memory() for t in b) for b in batches]
+    hout = torch.empty(Tr, H_, dtype=torch.bfloat16).pin_memory()
+
+    def e2e(n):
+        evs = []
+        for i in range(n):
+            flush.zero_()
+            hx, hid, hw = hb[i % NB]
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record()
+            y = ep(hx.to(dev, non_blocking=True), hw.to(dev, non_blocking=True), hid.to(dev, non_blocking=True))
+            hout.copy_(y, non_blocking=True)
+            a1.record()
+            evs.append((a0, a1))
+        return evs
+
+    e2e(max(1, args.warmup))
+    torch.cuda.synchronize(dev)
+    evs = e2e(args.steps)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs))
+    launches = 2 + nloc + 1
+    return {
+        "metric": METRIC if which == "decode" else f"MoE layer prefill tokens/s ({c['name']})",
+        "value": Tt * args.steps / (total_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": scaling, "vs_baseline": None,
+        "dtype": "fp16 MMA, fp32 accumulate (int trellis decode); bf16 exchange", "data": "synthetic",
+        "config": {"workload": f"{c['name']}, T={Tt} tokens/step ({Tr} per rank)", "experts": E_,
+                   "experts_per_rank": epr, "topk": k, "hidden": H_, "intermediate": I_,
+                   "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single, fixed capacity %d rows/rank" % Tr,
+                   "l2": "256 MB L2 flush before every step (untimed)",
+                   "timing": "CUDA events per step around the eager EP step, max over ranks"},
+        "us_per_layer": step_s * 1e6, "phases_us": {"ep": eph, "local": lph}, "roofline": roof,
+        "local_routes_per_rank": routes,
+        "e2e": {"value": Tt * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": Tr * H_ * 2 + Tr * k * 8 + Tr * k * 4, "d2h_bytes_per_step": Tr * H_ * 2,
+                "us_per_step": e2e_ms / args.steps * 1e3},
+        "gpu_launches": launches * args.steps, "clocks": clk.summary(),
+    }
+
+
+def run_prefill(args, rank, local_rank, world):
+    """Tensor-bound workloads (tcgen05 grouped GEMM path); single GPU."""
+    import numpy as np
+    import torch
+    from exl3_b200 import _native, moe, synthetic
+
+    w = PREFILL[args.workload]
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    T = args.tokens if args.tokens != 64 else w["tokens"]
+    pack, x, ids, wt = synthetic.make_config(w["cfg"], seed=0, tokens=T)
+    layer = moe.layer_from_pack(pack, dev)
+    NB = 2
+    batches = [(torch.from_numpy(x).to(dev).to(torch.bfloat16), torch.from_numpy(ids).to(dev),
+                torch.from_numpy(wt).to(dev))]
+    rng = np.random.default_rng(1234)
+    x2 = synthetic.activations(rng, T, w["H"])
+    if w["cfg"] == "cfg5":
+        ids2, w2 = synthetic.sigmoid_zipf_topk(rng, T, w["E"], w["topk"])
+    else:
+        ids2, w2 = synthetic.softmax_topk(rng, T, w["E"], w["topk"], 1.5)
+    batches.append((torch.from_numpy(x2).to(dev).to(torch.bfloat16), torch.from_numpy(ids2).to(dev),
+                    torch.from_numpy(w2).to(dev)))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    sx, sid, sw = (t.clone() for t in batches[0])
+    out = torch.empty(T, w["H"], dtype=torch.bfloat16, device=dev)
+
+    def fwd():
+        layer.apply(sx, sw, sid, out=out)
+
+    def load(b):
+        sx.copy_(batches[b % NB][0])
+        sid.copy_(batches[b % NB][1])
+        sw.copy_(batches[b % NB][2])
+
+    st = torch.cuda.Stream(dev)
+    st.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(st):
+        for _ in range(2):
+            fwd()
+    torch.cuda.current_stream(dev).wait_stream(st)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fwd()
+
+    def timed(n):
+        evs = []
+        for i in range(n):
+            flush.zero_()
+            load(i)
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record()
+            graph.replay()
+            a1.record()
+            evs.append((a0, a1))
+        return evs
+
+    timed(args.warmup)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local_rank) as clk:
+        evs = timed(args.steps)
+        torch.cuda.synchronize(dev)
+    total_ms = sum(a.elapsed_time(b) for a, b in evs)
+
+    _native.profile_enable(True, 2_000_000)
+    phases = []
+    for i in range(4):
+        load(i)
+        fwd()
+        phases.append(_native.profile_read())
+    _native.profile_enable(False)
+    names = ["prep", "rotate", "gate_up", "act", "down", "combine"]
+    ph = {n: statistics.median(p[j] for p in phases[1:]) * 1e3 for j, n in enumerate(names) if j < len(phases[0])}
+
+    H_, I_, k = w["H"], w["I"], w["topk"]
+    flops_layer = T * k * 6.0 * H_ * I_
+    flops_gu = T * k * 4.0 * H_ * I_
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tpk = float(json.load(f)["bf16_tflops"])
+        tkind = "measured"
+    except Exception:
+        tpk, tkind = 1590.0, "fallback"
+    gu_s = ph["gate_up"] / 1e6
+    step_s = total_ms / args.steps / 1e3
+    roofline = {"kernel": "tc_gemm_kernel x2 (gate, up: tcgen05 grouped GEMM)", "bound": "tensor",
+                "unit": "TFLOP/s", "achieved": flops_gu / gu_s / 1e12, "peak": tpk, "peak_kind": tkind,
+                "frac": flops_gu / gu_s / 1e12 / tpk, "flops_per_launch": flops_gu, "us_per_launch": ph["gate_up"],
+                "traffic": None,
+                "layer": {"flops": flops_layer, "us": step_s * 1e6, "achieved": flops_layer / step_s / 1e12,
+                          "frac": flops_layer / step_s / 1e12 / tpk}}
+    del graph
+    return {"metric": f"MoE layer prefill tokens/s ({w['name']})", "value": T * args.steps / (total_ms / 1e3),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16 MMA (tcgen05), fp32 accumulate", "data": "synthetic",
+            "config": {"workload": w["name"] + f", T={T}", "tokens_per_step": T,
+                       "l2": "256 MB L2 flush before every step (untimed)"},
+            "us_per_layer": step_s * 1e6, "phases_us": ph, "roofline": roofline,
+            "gpu_launches": 7 * args.steps, "clocks": clk.summary()}
+
+
 def _sweep_point(layer, dev, T, flush):
     import numpy as np
     import torch
@@ -462,14 +760,21 @@ def main():
     import torch
     import torch.distributed as dist
     from datetime import timedelta
+    if args.workload == "prefill":
+        print(json.dumps(run_prefill(args, rank, local_rank, world)), flush=True)
+        return
     if world > 1:
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     # the CPU sample runs first, before CUDA is touched (spawned workers)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and args.workload == "decode" and not args.no_cpu_baseline:
         cpu = cpu_reference(args.tokens, 5, 1, 2.0)
-    res = run_b200(args, rank, local_rank, world)
+    if args.workload == "ep" or world > 1:
+        res = run_ep(args, rank, local_rank, world, "ep" if args.workload == "ep" else "decode")
+    else:
+        res = run_b200(args, rank, local_rank, world)
     if cpu is not None:
         res["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
     if rank == 0:

@@ -148,6 +148,40 @@ int exl3_linear_noalloc(const void* x, int x_dtype, int64_t m, const void* trell
                         const void* svh, int64_t in_features, int64_t out_features, int K,
                         int codebook, void* y, int y_dtype, void* stream);
 
+/* Expert-parallel dispatch, source side (no counterpart in the reference,
+ * which leaves the exchange to vLLM's all-to-all backends and consumes only
+ * the resulting expert_map, src/vllm_exl3/exl3.py:2310-2354).  Rank g of
+ * `world` owns global experts [g*E/world, (g+1)*E/world), E = n_global
+ * (a multiple of world).  For every token t < n_valid (all tokens when
+ * n_valid is NULL) and every rank g owning at least one of its routes it
+ * writes one pair p: send_x[p] = x[t], send_ids[p][k] = the local id of
+ * route k on g or -1, send_w[p][k] = its weight (fp32) or 0, send_tok[p] = t,
+ * pair_idx[t][g] = p (-1 where t sends nothing to g).  Pairs are rank-major
+ * and token-ascending inside a rank; send_counts[g] = rank g's pairs, so rank
+ * g's rows are the contiguous block after the counts of ranks < g.  Size the
+ * pair buffers for tokens * min(world, topk) rows.  With capacity C > 0
+ * (C >= tokens, the same on every rank) rank g's pairs instead fill rows
+ * [g*C, g*C + send_counts[g]) of fixed C-row blocks; the other slots get
+ * send_tok -1, ids -1 and weight 0 (their send_x rows are not written), so
+ * the exchange is an equal-split all-to-all of C rows per rank and no count
+ * has to reach the host; size the buffers for world * C rows.  Routes with
+ * ids outside [0, E) are dropped.  x fp32/fp16/bf16 [tokens][hidden], hidden
+ * a multiple of 128, x and send_x 16-byte aligned. */
+int exl3_ep_dispatch(const void* x, int x_dtype, int64_t tokens, int64_t hidden, const void* topk_ids,
+                     int ids_dtype, const void* topk_weights, int w_dtype, int topk, int64_t n_global,
+                     int world, const int32_t* n_valid, void* send_x, int32_t* send_ids, float* send_w,
+                     int32_t* send_tok, int32_t* pair_idx, int32_t* send_counts, int64_t capacity,
+                     void* stream);
+
+/* Expert-parallel combine, source side (no reference counterpart; see
+ * exl3_ep_dispatch): out[t] = sum over ranks g = 0, 1, ... of
+ * partial[pair_idx[t][g]] where that is >= 0, accumulated in fp32 in that
+ * fixed order (deterministic, no atomics); rows t >= n_valid are zero.
+ * partial fp32/fp16/bf16 [pairs][hidden], out fp32/fp16/bf16 [tokens][hidden],
+ * both 16-byte aligned. */
+int exl3_ep_combine(const void* partial, int partial_dtype, const int32_t* pair_idx, int64_t tokens, int world,
+                    int64_t hidden, const int32_t* n_valid, void* out, int out_dtype, void* stream);
+
 /* Phase timing for benchmarks (no reference counterpart; the reference times
  * its kernels with CUDA events in tools/bench_moe_decode.py:24-55).  While
  * enabled, exl3_moe_forward and exl3_linear first launch a spin of

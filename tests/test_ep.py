@@ -1,0 +1,246 @@
+"""Expert parallelism: exchange logic on gloo ranks (CPU) and the native
+dispatch / combine kernels plus an emulated multi-rank step (GPU).
+
+The reference has no EP code of its own (it consumes vLLM's expert_map,
+src/vllm_exl3/exl3.py:2310-2354); the oracle for an EP layer is the
+single-rank eager loop over all experts (exl3.py:2357-2413), so a G-rank
+step must reproduce it within the layer tolerance.
+"""
+
+import socket
+
+import numpy as np
+import pytest
+
+import cpu_oracle as oracle
+import ep_helpers
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _close(got: np.ndarray, want: np.ndarray, rel: float = 2e-2, cos_min: float = 0.9995) -> None:
+    rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+    err = float(np.max(np.abs(got.astype(np.float64) - want)))
+    assert err <= rel * rms, (err, rms)
+    den = np.linalg.norm(got) * np.linalg.norm(want)
+    if den > 0:
+        assert float(np.dot(got.ravel(), want.ravel()) / den) >= cos_min
+
+
+# ---------------------------------------------------------------------------
+# CPU: gloo ranks, exchange logic with CPU stand-ins for the kernels
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("n_valid,capacity", [(None, None), (7, None), (None, 12), (5, 16)])
+def test_ep_gloo_world2_matches_single_rank(n_valid, capacity):
+    import torch.multiprocessing as mp
+    from exl3_b200 import synthetic
+
+    cfg = dict(seed=11, E=8, H=256, I=128, topk=2, T=12, n_valid=n_valid, capacity=capacity)
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    mp.start_processes(ep_helpers.gloo_worker, args=(world, _free_port(), cfg, q), nprocs=world,
+                       join=True, start_method="spawn")
+    got = dict()
+    counts = dict()
+    for _ in range(world):
+        r, y, c = q.get(timeout=60)
+        got[r] = y
+        counts[r] = c
+    pack = synthetic.make_moe_pack(cfg["seed"], cfg["E"], cfg["H"], cfg["I"], synthetic.CB_MCG, (4,))
+    dense = ep_helpers.dense_experts(pack, 0, cfg["E"])
+    rng = np.random.default_rng(cfg["seed"] + 7)
+    x = synthetic.activations(rng, cfg["T"] * world, cfg["H"])
+    ids, w = synthetic.softmax_topk(rng, cfg["T"] * world, cfg["E"], cfg["topk"])
+    ids[::5, 0] = -1
+    for r in range(world):
+        sl = slice(r * cfg["T"], (r + 1) * cfg["T"])
+        want = oracle.moe_eager(x[sl], ids[sl], w[sl], dense)
+        if n_valid is not None:
+            want[n_valid:] = 0.0
+        np.testing.assert_allclose(got[r], want, rtol=1e-5, atol=1e-5 * float(np.abs(want).max() + 1))
+    # what rank r sends to q is what q receives from r
+    if capacity is None:
+        for r in range(world):
+            for qq in range(world):
+                assert counts[r][0][qq] == counts[qq][1][r]
+
+
+def test_ep_cpu_dispatch_contract():
+    """The stand-in keeps the documented layout: rank-major, token-ascending."""
+    import torch
+    rng = np.random.default_rng(3)
+    T, H, E, topk, G = 20, 128, 12, 3, 3
+    x = torch.from_numpy(rng.normal(size=(T, H)).astype(np.float32))
+    ids = torch.from_numpy(rng.integers(-2, E + 2, size=(T, topk)))
+    w = torch.from_numpy(rng.random((T, topk)).astype(np.float32))
+    sx, sid, sw, stok, pidx, counts = ep_helpers.ep_dispatch_cpu(x, ids, w, E, G)
+    off = np.concatenate([[0], np.cumsum(counts.numpy())])
+    for g in range(G):
+        toks = stok[off[g]:off[g + 1]].numpy()
+        assert np.all(np.diff(toks) > 0)
+        for p in range(off[g], off[g + 1]):
+            t = int(stok[p])
+            assert int(pidx[t, g]) == p
+            assert torch.equal(sx[p], x[t])
+            for k in range(topk):
+                gid = int(ids[t, k])
+                mine = 0 <= gid < E and gid // (E // G) == g
+                assert int(sid[p, k]) == (gid - g * (E // G) if mine else -1)
+                assert float(sw[p, k]) == (float(w[t, k]) if mine else 0.0)
+
+
+def test_ep_rejects_uneven_split():
+    from exl3_b200.ep import Exl3ExpertParallel
+    layer = ep_helpers.DenseLocalLayer([{}] * 3)
+    with pytest.raises(ValueError):
+        Exl3ExpertParallel(layer, 8, ops=ep_helpers.CpuEpOps())  # world 1 holds all 8, not 3
+
+
+# ---------------------------------------------------------------------------
+# GPU: native kernels against the restatement; emulated G-rank step
+# ---------------------------------------------------------------------------
+@pytest.mark.gpu
+@pytest.mark.parametrize("G,dt,ids_dt,nv,cap", [(1, "bf16", "i64", None, 0), (2, "bf16", "i32", None, 0),
+                                                (4, "f16", "i64", 13, 0), (8, "f32", "i32", None, 0),
+                                                (3, "bf16", "i64", 0, 0), (2, "bf16", "i64", None, 37),
+                                                (4, "f32", "i32", 20, 50), (8, "bf16", "i64", None, 64)])
+def test_ep_dispatch_combine_match_restatement(native, cuda, G, dt, ids_dt, nv, cap):
+    import torch
+    from exl3_b200.ep import NativeEpOps
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[dt]
+    rng = np.random.default_rng(G * 31 + 5)
+    T, H, E, topk = 37, 384, 24, 6
+    x = torch.from_numpy(rng.normal(size=(T, H)).astype(np.float32)).to(tdt)
+    ids = torch.from_numpy(rng.integers(-1, E + 1, size=(T, topk))).to(
+        torch.int32 if ids_dt == "i32" else torch.int64)
+    w = torch.from_numpy(rng.random((T, topk)).astype(np.float32)).to(torch.bfloat16)
+    ops = NativeEpOps()
+    nvt = None if nv is None else torch.tensor([nv], dtype=torch.int32, device=cuda)
+    sx, sid, sw, pidx, counts = ops.dispatch(x.to(cuda), ids.to(cuda), w.to(cuda), E, G, nvt, capacity=cap)
+    wx, wid, ww, wtok, wpidx, wcounts = ep_helpers.ep_dispatch_cpu(x, ids, w, E, G, nv, cap)
+    P = int(wcounts.sum()) if not cap else G * cap
+    assert torch.equal(counts.cpu(), wcounts)
+    assert torch.equal(pidx.cpu()[:T], wpidx)
+    assert torch.equal(sid[:P].cpu(), wid)
+    assert torch.equal(sw[:P].cpu(), ww)
+    used = (wtok >= 0)  # empty capacity slots' rows are not written
+    assert torch.equal(sx[:P].cpu()[used], wx[used])
+    # combine: fp32 sums in rank order, bit-exact
+    for pdt, odt in ((torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16), (torch.float16, torch.float32)):
+        part = torch.from_numpy(rng.normal(size=(max(P, 1), H)).astype(np.float32)).to(pdt)
+        got = ops.combine(part.to(cuda), pidx, T, G, odt, nvt).cpu()
+        want = ep_helpers.ep_combine_cpu(part, wpidx, T, G, nv).to(odt)
+        assert torch.equal(got, want)
+
+
+def _emulated_step(layers, x, ids, w, E, G, combine_dtype):
+    """G ranks on one GPU: per-rank dispatch, the all-to-all as slicing,
+    per-rank local forward, the return all-to-all, per-rank combine."""
+    import torch
+    from exl3_b200.ep import NativeEpOps
+    ops = NativeEpOps()
+    T = x.shape[0] // G
+    disp = [ops.dispatch(x[r * T:(r + 1) * T], ids[r * T:(r + 1) * T], w[r * T:(r + 1) * T], E, G) for r in range(G)]
+    counts = [d[4].cpu().tolist() for d in disp]
+    offs = [np.concatenate([[0], np.cumsum(c)]).astype(int) for c in counts]
+    partial_back = [[None] * G for _ in range(G)]
+    for q in range(G):  # receiver
+        rx = torch.cat([disp[r][0][offs[r][q]:offs[r][q + 1]] for r in range(G)])
+        rid = torch.cat([disp[r][1][offs[r][q]:offs[r][q + 1]] for r in range(G)])
+        rw = torch.cat([disp[r][2][offs[r][q]:offs[r][q + 1]] for r in range(G)])
+        part = ops.local(layers[q], rx, rid, rw, combine_dtype, None)
+        o = 0
+        for r in range(G):
+            n = counts[r][q]
+            partial_back[r][q] = part[o:o + n]
+            o += n
+    outs = []
+    for r in range(G):
+        back = torch.cat([partial_back[r][q] for q in range(G)])
+        outs.append(ops.combine(back, disp[r][3], T, G, x.dtype))
+    return torch.cat(outs)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("G,cdt", [(2, "bf16"), (4, "f32")])
+def test_ep_emulated_ranks_match_single_gpu_and_oracle(native, cuda, G, cdt):
+    import torch
+    from exl3_b200 import moe, synthetic
+    E, H, I, topk, Tr = 16, 512, 256, 4, 24
+    pack = synthetic.make_moe_pack(21, E, H, I, synthetic.CB_MCG, (2, 3, 4))
+    full = moe.layer_from_pack(pack, cuda)
+    epr = E // G
+    layers = []
+    for r in range(G):
+        sub = synthetic.MoEPack(H, I, pack.codebook, pack.experts[r * epr:(r + 1) * epr])
+        layers.append(moe.layer_from_pack(sub, cuda))
+    rng = np.random.default_rng(99)
+    xs = synthetic.activations(rng, Tr * G, H)
+    ids, w = synthetic.softmax_topk(rng, Tr * G, E, topk)
+    x = torch.from_numpy(xs).to(torch.bfloat16).to(cuda)
+    idt = torch.from_numpy(ids).to(cuda)
+    wt = torch.from_numpy(w).to(cuda)
+    cdt_t = torch.bfloat16 if cdt == "bf16" else torch.float32
+    got = _emulated_step(layers, x, idt, wt, E, G, cdt_t).float().cpu().numpy()
+    single = full.apply(x, wt, idt).float().cpu().numpy()
+    _close(got, single)
+    dense = ep_helpers.dense_experts(pack, 0, E)
+    want = oracle.moe_eager(x.float().cpu().numpy(), ids, w, dense)
+    _close(got, want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("cap", [None, 48])
+def test_ep_world1_module_matches_layer(native, cuda, cap):
+    import torch
+    from exl3_b200 import moe, synthetic
+    from exl3_b200.ep import Exl3ExpertParallel
+    pack = synthetic.make_moe_pack(5, 8, 256, 128, synthetic.CB_MCG, (4,))
+    layer = moe.layer_from_pack(pack, cuda)
+    ep = Exl3ExpertParallel(layer, 8, combine_dtype=torch.float32, capacity=cap)
+    rng = np.random.default_rng(4)
+    x = torch.from_numpy(synthetic.activations(rng, 40, 256)).to(torch.bfloat16).to(cuda)
+    ids, w = synthetic.softmax_topk(rng, 40, 8, 2)
+    idt, wt = torch.from_numpy(ids).to(cuda), torch.from_numpy(w).to(cuda)
+    got = ep(x, wt, idt).float().cpu().numpy()
+    want = layer.apply(x, wt, idt).float().cpu().numpy()
+    _close(got, want, rel=1e-2)
+    nv = torch.tensor([17], dtype=torch.int32, device=cuda)
+    got = ep(x, wt, idt, n_valid=nv).float().cpu().numpy()
+    assert np.all(got[17:] == 0)
+    _close(got[:17], want[:17], rel=1e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("capacity", [None, 40])
+def test_ep_nccl_two_gpus(native, capacity):
+    """Two ranks over NCCL on two GPUs (skipped on a one-GPU box)."""
+    import torch
+    import torch.multiprocessing as mp
+    from exl3_b200 import moe, synthetic
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    cfg = dict(seed=17, E=16, H=512, I=256, topk=4, T=40, capacity=capacity)
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    mp.start_processes(ep_helpers.nccl_worker, args=(world, _free_port(), cfg, q), nprocs=world, join=True,
+                       start_method="spawn")
+    got = {}
+    for _ in range(world):
+        r, y, _c = q.get(timeout=120)
+        got[r] = y
+    pack = synthetic.make_moe_pack(cfg["seed"], cfg["E"], cfg["H"], cfg["I"], synthetic.CB_MCG, (2, 3, 4))
+    dense = ep_helpers.dense_experts(pack, 0, cfg["E"])
+    rng = np.random.default_rng(cfg["seed"] + 7)
+    x = synthetic.activations(rng, cfg["T"] * world, cfg["H"])
+    ids, w = synthetic.softmax_topk(rng, cfg["T"] * world, cfg["E"], cfg["topk"])
+    xh = x.astype(np.float32)
+    for r in range(world):
+        sl = slice(r * cfg["T"], (r + 1) * cfg["T"])
+        _close(got[r], oracle.moe_eager(xh[sl], ids[sl], w[sl], dense))

@@ -303,6 +303,75 @@ int exl3_fat_gemm(const void* a, int64_t m, const void* packed, const void* svh,
     return e == cudaSuccess ? EXL3_OK : cuda_fail(e, "exl3_fat_gemm");
 }
 
+int exl3_ep_dispatch(const void* x, int x_dtype, int64_t tokens, int64_t hidden, const void* ids, int ids_dtype,
+                     const void* weights, int w_dtype, int topk, int64_t n_global, int world,
+                     const int32_t* n_valid, void* send_x, int32_t* send_ids, float* send_w, int32_t* send_tok,
+                     int32_t* pair_idx, int32_t* send_counts, int64_t capacity, void* stream) {
+    const char* who = "exl3_ep_dispatch";
+    if (!x || !ids || !weights) return fail(EXL3_ERR_ARG, "%s: null x/ids/weights", who);
+    if (!send_x || !send_ids || !send_w || !send_tok || !pair_idx || !send_counts)
+        return fail(EXL3_ERR_ARG, "%s: null output buffer", who);
+    if (!float_dtype(x_dtype) || !float_dtype(w_dtype))
+        return fail(EXL3_ERR_ARG, "%s: x/weights dtype must be fp32, fp16 or bf16", who);
+    if (ids_dtype != EXL3_DT_I32 && ids_dtype != EXL3_DT_I64)
+        return fail(EXL3_ERR_ARG, "%s: expert ids must be int32 or int64", who);
+    if (world < 1 || world > exl3::kEpMaxWorld)
+        return fail(EXL3_ERR_ARG, "%s: world size must be in 1..%d", who, exl3::kEpMaxWorld);
+    if (n_global < world || n_global % world)
+        return fail(EXL3_ERR_ARG, "%s: %lld experts do not split evenly over %d ranks", who, (long long)n_global,
+                    world);
+    if (topk < 1 || topk > 64) return fail(EXL3_ERR_ARG, "%s: topk must be in 1..64", who);
+    if (tokens < 0 || tokens * int64_t(world) > INT32_MAX)
+        return fail(EXL3_ERR_ARG, "%s: tokens x world must fit int32", who);
+    if (hidden <= 0 || hidden % 128 || hidden > INT32_MAX)
+        return fail(EXL3_ERR_ARG, "%s: hidden width must be a positive multiple of 128", who);
+    if (!aligned(x, 16) || !aligned(send_x, 16)) return fail(EXL3_ERR_ARG, "%s: x/send_x must be 16-byte aligned", who);
+    if (capacity < 0 || (capacity > 0 && capacity < tokens) || capacity * int64_t(world) > INT32_MAX)
+        return fail(EXL3_ERR_ARG, "%s: capacity must be 0 or in [tokens, INT32_MAX / world] (got %lld)", who,
+                    (long long)capacity);
+    exl3::EpDispatchCall c;
+    c.x = x;
+    c.x_esize = x_dtype == EXL3_DT_F32 ? 4 : 2;
+    c.tokens = tokens;
+    c.hidden = int(hidden);
+    c.ids = ids;
+    c.ids_dtype = ids_dtype;
+    c.weights = weights;
+    c.w_dtype = w_dtype;
+    c.topk = topk;
+    c.n_global = n_global;
+    c.world = world;
+    c.n_valid = n_valid;
+    c.send_x = send_x;
+    c.send_ids = send_ids;
+    c.send_w = send_w;
+    c.send_tok = send_tok;
+    c.pair_idx = pair_idx;
+    c.send_counts = send_counts;
+    c.capacity = capacity;
+    cudaError_t e = exl3::run_ep_dispatch(c, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, who);
+}
+
+int exl3_ep_combine(const void* partial, int partial_dtype, const int32_t* pair_idx, int64_t tokens, int world,
+                    int64_t hidden, const int32_t* n_valid, void* out, int out_dtype, void* stream) {
+    const char* who = "exl3_ep_combine";
+    if (!partial || !pair_idx || !out) return fail(EXL3_ERR_ARG, "%s: null argument", who);
+    if (!float_dtype(partial_dtype) || !float_dtype(out_dtype))
+        return fail(EXL3_ERR_ARG, "%s: partial/out dtype must be fp32, fp16 or bf16", who);
+    if (world < 1 || world > exl3::kEpMaxWorld)
+        return fail(EXL3_ERR_ARG, "%s: world size must be in 1..%d", who, exl3::kEpMaxWorld);
+    if (tokens < 0 || tokens * int64_t(world) > INT32_MAX)
+        return fail(EXL3_ERR_ARG, "%s: tokens x world must fit int32", who);
+    if (hidden <= 0 || hidden % 128 || hidden > INT32_MAX)
+        return fail(EXL3_ERR_ARG, "%s: hidden width must be a positive multiple of 128", who);
+    if (!aligned(partial, 16) || !aligned(out, 16))
+        return fail(EXL3_ERR_ARG, "%s: partial/out must be 16-byte aligned", who);
+    cudaError_t e = exl3::run_ep_combine(partial, partial_dtype, pair_idx, tokens, world, int(hidden), n_valid, out,
+                                         out_dtype, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, who);
+}
+
 int exl3_profile_enable(int on, long long delay_cycles) {
     exl3::profile_enable(on != 0, delay_cycles);
     return EXL3_OK;

@@ -1,0 +1,284 @@
+// ep.cu -- expert-parallel dispatch/combine around the local routed-expert
+// forward.
+//
+// Experts are split into `world` contiguous blocks of n_global/world (rank g
+// owns experts [g*epr, (g+1)*epr)), the linear expert_map the reference's
+// plugin consumes (src/vllm_exl3/exl3.py:2310-2354, map_topk_to_local at
+// :2332).  A token is sent once to every rank that owns at least one of its
+// routes (a "pair" (token, rank)); the pair carries the token row plus topk
+// (local id, weight) slots, -1 / 0 for routes owned elsewhere, so the
+// receiving rank runs the ordinary fused forward on it and returns one
+// partial row: the weighted sum of that token's local routes.  The source
+// adds its pairs' partial rows in rank order (no float atomics: the sum is
+// deterministic).
+//
+// Send-buffer order is rank-major, token-ascending within a rank, so rank g's
+// rows are one contiguous block: packed ([off_g, off_g + count_g), the split
+// layout of an all-to-all with per-rank counts) or, given a capacity C >= the
+// tokens of any rank, [g*C, g*C + count_g) of fixed C-row blocks whose empty
+// slots carry no routes -- an equal-split all-to-all whose sizes never reach
+// the host, so a whole step can be captured in a CUDA graph.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "exl3_common.cuh"
+#include "exl3_internal.h"
+
+namespace exl3 {
+namespace {
+
+constexpr int kEpPlanThreads = 1024;
+constexpr int kEpWarps = kEpPlanThreads / 32;
+
+struct EpPlanArgs {
+    const void* ids;
+    int ids_dtype;
+    const void* weights;
+    int w_dtype;
+    int64_t tokens;
+    int topk;
+    int64_t n_global;
+    int world;
+    const int32_t* n_valid;
+    int32_t* send_ids;
+    float* send_w;
+    int32_t* send_tok;
+    int32_t* pair_idx;
+    int32_t* send_counts;
+    int64_t capacity;  // > 0: rank g's pairs start at row g * capacity
+};
+
+// bit g set <=> a route of token t is owned by rank g (invalid ids own nothing)
+__device__ __forceinline__ uint64_t token_ranks(const EpPlanArgs& a, int64_t t, int64_t epr) {
+    uint64_t m = 0;
+    for (int k = 0; k < a.topk; ++k) {
+        const int64_t id = load_id(a.ids, t * a.topk + k, a.ids_dtype);
+        if (id >= 0 && id < a.n_global) m |= uint64_t(1) << int(id / epr);
+    }
+    return m;
+}
+
+// One CTA.  Pass 1 counts pairs per rank (warp ballots); pass 2 ranks every
+// pair inside its rank's block, chunk by chunk, and writes the pair's meta.
+__global__ void __launch_bounds__(kEpPlanThreads) ep_plan_kernel(const EpPlanArgs a) {
+    __shared__ int wpos[kEpWarps][kEpMaxWorld];
+    __shared__ int run[kEpMaxWorld];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = a.world;
+    int64_t T = a.tokens;
+    if (a.n_valid) T = min(T, int64_t(max(0, *a.n_valid)));
+    const int64_t epr = a.n_global / G;
+    const unsigned lt = (1u << lane) - 1u;
+
+    if (tid < G) run[tid] = 0;
+    __syncthreads();
+    for (int64_t c = 0; c < T; c += kEpPlanThreads) {
+        const int64_t t = c + tid;
+        const uint64_t m = t < T ? token_ranks(a, t, epr) : 0;
+        for (int g = 0; g < G; ++g) {
+            const unsigned b = __ballot_sync(0xffffffffu, (m >> g) & 1);
+            if (lane == 0 && b) atomicAdd(&run[g], __popc(b));
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int s = 0;
+        for (int g = 0; g < G; ++g) {
+            const int n = run[g];
+            a.send_counts[g] = n;
+            run[g] = a.capacity > 0 ? int(g * a.capacity) : s;  // position of rank g's next pair
+            s += n;
+        }
+    }
+    __syncthreads();
+    if (a.capacity > 0) {
+        // empty slots of each rank's block: no token, no routes
+        for (int g = 0; g < G; ++g) {
+            const int64_t n = a.send_counts[g];
+            for (int64_t i = n + tid; i < a.capacity; i += kEpPlanThreads) {
+                const int64_t slot = g * a.capacity + i;
+                a.send_tok[slot] = -1;
+                for (int k = 0; k < a.topk; ++k) {
+                    a.send_ids[slot * a.topk + k] = -1;
+                    a.send_w[slot * a.topk + k] = 0.f;
+                }
+            }
+        }
+    }
+
+    for (int64_t c = 0; c < T; c += kEpPlanThreads) {
+        const int64_t t = c + tid;
+        const uint64_t m = t < T ? token_ranks(a, t, epr) : 0;
+        for (int g = 0; g < G; ++g) {
+            const unsigned b = __ballot_sync(0xffffffffu, (m >> g) & 1);
+            if (lane == 0) wpos[warp][g] = __popc(b);
+        }
+        __syncthreads();
+        if (tid < G) {
+            int s = run[tid];
+            for (int w = 0; w < kEpWarps; ++w) {
+                const int v = wpos[w][tid];
+                wpos[w][tid] = s;
+                s += v;
+            }
+            run[tid] = s;
+        }
+        __syncthreads();
+        for (int g = 0; g < G; ++g) {
+            const bool mine = (m >> g) & 1;
+            const unsigned b = __ballot_sync(0xffffffffu, mine);
+            if (mine) {
+                const int pos = wpos[warp][g] + __popc(b & lt);
+                a.pair_idx[t * G + g] = pos;
+                a.send_tok[pos] = int32_t(t);
+                for (int k = 0; k < a.topk; ++k) {
+                    const int64_t id = load_id(a.ids, t * a.topk + k, a.ids_dtype);
+                    const bool own = id >= 0 && id < a.n_global && id / epr == g;
+                    a.send_ids[int64_t(pos) * a.topk + k] = own ? int32_t(id - g * epr) : -1;
+                    a.send_w[int64_t(pos) * a.topk + k] = own ? load_as_float(a.weights, t * a.topk + k, a.w_dtype) : 0.f;
+                }
+            } else if (t < T) {
+                a.pair_idx[t * G + g] = -1;
+            }
+        }
+        __syncthreads();  // wpos is rewritten by the next chunk
+    }
+    // rows past n_valid own no pairs
+    for (int64_t i = T * G + tid; i < a.tokens * G; i += kEpPlanThreads) a.pair_idx[i] = -1;
+}
+
+// Copy each pair's token row into the send buffer: warp per pair, 16-byte
+// vectors (rows are whole multiples of 256 bytes).
+// With a capacity the rows are the world * capacity slots; empty slots
+// (send_tok -1) are skipped and keep whatever the buffer held.
+__global__ void __launch_bounds__(256) ep_gather_kernel(const uint4* __restrict__ x, int64_t row_vecs,
+                                                        const int32_t* __restrict__ send_tok,
+                                                        const int32_t* __restrict__ send_counts, int world,
+                                                        int64_t capacity, uint4* __restrict__ send_x) {
+    __shared__ int64_t total;
+    if (threadIdx.x == 0) {
+        int64_t s = 0;
+        for (int g = 0; g < world; ++g) s += send_counts[g];
+        total = capacity > 0 ? world * capacity : s;
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t p = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; p < total; p += nw) {
+        const int tok = send_tok[p];
+        if (tok < 0) continue;
+        const uint4* src = x + int64_t(tok) * row_vecs;
+        uint4* dst = send_x + p * row_vecs;
+        for (int64_t v = lane; v < row_vecs; v += 32) dst[v] = src[v];
+    }
+}
+
+__device__ __forceinline__ void load4(const void* p, int64_t i, int dt, float (&v)[4]) {
+    if (dt == DT_F32) {
+        const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+        v[0] = f.x, v[1] = f.y, v[2] = f.z, v[3] = f.w;
+    } else {
+        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p) + i);
+        if (dt == DT_F16) {
+            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+            v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+        } else {
+            const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+            const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+            v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+        }
+    }
+}
+
+__device__ __forceinline__ void store4(void* p, int64_t i, int dt, const float (&v)[4]) {
+    if (dt == DT_F32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(p) + i) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+        uint2 u;
+        if (dt == DT_F16) {
+            const __half2 a = __floats2half2_rn(v[0], v[1]), b = __floats2half2_rn(v[2], v[3]);
+            u.x = *reinterpret_cast<const uint32_t*>(&a);
+            u.y = *reinterpret_cast<const uint32_t*>(&b);
+        } else {
+            const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+            u.x = *reinterpret_cast<const uint32_t*>(&a);
+            u.y = *reinterpret_cast<const uint32_t*>(&b);
+        }
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p) + i) = u;
+    }
+}
+
+// out[t] = sum over ranks g (ascending) of partial[pair_idx[t][g]]; warp per
+// token, lanes holding 4 consecutive features.  Rows past n_valid are zero.
+__global__ void __launch_bounds__(256) ep_combine_kernel(const void* __restrict__ partial, int pdt,
+                                                         const int32_t* __restrict__ pair_idx, int64_t tokens,
+                                                         int world, int hidden, const int32_t* n_valid,
+                                                         void* __restrict__ out, int odt) {
+    const int lane = threadIdx.x & 31;
+    int64_t T = tokens;
+    if (n_valid) T = min(T, int64_t(max(0, *n_valid)));
+    const int64_t nw = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t t = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; t < tokens; t += nw) {
+        const bool live = t < T;
+        const int p0 = live && lane < world ? pair_idx[t * world + lane] : -1;
+        const int p1 = live && lane + 32 < world ? pair_idx[t * world + lane + 32] : -1;
+        for (int c0 = 4 * lane; c0 < hidden; c0 += 128) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            if (live) {
+                for (int g = 0; g < world; ++g) {
+                    const int p = g < 32 ? __shfl_sync(0xffffffffu, p0, g) : __shfl_sync(0xffffffffu, p1, g - 32);
+                    if (p < 0) continue;
+                    float v[4];
+                    load4(partial, int64_t(p) * hidden + c0, pdt, v);
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) acc[i] += v[i];
+                }
+            }
+            store4(out, t * hidden + c0, odt, acc);
+        }
+    }
+}
+
+}  // namespace
+
+cudaError_t run_ep_dispatch(const EpDispatchCall& c, cudaStream_t s) {
+    EpPlanArgs a;
+    a.ids = c.ids;
+    a.ids_dtype = c.ids_dtype;
+    a.weights = c.weights;
+    a.w_dtype = c.w_dtype;
+    a.tokens = c.tokens;
+    a.topk = c.topk;
+    a.n_global = c.n_global;
+    a.world = c.world;
+    a.n_valid = c.n_valid;
+    a.send_ids = c.send_ids;
+    a.send_w = c.send_w;
+    a.send_tok = c.send_tok;
+    a.pair_idx = c.pair_idx;
+    a.send_counts = c.send_counts;
+    a.capacity = c.capacity;
+    ep_plan_kernel<<<1, kEpPlanThreads, 0, s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || c.tokens == 0) return e;
+    const int64_t row_vecs = c.hidden * int64_t(c.x_esize) / 16;
+    const int64_t max_pairs =
+        c.capacity > 0 ? c.world * c.capacity : c.tokens * int64_t(std::min(c.world, c.topk));
+    const int grid = int(std::max<int64_t>(1, std::min<int64_t>((max_pairs + 7) / 8, int64_t(num_sms_current()) * 8)));
+    ep_gather_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(c.x), row_vecs, c.send_tok, c.send_counts,
+                                          c.world, c.capacity, static_cast<uint4*>(c.send_x));
+    return cudaGetLastError();
+}
+
+cudaError_t run_ep_combine(const void* partial, int pdt, const int32_t* pair_idx, int64_t tokens, int world,
+                           int hidden, const int32_t* n_valid, void* out, int odt, cudaStream_t s) {
+    if (tokens == 0) return cudaSuccess;
+    const int grid = int(std::max<int64_t>(1, std::min<int64_t>((tokens + 7) / 8, int64_t(num_sms_current()) * 8)));
+    ep_combine_kernel<<<grid, 256, 0, s>>>(partial, pdt, pair_idx, tokens, world, hidden, n_valid, out, odt);
+    return cudaGetLastError();
+}
+
+}  // namespace exl3

@@ -91,6 +91,36 @@ cudaError_t run_reconstruct(int K, int cb, bool full, const void* trellis, const
 cudaError_t run_had128(const void* x, void* y, int64_t rows, int64_t n, const void* pre,
                        const void* post, float scale, cudaStream_t s);
 
+// Expert-parallel dispatch (source side): rank g owns experts
+// [g * n_global / world, (g + 1) * n_global / world).
+constexpr int kEpMaxWorld = 64;
+
+struct EpDispatchCall {
+    const void* x = nullptr;  // [tokens][hidden], element size x_esize
+    int x_esize = 2;
+    int64_t tokens = 0;
+    int hidden = 0;
+    const void* ids = nullptr;
+    int ids_dtype = 3;
+    const void* weights = nullptr;
+    int w_dtype = 0;
+    int topk = 0;
+    int64_t n_global = 0;
+    int world = 1;
+    const int32_t* n_valid = nullptr;
+    void* send_x = nullptr;        // [pairs][hidden]
+    int32_t* send_ids = nullptr;   // [pairs][topk] local expert id or -1
+    float* send_w = nullptr;       // [pairs][topk]
+    int32_t* send_tok = nullptr;   // [pairs] source token
+    int32_t* pair_idx = nullptr;   // [tokens][world] pair row or -1
+    int32_t* send_counts = nullptr;  // [world]
+    int64_t capacity = 0;            // > 0: fixed blocks of capacity rows per rank
+};
+
+cudaError_t run_ep_dispatch(const EpDispatchCall& c, cudaStream_t s);
+cudaError_t run_ep_combine(const void* partial, int pdt, const int32_t* pair_idx, int64_t tokens, int world,
+                           int hidden, const int32_t* n_valid, void* out, int odt, cudaStream_t s);
+
 int num_sms_current();
 void tc_pick_stages(int kmax, int& stages, size_t& smem);
 void profile_enable(bool on, long long delay_cycles);

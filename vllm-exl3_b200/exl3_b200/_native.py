@@ -57,6 +57,8 @@ SIGNATURES = {
     "exl3_batched_linear": (I32, [P, I32, I64, P, P, P, I32, P, I32, I64, I64, I32, I32, P, I32, P, SZ, P]),
     "exl3_fat_gemm": (I32, [P, I64, P, P, I64, I64, I32, I32, P, P, P, P, SZ, P]),
     "exl3_linear_noalloc": (I32, [P, I32, I64, P, P, P, I64, I64, I32, I32, P, I32, P]),
+    "exl3_ep_dispatch": (I32, [P, I32, I64, I64, P, I32, P, I32, I32, I64, I32, P, P, P, P, P, P, P, I64, P]),
+    "exl3_ep_combine": (I32, [P, I32, P, I64, I32, I64, P, P, I32, P]),
     "exl3_profile_enable": (I32, [I32, ctypes.c_longlong]),
     "exl3_profile_read": (I32, [ctypes.POINTER(F32), I32, ctypes.POINTER(I32)]),
 }

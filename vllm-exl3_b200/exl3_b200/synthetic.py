@@ -85,6 +85,26 @@ def make_moe_pack(seed: int, n_experts: int, hidden: int, inter: int, codebook: 
     return pack
 
 
+def make_moe_pack_slice(seed: int, n_experts: int, hidden: int, inter: int, codebook: int,
+                        k_choices=(4,), k_probs=None, lo: int = 0, hi: int | None = None) -> MoEPack:
+    """Experts [lo, hi) of an n_experts pack whose expert e is drawn from its
+    own generator (seed, e): any rank of an expert-parallel group builds its
+    shard without generating the others.  Per-expert K comes from one draw
+    over all experts, so every rank agrees on it."""
+    hi = n_experts if hi is None else hi
+    ks = np.random.default_rng(seed).choice(np.asarray(k_choices), size=n_experts, p=k_probs)
+    pack = MoEPack(hidden, inter, codebook)
+    for e in range(lo, hi):
+        rng = np.random.default_rng([seed, e])
+        K = int(ks[e])
+        pack.experts.append({
+            "gate": make_projection(rng, hidden, inter, K, codebook),
+            "up": make_projection(rng, hidden, inter, K, codebook),
+            "down": make_projection(rng, inter, hidden, K, codebook),
+        })
+    return pack
+
+
 def softmax_topk(rng: np.random.Generator, tokens: int, n_experts: int, topk: int,
                  sigma: float = 1.0):
     logits = rng.normal(0.0, sigma, size=(tokens, n_experts)).astype(np.float32)
