@@ -451,7 +451,7 @@ def run_ep(args, rank, local_rank, world, which):
     kbits = [e["gate"].K for e in pack.experts]
     layer = moe.layer_from_pack(pack, dev)
     del pack
-    ep = Exl3ExpertParallel(layer, E_, combine_dtype=torch.bfloat16, capacity=Tr)
+    ep = Exl3ExpertParallel(layer, E_, capacity=Tr)
     NB = 4 if which == "decode" else 2
     batches, local_routes, local_experts = [], [], []
     for b in range(NB):
@@ -579,7 +579,7 @@ def run_ep(args, rank, local_rank, world, which):
         "value": Tt * args.steps / (total_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
         "scaling": scaling, "vs_baseline": None,
-        "dtype": "fp16 MMA, fp32 accumulate (int trellis decode); bf16 exchange", "data": "synthetic",
+        "dtype": "fp16 MMA, fp32 accumulate (int trellis decode); bf16 rows out, fp32 partials back", "data": "synthetic",
         "config": {"workload": f"{c['name']}, T={Tt} tokens/step ({Tr} per rank)", "experts": E_,
                    "experts_per_rank": epr, "topk": k, "hidden": H_, "intermediate": I_,
                    "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single, fixed capacity %d rows/rank" % Tr,

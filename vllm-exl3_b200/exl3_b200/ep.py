@@ -88,8 +88,9 @@ class Exl3ExpertParallel(torch.nn.Module):
     :class:`exl3_b200.moe.Exl3RoutedExperts`, no expert_map); ``forward``
     takes this rank's tokens with GLOBAL expert ids and returns their full
     routed output, like the single-GPU layer.  ``combine_dtype`` is the dtype
-    partial rows travel in (bf16 halves the return traffic; fp32 keeps the
-    local sums exact).
+    partial rows travel in: fp32 (default) keeps each rank's partial sum
+    exact; bf16 halves the return traffic at the cost of one bf16 rounding
+    per partial (about one bf16 ulp of the output).
 
     ``capacity`` (rows, >= the tokens any rank passes in one call, the same
     on every rank) switches to fixed per-rank blocks: the exchanges become
@@ -99,7 +100,7 @@ class Exl3ExpertParallel(torch.nn.Module):
     pairs, with one host synchronisation per step for the split sizes.
     """
 
-    def __init__(self, local_layer, n_global: int, group=None, combine_dtype: torch.dtype = torch.bfloat16,
+    def __init__(self, local_layer, n_global: int, group=None, combine_dtype: torch.dtype = torch.float32,
                  ops=None, capacity: int | None = None):
         super().__init__()
         self.layer = local_layer
