@@ -22,6 +22,21 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def _run_ranks(worker, world: int, cfg: dict, timeout: float) -> list:
+    """Spawn `world` ranks of `worker` and collect their results.  The queue is
+    drained before the join: a child whose queued result is larger than the
+    pipe buffer cannot exit until the parent reads it."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = mp.start_processes(worker, args=(world, _free_port(), cfg, q), nprocs=world, join=False,
+                               start_method="spawn")
+    out = [q.get(timeout=timeout) for _ in range(world)]
+    while not procs.join(timeout=timeout):
+        pass
+    return out
+
+
 def _close(got: np.ndarray, want: np.ndarray, rel: float = 2e-2, cos_min: float = 0.9995) -> None:
     rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
     err = float(np.max(np.abs(got.astype(np.float64) - want)))
@@ -36,19 +51,12 @@ def _close(got: np.ndarray, want: np.ndarray, rel: float = 2e-2, cos_min: float 
 # ---------------------------------------------------------------------------
 @pytest.mark.parametrize("n_valid,capacity", [(None, None), (7, None), (None, 12), (5, 16)])
 def test_ep_gloo_world2_matches_single_rank(n_valid, capacity):
-    import torch.multiprocessing as mp
     from exl3_b200 import synthetic
 
     cfg = dict(seed=11, E=8, H=256, I=128, topk=2, T=12, n_valid=n_valid, capacity=capacity)
     world = 2
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    mp.start_processes(ep_helpers.gloo_worker, args=(world, _free_port(), cfg, q), nprocs=world,
-                       join=True, start_method="spawn")
-    got = dict()
-    counts = dict()
-    for _ in range(world):
-        r, y, c = q.get(timeout=60)
+    got, counts = {}, {}
+    for r, y, c in _run_ranks(ep_helpers.gloo_worker, world, cfg, 60):
         got[r] = y
         counts[r] = c
     pack = synthetic.make_moe_pack(cfg["seed"], cfg["E"], cfg["H"], cfg["I"], synthetic.CB_MCG, (4,))
@@ -229,20 +237,12 @@ def test_ep_world1_module_matches_layer(native, cuda, cap):
 def test_ep_nccl_two_gpus(native, capacity):
     """Two ranks over NCCL on two GPUs (skipped on a one-GPU box)."""
     import torch
-    import torch.multiprocessing as mp
-    from exl3_b200 import moe, synthetic
+    from exl3_b200 import synthetic
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     cfg = dict(seed=17, E=16, H=512, I=256, topk=4, T=40, capacity=capacity)
     world = 2
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    mp.start_processes(ep_helpers.nccl_worker, args=(world, _free_port(), cfg, q), nprocs=world, join=True,
-                       start_method="spawn")
-    got = {}
-    for _ in range(world):
-        r, y, _c = q.get(timeout=120)
-        got[r] = y
+    got = {r: y for r, y, _c in _run_ranks(ep_helpers.nccl_worker, world, cfg, 120)}
     pack = synthetic.make_moe_pack(cfg["seed"], cfg["E"], cfg["H"], cfg["I"], synthetic.CB_MCG, (2, 3, 4))
     dense = ep_helpers.dense_experts(pack, 0, cfg["E"])
     rng = np.random.default_rng(cfg["seed"] + 7)

@@ -83,6 +83,19 @@ def test_prefill_gemm_path_uniform_k(native, cuda, tokens):
     _close(_run(layer, cuda, x, ids, w, dtype=torch.float32), want)
 
 
+@pytest.mark.parametrize("tokens", [512, 700])
+def test_prefill_gemm_256_row_tiles(native, cuda, tokens):
+    """>= 192 routes per expert: 256-row work tiles (two TMEM accumulators
+    sharing every decoded weight tile), including tiles whose second half is
+    partly or wholly empty."""
+    import torch
+    pack, layer, x, ids, w = _setup(cuda, "cfg2", seed=90 + tokens, tokens=tokens, n_experts=16,
+                                    hidden=512, inter=384, k_choices=(2, 3, 4), k_probs=None)
+    want = oracle.moe_eager(x, ids, w, _dense(pack))
+    _close(_run(layer, cuda, x, ids, w, dtype=torch.float32), want)
+    _close(_run(layer, cuda, x, ids, w, dtype=torch.bfloat16), want)
+
+
 def test_prefill_gemm_path_mixed_k_mul1_limit(native, cuda):
     import torch
     pack, layer, x, ids, w = _setup(cuda, "cfg3", seed=77, tokens=256, n_experts=10, hidden=384,

@@ -45,7 +45,8 @@ struct MoePlan {
     size_t smem1 = 0, smem2 = 0;
     // prefill path: tcgen05 grouped GEMM over 128-row expert tiles
     bool gemm = false;
-    int64_t t128max = 0;
+    int tile_m = 128;      // rows per GEMM work tile: 128 or 256
+    int64_t t128max = 0;   // max work tiles
     int tc_stages = 0;
     size_t tc_smem = 0;
     // offsets
@@ -122,7 +123,9 @@ cudaError_t run_ep_combine(const void* partial, int pdt, const int32_t* pair_idx
                            int hidden, const int32_t* n_valid, void* out, int odt, cudaStream_t s);
 
 int num_sms_current();
-void tc_pick_stages(int kmax, int& stages, size_t& smem);
+// stages and dynamic smem of the GEMM for mt 128-row halves per tile; false
+// if two stages do not fit at two CTAs per SM
+bool tc_pick_stages(int kmax, int mt, int& stages, size_t& smem);
 void profile_enable(bool on, long long delay_cycles);
 int profile_read(float* ms, int max_phases);
 

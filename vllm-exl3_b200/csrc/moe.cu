@@ -68,7 +68,7 @@ struct WsPtrs {
     int* cnt1;
     int* cnt2;
     int* ntiles128;
-    int4* tiles128;  // {expert, first sorted row, rows <= 128, 0}: the GEMM path's work tiles
+    int4* tiles128;  // {expert, first sorted row, rows <= tile_rows, 0}: the GEMM path's work tiles
     float* g;
     float* u;
     __half* x2;
@@ -118,6 +118,7 @@ struct PrepArgs {
     int batched;  // ids is one expert list shared by every row: route r -> ids[r % topk]
     int cnt1_n;
     int cnt2_n;
+    int tile_rows;  // GEMM path: rows per work tile (128 or 256)
     WsPtrs w;
 };
 
@@ -180,11 +181,12 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
     // padded row offsets and slot offsets
     const int per = (E + kPrepThreads - 1) / kPrepThreads;
     const int e0 = min(E, tid * per), e1 = min(E, e0 + per);
+    const int TR = a.tile_rows;
     int sp = 0, ss = 0, st = 0;
     for (int e = e0; e < e1; ++e) {
         sp += (cnt[e] + 15) & ~15;
         ss += (cnt[e] + 15) >> 4;
-        st += (cnt[e] + 127) >> 7;
+        st += (cnt[e] + TR - 1) / TR;
     }
     int tot_p, tot_s, tot_t;
     int xp = block_excl_scan(sp, &tot_p, sh32);
@@ -196,9 +198,9 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
         for (int j = 0; j < ((n + 15) >> 4); ++j)
             a.w.slots[xs + j] = make_int4(e, xp + 16 * j, min(16, n - 16 * j), 0);
         if (a.w.tiles128)
-            for (int j = 0; j < ((n + 127) >> 7); ++j)
-                a.w.tiles128[xt + j] = make_int4(e, xp + 128 * j, min(128, n - 128 * j), 0);
-        xt += (n + 127) >> 7;
+            for (int j = 0; j < (n + TR - 1) / TR; ++j)
+                a.w.tiles128[xt + j] = make_int4(e, xp + TR * j, min(TR, n - TR * j), 0);
+        xt += (n + TR - 1) / TR;
         for (int q = xp + n; q < xp + ((n + 15) & ~15); ++q) {
             a.w.sorted_tok[q] = -1;
             a.w.sorted_route[q] = -1;
@@ -338,48 +340,87 @@ __global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a) {
     }
 }
 
-// GEMM path: one warp per (sorted row, projection), all 128-blocks of the row,
-// lanes holding 4 consecutive features; output fp16 row-major [proj][row][in].
+// Four consecutive activations as float; VEC = one 8- or 16-byte load.
+template <int XDT, bool VEC>
+__device__ __forceinline__ void load_x4(const void* x, int64_t i, float (&v)[4]) {
+    if constexpr (VEC && XDT == DT_F32) {
+        const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + i);
+        v[0] = f.x, v[1] = f.y, v[2] = f.z, v[3] = f.w;
+    } else if constexpr (VEC && XDT == DT_F16) {
+        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + i);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+        v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+    } else if constexpr (VEC && XDT == DT_BF16) {
+        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + i);
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+    } else {
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = load_as_float(x, i + k, XDT);
+    }
+}
+
+// GEMM path: one warp per sorted row; the row is read once and rotated for
+// every projection (gate and up have their own suh); lanes hold 4
+// consecutive features; output fp16 row-major [proj][row][in].
+template <int XDT, bool VEC>
 __global__ void __launch_bounds__(256) rotate_rows_kernel(const RotArgs a, const int* __restrict__ sorted_exp) {
     const int lane = threadIdx.x & 31;
     const int nkb = a.in_f / 128;
-    const int64_t total = min(int64_t(a.nslots[1]), int64_t(a.rpad)) * a.nproj;  // rows in use only
-    for (int64_t it = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; it < total;
-         it += (int64_t(gridDim.x) * blockDim.x) >> 5) {
-        const int64_t p = it / a.nproj;
-        const int pj = int(it % a.nproj);
+    const int64_t nrows = min(int64_t(a.nslots[1]), int64_t(a.rpad));  // rows in use only
+    for (int64_t p = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; p < nrows;
+         p += (int64_t(gridDim.x) * blockDim.x) >> 5) {
         const int tok = a.sorted_tok[p];
         if (tok < 0) continue;  // padding row
-        const __half* suh = a.prerotated ? nullptr : proj_suh(a.proj[pj], sorted_exp[p]);
-        if (suh == nullptr && !a.prerotated) {
-            if (lane == 0) set_status(a.status, DEV_NULL_PTR);
-            continue;
+        const __half* suh[2] = {nullptr, nullptr};
+        if (!a.prerotated) {
+            const int e = sorted_exp[p];
+            bool bad = false;
+            for (int pj = 0; pj < a.nproj; ++pj) {
+                suh[pj] = proj_suh(a.proj[pj], e);
+                bad = bad || suh[pj] == nullptr;
+            }
+            if (bad) {
+                if (lane == 0) set_status(a.status, DEV_NULL_PTR);
+                continue;
+            }
         }
         const int64_t xrow = int64_t(tok) * a.in_f;
-        __half* dst = a.xr + (int64_t(pj) * a.rpad + p) * a.in_f;
-        #pragma unroll 4
+        #pragma unroll 2
         for (int kb = 0; kb < nkb; ++kb) {
             const int c0 = kb * 128 + 4 * lane;
-            float v[4];
+            float xv[4];
+            load_x4<XDT, VEC>(a.x, xrow + c0, xv);
             #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                v[i] = __half2float(__float2half_rn(load_as_float(a.x, xrow + c0 + i, a.x_dtype)));
-            if (!a.prerotated) {
-                // suh comes from the caller's tables: only 2-byte alignment is guaranteed
-                #pragma unroll
-                for (int i = 0; i < 4; ++i) v[i] *= __half2float(suh[c0 + i]);
-                fwht128_warp_contig(v, lane);
-                #pragma unroll
-                for (int i = 0; i < 4; ++i) v[i] *= kHadNorm;
+            for (int i = 0; i < 4; ++i) xv[i] = __half2float(__float2half_rn(xv[i]));
+            for (int pj = 0; pj < a.nproj; ++pj) {
+                float v[4] = {xv[0], xv[1], xv[2], xv[3]};
+                if (!a.prerotated) {
+                    // suh comes from the caller's tables: only 2-byte alignment is guaranteed
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) v[i] *= __half2float(suh[pj][c0 + i]);
+                    fwht128_warp_contig(v, lane);
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) v[i] *= kHadNorm;
+                }
+                const __half2 h01 = __floats2half2_rn(v[0], v[1]);
+                const __half2 h23 = __floats2half2_rn(v[2], v[3]);
+                uint2 o;
+                o.x = *reinterpret_cast<const uint32_t*>(&h01);
+                o.y = *reinterpret_cast<const uint32_t*>(&h23);
+                *reinterpret_cast<uint2*>(a.xr + (int64_t(pj) * a.rpad + p) * a.in_f + c0) = o;
             }
-            const __half2 h01 = __floats2half2_rn(v[0], v[1]);
-            const __half2 h23 = __floats2half2_rn(v[2], v[3]);
-            uint2 o;
-            o.x = *reinterpret_cast<const uint32_t*>(&h01);
-            o.y = *reinterpret_cast<const uint32_t*>(&h23);
-            *reinterpret_cast<uint2*>(dst + c0) = o;
         }
     }
+}
+
+template <int XDT>
+static void launch_rotate_rows(const RotArgs& ra, const int* sorted_exp, int grid, cudaStream_t s) {
+    const bool vec = (reinterpret_cast<uintptr_t>(ra.x) & 15) == 0;
+    if (vec) rotate_rows_kernel<XDT, true><<<grid, 256, 0, s>>>(ra, sorted_exp);
+    else rotate_rows_kernel<XDT, false><<<grid, 256, 0, s>>>(ra, sorted_exp);
 }
 
 // ---------------------------------------------------------------------------
@@ -897,10 +938,14 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     }
 
     // prefill-sized batches (>= 32 rows per active expert on average) take the
-    // tcgen05 GEMM path, which decodes each weight tile once per 128 rows
+    // tcgen05 GEMM path, which decodes each weight tile once per work tile of
+    // 128 rows -- or of 256 rows (two accumulators sharing every decoded
+    // tile) once experts average >= 192 rows and two such stages fit
     p.gemm = allow_gemm && p.routes >= 32 * act_max;
-    p.t128max = p.routes / 128 + act_max + 1;
-    tc_pick_stages(kmax, p.tc_stages, p.tc_smem);
+    p.tile_m = 128;
+    if (p.routes >= 192 * act_max && tc_pick_stages(kmax, 2, p.tc_stages, p.tc_smem)) p.tile_m = 256;
+    else tc_pick_stages(kmax, 1, p.tc_stages, p.tc_smem);
+    p.t128max = p.routes / p.tile_m + act_max + 1;
 
     size_t o = 0;
     auto take = [&](size_t bytes) {
@@ -922,7 +967,7 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     if (p.gemm) {
         p.off_xr = take(size_t(nproj1) * p.rpad * hidden * 2);
         p.off_g = take(linear ? 0 : size_t(p.rpad) * inter * 4);
-        p.off_u = take(linear ? 0 : size_t(p.rpad) * inter * 4);
+        p.off_u = take(0);
         p.off_x2 = take(linear ? 0 : size_t(p.rpad) * inter * 2);
         p.off_yd = take(linear ? 0 : size_t(p.rpad) * hidden * 4);
         p.off_a2 = p.off_part1 = p.off_part2 = take(0);
@@ -1029,7 +1074,7 @@ static cudaError_t run_moe_gemm(const MoePlan& p, const MoeCall& c, const WsPtrs
         t.epi = TC_EPI_LINEAR;
         t.y = c.out;
         t.y_dtype = c.out_dtype;
-        e = run_tc_gemm(c.cb, t, w.xr, p.rpad, p.t128max * t.ncb, p.tc_smem, s);
+        e = run_tc_gemm(c.cb, p.tile_m / 128, t, w.xr, p.rpad, p.t128max * t.ncb, p.tc_smem, s);
         prof_mark(s);
         return e;
     }
@@ -1040,37 +1085,29 @@ static cudaError_t run_moe_gemm(const MoePlan& p, const MoeCall& c, const WsPtrs
     t.epi = TC_EPI_ROWS;
     t.proj = c.gate;
     t.yrows = w.g;
-    if ((e = run_tc_gemm(c.cb, t, w.xr, p.rpad, p.t128max * t.ncb, p.tc_smem, s)) != cudaSuccess) return e;
+    const int mt = p.tile_m / 128;
+    if ((e = run_tc_gemm(c.cb, mt, t, w.xr, p.rpad, p.t128max * t.ncb, p.tc_smem, s)) != cudaSuccess) return e;
+    // up, fused with SwiGLU and the down input rotation (reads the gate rows)
     t.proj = c.up;
-    t.yrows = w.u;
-    if ((e = run_tc_gemm(c.cb, t, w.xr + size_t(p.rpad) * p.hidden, p.rpad, p.t128max * t.ncb, p.tc_smem, s)) !=
-        cudaSuccess)
+    t.epi = TC_EPI_UPACT;
+    t.g_rows = w.g;
+    t.x2 = w.x2;
+    t.down = c.down;
+    t.limit = c.limit;
+    t.act = c.act;
+    t.sorted_exp = w.sorted_exp;
+    if ((e = run_tc_gemm(c.cb, mt, t, w.xr + size_t(p.rpad) * p.hidden, p.rpad, p.t128max * t.ncb, p.tc_smem,
+                         s)) != cudaSuccess)
         return e;
     prof_mark(s);
-    ActArgs aa{};
-    aa.g = w.g;
-    aa.u = w.u;
-    aa.x2 = w.x2;
-    aa.down = c.down;
-    aa.ntiles = w.ntiles128;
-    aa.tiles = w.tiles128;
-    aa.inter = p.inter;
-    aa.limit = c.limit;
-    aa.act = c.act;
-    aa.status = w.status;
-    aa.rpad = p.rpad;
-    aa.nrows = w.nslots + 1;
-    aa.sorted_tok = w.sorted_tok;
-    aa.sorted_exp = w.sorted_exp;
-    if ((e = run_tc_act(aa, nsm * 8, s)) != cudaSuccess) return e;
-    prof_mark(s);
+    prof_mark(s);  // the activation phase is part of the up launch
     t.proj = c.down;
     t.in_f = p.inter;
     t.out_f = p.hidden;
     t.ncb = p.hidden / 128;
     t.epi = TC_EPI_DOWN;
     t.yrows = w.yd;
-    if ((e = run_tc_gemm(c.cb, t, w.x2, p.rpad, p.t128max * t.ncb, p.tc_smem, s)) != cudaSuccess) return e;
+    if ((e = run_tc_gemm(c.cb, mt, t, w.x2, p.rpad, p.t128max * t.ncb, p.tc_smem, s)) != cudaSuccess) return e;
     prof_mark(s);
     const int64_t total = p.t_max * (p.hidden / 4);
     const int64_t blocks = std::min<int64_t>((total + 255) / 256, int64_t(nsm) * 16);
@@ -1104,6 +1141,7 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     pa.batched = c.batched ? 1 : 0;
     pa.cnt1_n = p.gemm ? 0 : int(p.smax * p.ncb1);
     pa.cnt2_n = (p.linear || p.gemm) ? 0 : int(p.smax * p.ncb2);
+    pa.tile_rows = p.tile_m;
     pa.w = w;
     prof_begin(s);
     prep_kernel<<<1, kPrepThreads, 0, s>>>(pa);
@@ -1126,7 +1164,11 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     ra.status = w.status;
     ra.prerotated = c.prerotated ? 1 : 0;
     ra.rowmajor = p.gemm ? 1 : 0;
-    if (p.gemm) rotate_rows_kernel<<<nsm * 8, 256, 0, s>>>(ra, w.sorted_exp);
+    if (p.gemm) {
+        if (c.x_dtype == DT_F32) launch_rotate_rows<DT_F32>(ra, w.sorted_exp, nsm * 8, s);
+        else if (c.x_dtype == DT_F16) launch_rotate_rows<DT_F16>(ra, w.sorted_exp, nsm * 8, s);
+        else launch_rotate_rows<DT_BF16>(ra, w.sorted_exp, nsm * 8, s);
+    }
     else rotate_kernel<<<nsm * 8, 256, 0, s>>>(ra);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     prof_mark(s);

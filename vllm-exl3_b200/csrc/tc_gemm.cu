@@ -1,6 +1,8 @@
 // tc_gemm.cu -- routed grouped GEMM for prefill-sized batches on sm_100a:
 // tcgen05 tensor cores with TMEM accumulators, TMA-fed activations and
-// weights decoded from the trellis into shared memory.
+// weights decoded from the trellis into shared memory.  The up projection's
+// epilogue also applies the activation and the down projection's input
+// rotation, so gate/up never make a second round trip through HBM.
 //
 // Replaces the reference's prefill tiers: ExLlamaV3 exl3_moe / exl3_moe_mixedk
 // (expert-batched, src/vllm_exl3/exl3.py:3275-3579) and the fat-expert tier
@@ -44,9 +46,11 @@ constexpr int kTcKt = kTcK / 16;            // k-tiles per stage
 constexpr int kTcABytes = kTcM * kTcK * 2;  // 16 KB
 constexpr int kTcBBytes = kTcN * kTcK * 2;  // 16 KB
 
+// Stage layout: mt activation halves of 128 rows (16 KB each, one TMA box
+// apiece), the decoded 128 x 64 weight tile (16 KB), the raw trellis words.
 __host__ __device__ inline size_t tc_raw_bytes(int kmax) { return size_t(kTcKt) * 256 * kmax; }
-__host__ __device__ inline size_t tc_stage_bytes(int kmax) {
-    return (size_t(kTcABytes + kTcBBytes) + tc_raw_bytes(kmax) + 1023) & ~size_t(1023);
+__host__ __device__ inline size_t tc_stage_bytes(int kmax, int mt) {
+    return (size_t(mt) * kTcABytes + kTcBBytes + tc_raw_bytes(kmax) + 1023) & ~size_t(1023);
 }
 
 template <int K, int CB>
@@ -90,13 +94,17 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* sta
 
 constexpr int kTcEpiPitch = 129;  // fp32 pitch of the epilogue tile (conflict-free row and column sweeps)
 
-template <int CB>
+// MT = 128-row halves per work tile: with MT = 2 one decoded weight tile
+// feeds two M128 MMAs (two TMEM accumulators), halving the decode per FLOP.
+template <int CB, int MT>
 __global__ void __launch_bounds__(kTcThreads, 2)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ TcArgs a) {
     extern __shared__ __align__(1024) char tc_smem_raw[];
     char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = a.stages;
-    const size_t stage_bytes = tc_stage_bytes(a.kmax);
+    const size_t stage_bytes = tc_stage_bytes(a.kmax, MT);
+    constexpr int kBOff = MT * kTcABytes;             // decoded weight tile
+    constexpr int kRawOff = MT * kTcABytes + kTcBBytes;  // raw trellis words
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(S) * stage_bytes);
     uint64_t* dec = full + S;
     uint64_t* empty = dec + S;
@@ -115,6 +123,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
     const bool ok = K >= 2 && K <= a.kmax && trellis != nullptr && (reinterpret_cast<uintptr_t>(trellis) & 15) == 0;
     const int nst = a.in_f / kTcK;
     const int ntiles_out = a.out_f / 16;
+    const int nh = (MT == 2 && rows > 128) ? 2 : 1;  // halves holding rows (CTA-uniform)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -128,7 +137,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
         if (!ok) set_status(a.status, K < 2 || K > a.kmax ? DEV_BAD_K : (trellis ? DEV_BAD_ALIGN : DEV_NULL_PTR));
         mbar_fence_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, kTcN);
+    if (warp == 1) tmem_alloc(tmem_slot, kTcN * MT);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -142,14 +151,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                 if (!tc_wait(&empty[s], ph ^ 1u, a.status, abort_flag)) break;
                 char* st = smem + size_t(s) * stage_bytes;
                 const uint32_t rawb = ok ? uint32_t(kTcKt * 256 * K) : 0u;
-                mbar_arrive_expect_tx(&full[s], uint32_t(kTcABytes) + rawb);
-                tma_load_2d(st, &amap, ks * kTcK, p0, &full[s]);
+                mbar_arrive_expect_tx(&full[s], uint32_t(nh * kTcABytes) + rawb);
+                for (int h = 0; h < nh; ++h) tma_load_2d(st + h * kTcABytes, &amap, ks * kTcK, p0 + 128 * h, &full[s]);
                 if (ok) {
                     const int tw = 16 * K;
                     for (int kk = 0; kk < kTcKt; ++kk) {
                         const uint16_t* src =
                             trellis + (int64_t(ks * kTcKt + kk) * ntiles_out + int64_t(cb) * 8) * tw;
-                        bulk_g2s(st + kTcABytes + kTcBBytes + size_t(kk) * 256 * K, src, uint32_t(256 * K), &full[s]);
+                        bulk_g2s(st + kRawOff + size_t(kk) * 256 * K, src, uint32_t(256 * K), &full[s]);
                     }
                 }
             }
@@ -164,11 +173,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                 if (!tc_wait(&dec[s], ph, a.status, abort_flag)) break;
                 tc_fence_after();
                 const uint32_t abase = smem_u32(smem + size_t(s) * stage_bytes);
-                const uint32_t bbase = abase + kTcABytes;
+                const uint32_t bbase = abase + kBOff;
                 #pragma unroll
                 for (int k4 = 0; k4 < kTcK / 16; ++k4) {
-                    umma_f16(taddr, umma_desc_k_sw128(abase + 32 * k4), umma_desc_k_sw128(bbase + 32 * k4), idesc,
-                             (ks | k4) != 0);
+                    const uint64_t bdesc = umma_desc_k_sw128(bbase + 32 * k4);
+                    for (int h = 0; h < nh; ++h)
+                        umma_f16(taddr + uint32_t(kTcN * h), umma_desc_k_sw128(abase + h * kTcABytes + 32 * k4), bdesc,
+                                 idesc, (ks | k4) != 0);
                 }
                 umma_commit(&empty[s]);
             }
@@ -181,9 +192,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
             const uint32_t ph = uint32_t(ks / S) & 1u;
             const bool landed = tc_wait(&full[s], ph, a.status, abort_flag);
             char* st = smem + size_t(s) * stage_bytes;
-            char* bsm = st + kTcABytes;
+            char* bsm = st + kBOff;
             if (landed && ok) {
-                tc_decode_slice_k<CB>(K, st + kTcABytes + kTcBBytes, bsm, d, lane);
+                tc_decode_slice_k<CB>(K, st + kRawOff, bsm, d, lane);
             } else {
                 // zero weights: the MMA then adds nothing for this stage
                 for (int i = lane; i < 16 * kTcK / 2; i += 32) {
@@ -197,108 +208,92 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
         }
 
         // ---------------------------- epilogue ----------------------------
-        // the stage memory is free once every MMA has completed (accf)
+        // the stage memory is free once every MMA has completed (accf); one
+        // 128-row half at a time goes TMEM -> smem tile -> FWHT -> rows
         float* ep = reinterpret_cast<float*>(smem);  // [128][kTcEpiPitch]
-        if (warp < 6) {
-            // on an abort still wait (bounded) for issued MMAs before TMEM is read or freed
-            if (!tc_wait(accf, 0u, a.status, abort_flag)) mbar_wait(accf, 0u, a.status);
-            tc_fence_after();
-            const int q = warp & 3;  // TMEM lane quarter this warp may access
-            const int row = 32 * q + lane;
-            #pragma unroll 1
-            for (int c4 = 0; c4 < 4; ++c4) {
-                float part[32];
-                tmem_ld32(taddr + (uint32_t(32 * q) << 16) + uint32_t(32 * c4), part);
-                #pragma unroll
-                for (int i = 0; i < 32; ++i) ep[row * kTcEpiPitch + 32 * c4 + i] = part[i];
-            }
-            tc_fence_before();
-        }
-        named_bar_sync(1, 8 * 32);
         const __half* svh = proj_svh(a.proj, e) + cb * 128;
         float sv[4];
         #pragma unroll
         for (int i = 0; i < 4; ++i) sv[i] = __half2float(svh[lane + 32 * i]) * kHadNorm;
-        for (int r = d; r < rows; r += 8) {
-            float x[4];
-            #pragma unroll
-            for (int i = 0; i < 4; ++i) x[i] = ep[r * kTcEpiPitch + lane + 32 * i];
-            fwht128_warp(x, lane);
-            const int64_t p = p0 + r;
-            float wmul = 1.f;
-            if (a.epi == TC_EPI_DOWN) wmul = a.sorted_w[p];
-            #pragma unroll
-            for (int i = 0; i < 4; ++i) x[i] *= sv[i] * wmul;
-            if (a.epi == TC_EPI_LINEAR) {
-                const int tok = a.sorted_tok[p];
-                if (tok < 0) continue;
-                if (a.scatter_idx) {
-                    // one route per destination row per call: plain read-modify-write
-                    float* dst = static_cast<float*>(a.y) + a.scatter_idx[tok] * a.out_f + cb * 128;
-                    const float w = __half2float(a.scatter_w[tok]);
-                    #pragma unroll
-                    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] += w * x[i];
-                } else {
-                    #pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        store_from_float(a.y, int64_t(tok) * a.out_f + cb * 128 + lane + 32 * i, a.y_dtype, x[i]);
+        for (int h = 0; h < nh; ++h) {
+            if (warp < 6) {
+                if (h == 0) {
+                    // on an abort still wait (bounded) for issued MMAs before TMEM is read or freed
+                    if (!tc_wait(accf, 0u, a.status, abort_flag)) mbar_wait(accf, 0u, a.status);
+                    tc_fence_after();
                 }
-            } else {
-                float* dst = a.yrows + p * a.out_f + cb * 128;
-                #pragma unroll
-                for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = x[i];
+                const int q = warp & 3;  // TMEM lane quarter this warp may access
+                const int row = 32 * q + lane;
+                #pragma unroll 1
+                for (int c4 = 0; c4 < 4; ++c4) {
+                    float part[32];
+                    tmem_ld32(taddr + (uint32_t(32 * q) << 16) + uint32_t(kTcN * h + 32 * c4), part);
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) ep[row * kTcEpiPitch + 32 * c4 + i] = part[i];
+                }
+                tc_fence_before();
             }
+            named_bar_sync(1, 8 * 32);
+            const int rows_h = min(128, rows - 128 * h);
+            for (int r = d; r < rows_h; r += 8) {
+                float x[4];
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) x[i] = ep[r * kTcEpiPitch + lane + 32 * i];
+                fwht128_warp(x, lane);
+                const int64_t p = p0 + 128 * h + r;
+                float wmul = 1.f;
+                if (a.epi == TC_EPI_DOWN) wmul = a.sorted_w[p];
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) x[i] *= sv[i] * wmul;
+                if (a.epi == TC_EPI_LINEAR) {
+                    const int tok = a.sorted_tok[p];
+                    if (tok < 0) continue;
+                    if (a.scatter_idx) {
+                        // one route per destination row per call: plain read-modify-write
+                        float* dst = static_cast<float*>(a.y) + a.scatter_idx[tok] * a.out_f + cb * 128;
+                        const float w = __half2float(a.scatter_w[tok]);
+                        #pragma unroll
+                        for (int i = 0; i < 4; ++i) dst[lane + 32 * i] += w * x[i];
+                    } else {
+                        #pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            store_from_float(a.y, int64_t(tok) * a.out_f + cb * 128 + lane + 32 * i, a.y_dtype, x[i]);
+                    }
+                } else if (a.epi == TC_EPI_UPACT) {
+                    // x = up; SwiGLU (+clamp) with the gate row, fp16 like the
+                    // reference's act.half(), o suh_down, the down input's
+                    // 128-point rotation (this column block is one Hadamard block)
+                    const float* gr = a.g_rows + p * a.out_f + cb * 128;
+                    const __half* su = proj_suh(a.down, a.sorted_exp[p]);
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        float g = gr[lane + 32 * i], u = x[i];
+                        if (a.limit > 0.f) {
+                            g = fminf(g, a.limit);
+                            u = fminf(fmaxf(u, -a.limit), a.limit);
+                        }
+                        const float act = a.act == 3 ? (u + 1.0f) * g / (1.0f + expf(-1.702f * g))
+                                                     : g / (1.0f + expf(-g)) * u;
+                        x[i] = __half2float(__float2half_rn(act)) *
+                               (su ? __half2float(su[cb * 128 + lane + 32 * i]) : 0.f);
+                    }
+                    fwht128_warp(x, lane);
+                    __half* dst = a.x2 + p * a.out_f + cb * 128;
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2half_rn(x[i] * kHadNorm);
+                } else {
+                    float* dst = a.yrows + p * a.out_f + cb * 128;
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = x[i];
+                }
+            }
+            if (h + 1 < nh) named_bar_sync(1, 8 * 32);  // the tile is refilled with the next half
         }
     }
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(taddr, kTcN);
-    }
-}
-
-// gate/up rows -> SwiGLU (+clamp) -> fp16 -> o suh_down -> H128/sqrt128 ->
-// fp16 row-major down input; one warp per (tile row, 128-block)
-__global__ void __launch_bounds__(256) tc_act_kernel(const ActArgs a) {
-    // one warp per sorted row, lanes holding 4 consecutive features
-    const int lane = threadIdx.x & 31;
-    const int nkb = a.inter / 128;
-    const int64_t nrows = min(int64_t(*a.nrows), int64_t(a.rpad));  // rows past it are stale
-    for (int64_t p = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; p < nrows;
-         p += (int64_t(gridDim.x) * blockDim.x) >> 5) {
-        if (a.sorted_tok[p] < 0) continue;  // padding row
-        const int64_t eid = a.sorted_exp[p];
-        const __half* suh = reinterpret_cast<const __half*>(a.down.suh_tbl ? a.down.suh_tbl[eid] : 0);
-        const float* gr = a.g + p * a.inter;
-        const float* ur = a.u + p * a.inter;
-        __half* dst = a.x2 + p * a.inter;
-        #pragma unroll 2
-        for (int kb = 0; kb < nkb; ++kb) {
-            const int c0 = kb * 128 + 4 * lane;
-            const float4 g4 = *reinterpret_cast<const float4*>(gr + c0);
-            const float4 u4 = *reinterpret_cast<const float4*>(ur + c0);
-            const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
-            float x[4];
-            #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float g = gv[i], u = uv[i];
-                if (a.limit > 0.f) {
-                    g = fminf(g, a.limit);
-                    u = fminf(fmaxf(u, -a.limit), a.limit);
-                }
-                float act;
-                if (a.act == 3) act = (u + 1.0f) * g / (1.0f + expf(-1.702f * g));
-                else act = g / (1.0f + expf(-g)) * u;
-                x[i] = __half2float(__float2half_rn(act)) * (suh ? __half2float(suh[c0 + i]) : 0.f);
-            }
-            fwht128_warp_contig(x, lane);
-            const __half2 h01 = __floats2half2_rn(x[0] * kHadNorm, x[1] * kHadNorm);
-            const __half2 h23 = __floats2half2_rn(x[2] * kHadNorm, x[3] * kHadNorm);
-            uint2 o;
-            o.x = *reinterpret_cast<const uint32_t*>(&h01);
-            o.y = *reinterpret_cast<const uint32_t*>(&h23);
-            *reinterpret_cast<uint2*>(dst + c0) = o;
-        }
+        tmem_dealloc(taddr, kTcN * MT);
     }
 }
 
@@ -336,27 +331,34 @@ static cudaError_t make_act_map(CUtensorMap* m, const void* base, int64_t rows, 
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-void tc_pick_stages(int kmax, int& stages, size_t& smem) {
+bool tc_pick_stages(int kmax, int mt, int& stages, size_t& smem) {
     // two CTAs per SM; the epilogue tile [128][129] fp32 reuses the stages
     const size_t budget = (228 * 1024) / 2 - 1024 /* per-CTA reserve */ - 1024 /* alignment */ - 256;
-    const size_t sb = tc_stage_bytes(kmax);
-    int s = int(std::min<size_t>(6, budget / sb));
-    if (s < 2) s = 2;
+    const size_t sb = tc_stage_bytes(kmax, mt);
     const size_t epi = size_t(128) * kTcEpiPitch * 4;
+    int s = int(std::min<size_t>(6, budget / sb));
     if (size_t(s) * sb < epi) s = int((epi + sb - 1) / sb);
+    if (s < 2 || size_t(s) * sb > budget) return false;
     stages = s;
     smem = size_t(s) * sb + 1024 + 256;
+    return true;
 }
 
-cudaError_t run_tc_gemm(int cb, const TcArgs& a, const void* act, int64_t act_rows, int64_t grid,
+cudaError_t run_tc_gemm(int cb, int mt, const TcArgs& a, const void* act, int64_t act_rows, int64_t grid,
                         size_t smem, cudaStream_t s) {
     CUtensorMap map;
     cudaError_t e = make_act_map(&map, act, act_rows, a.in_f);
     if (e != cudaSuccess) return e;
     void (*kern)(CUtensorMap, TcArgs);
-    if (cb == CB_MCG) kern = tc_gemm_kernel<CB_MCG>;
-    else if (cb == CB_MUL1) kern = tc_gemm_kernel<CB_MUL1>;
-    else kern = tc_gemm_kernel<CB_3INST>;
+    if (mt == 2) {
+        if (cb == CB_MCG) kern = tc_gemm_kernel<CB_MCG, 2>;
+        else if (cb == CB_MUL1) kern = tc_gemm_kernel<CB_MUL1, 2>;
+        else kern = tc_gemm_kernel<CB_3INST, 2>;
+    } else {
+        if (cb == CB_MCG) kern = tc_gemm_kernel<CB_MCG, 1>;
+        else if (cb == CB_MUL1) kern = tc_gemm_kernel<CB_MUL1, 1>;
+        else kern = tc_gemm_kernel<CB_3INST, 1>;
+    }
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
     if (grid <= 0) return cudaSuccess;
@@ -364,9 +366,5 @@ cudaError_t run_tc_gemm(int cb, const TcArgs& a, const void* act, int64_t act_ro
     return cudaGetLastError();
 }
 
-cudaError_t run_tc_act(const ActArgs& a, int grid, cudaStream_t s) {
-    tc_act_kernel<<<grid, 256, 0, s>>>(a);
-    return cudaGetLastError();
-}
 
 }  // namespace exl3

@@ -8,14 +8,18 @@
 
 namespace exl3 {
 
-enum TcEpi : int { TC_EPI_ROWS = 0, TC_EPI_DOWN = 1, TC_EPI_LINEAR = 2 };
+// epilogues: ROWS = fp32 rows; DOWN = fp32 rows x route weight; LINEAR =
+// the caller's dtype per token (or weighted scatter); UPACT = the up
+// projection fused with the activation: reads the gate rows, writes the
+// fp16 down input H128(act o suh_down)/sqrt128
+enum TcEpi : int { TC_EPI_ROWS = 0, TC_EPI_DOWN = 1, TC_EPI_LINEAR = 2, TC_EPI_UPACT = 3 };
 
 struct TcArgs {
     int* status;
     ProjRef proj;
     int in_f, out_f, ncb, kmax, stages;
     const int* ntiles;
-    const int4* tiles;  // {expert, first sorted row, rows <= 128, 0}
+    const int4* tiles;  // {expert, first sorted row, rows <= 128 * mt, 0}
     int epi;
     float* yrows;           // TC_EPI_ROWS / TC_EPI_DOWN: [rows][out_f] fp32
     const float* sorted_w;  // TC_EPI_DOWN: route weight per sorted row
@@ -24,29 +28,20 @@ struct TcArgs {
     const int* sorted_tok;
     const int64_t* scatter_idx;
     const __half* scatter_w;
-};
-
-struct ActArgs {
-    const float* g;
-    const float* u;
-    __half* x2;
-    ProjRef down;
-    const int* ntiles;
-    const int4* tiles;
-    int inter;
-    float limit;
-    int act;
-    int* status;
-    int64_t rpad;
-    const int* nrows;  // sorted rows in use (written by the prep kernel)
-    const int* sorted_tok;
+    // TC_EPI_UPACT
+    const float* g_rows;  // [rows][out_f] gate rows (after o svh)
+    __half* x2;           // [rows][out_f] fp16 down input
+    ProjRef down;         // suh of the down projection
+    float limit;          // SwiGLU clamp (0 = off)
+    int act;              // 0 SiLU, 3 SwiGLU-OAI
     const int* sorted_exp;
 };
 
-// act: fp16 row-major [act_rows][in_f] activations (TMA source); grid: upper
-// bound on tiles x column blocks (extra CTAs exit at once)
-cudaError_t run_tc_gemm(int cb, const TcArgs& a, const void* act, int64_t act_rows, int64_t grid, size_t smem,
-                        cudaStream_t s);
-cudaError_t run_tc_act(const ActArgs& a, int grid, cudaStream_t s);
+
+// act: fp16 row-major [act_rows][in_f] activations (TMA source); mt: 128-row
+// halves per work tile (1 or 2); grid: upper bound on tiles x column blocks
+// (extra CTAs exit at once)
+cudaError_t run_tc_gemm(int cb, int mt, const TcArgs& a, const void* act, int64_t act_rows, int64_t grid,
+                        size_t smem, cudaStream_t s);
 
 }  // namespace exl3

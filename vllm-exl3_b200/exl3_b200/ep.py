@@ -10,12 +10,13 @@ token exchange to vLLM's all-to-all backends.  One layer step:
    weight slots, -1 / 0 for routes owned elsewhere) are packed rank-major.
 2. ``all_to_all_single`` of the per-rank pair counts; the counts come to the
    host (the step's one synchronisation: the row exchange needs its splits).
-3. ``all_to_all_single`` of the rows, local ids and weights (NCCL over
-   NVLink; gloo on CPU in the tests).
+3. The rows, local ids and weights go to their ranks as one group of
+   point-to-point transfers (one NCCL launch over NVLink; gloo on CPU in the
+   tests).
 4. The local fused forward (``exl3_moe_forward``) over the received pairs,
    which returns one partial row per pair: that token's weighted sum over
    the routes this rank owns.
-5. ``all_to_all_single`` of the partial rows back to their sources.
+5. The partial rows go back to their sources (one more group).
 6. ``exl3_ep_combine`` (native): per-token sum over ranks in rank order --
    deterministic, no atomics.
 
@@ -149,6 +150,32 @@ class Exl3ExpertParallel(torch.nn.Module):
             return
         dist.all_to_all_single(out, inp, out_split, in_split, group=self.group)
 
+    def _exchange(self, pairs: list, s_split: list[int], r_split: list[int]) -> None:
+        """All-to-all of several (recv, send) tensor pairs as ONE group of
+        point-to-point transfers (one NCCL launch): rank q's block of each
+        send tensor goes to q, whose block of the recv tensor receives it.
+        The block to this rank itself is a local copy."""
+        so = [0] * (self.world + 1)
+        ro = [0] * (self.world + 1)
+        for g in range(self.world):
+            so[g + 1] = so[g] + s_split[g]
+            ro[g + 1] = ro[g] + r_split[g]
+        ops = []
+        for q in range(self.world):
+            peer = q if self.group is None else dist.get_global_rank(self.group, q)
+            for recv, send in pairs:
+                if q == self.rank:
+                    if s_split[q]:
+                        recv[ro[q]:ro[q + 1]].copy_(send[so[q]:so[q + 1]])
+                    continue
+                if s_split[q]:
+                    ops.append(dist.P2POp(dist.isend, send[so[q]:so[q + 1]], peer, group=self.group))
+                if r_split[q]:
+                    ops.append(dist.P2POp(dist.irecv, recv[ro[q]:ro[q + 1]], peer, group=self.group))
+        if ops:
+            for work in dist.batch_isend_irecv(ops):
+                work.wait()
+
     def forward(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
                 limit: float | None = None, n_valid: torch.Tensor | None = None,
                 out: torch.Tensor | None = None) -> torch.Tensor:
@@ -180,9 +207,7 @@ class Exl3ExpertParallel(torch.nn.Module):
             recv_x = x.new_empty(R, H)
             recv_ids = send_ids.new_empty(R, topk)
             recv_w = send_w.new_empty(R, topk)
-            self._a2a(recv_x, send_x[:S], r_split, s_split)
-            self._a2a(recv_ids, send_ids[:S], r_split, s_split)
-            self._a2a(recv_w, send_w[:S], r_split, s_split)
+            self._exchange([(recv_x, send_x), (recv_ids, send_ids), (recv_w, send_w)], s_split, r_split)
         self._mark()
         partial = self.ops.local(self.layer, recv_x, recv_ids, recv_w, self.combine_dtype, limit)
         self._mark()
@@ -190,7 +215,7 @@ class Exl3ExpertParallel(torch.nn.Module):
             back = partial
         else:
             back = partial.new_empty(max(S, 1), H)
-            self._a2a(back[:S], partial, s_split, r_split)
+            self._exchange([(back, partial)], r_split, s_split)
         self._mark()
         y = self.ops.combine(back, pair_idx, T, G, x.dtype, n_valid, out=out)
         self._mark()
@@ -213,9 +238,7 @@ class Exl3ExpertParallel(torch.nn.Module):
             recv_x = torch.empty_like(send_x)
             recv_ids = torch.empty_like(send_ids)
             recv_w = torch.empty_like(send_w)
-            dist.all_to_all_single(recv_x, send_x, group=self.group)
-            dist.all_to_all_single(recv_ids, send_ids, group=self.group)
-            dist.all_to_all_single(recv_w, send_w, group=self.group)
+            self._exchange([(recv_x, send_x), (recv_ids, send_ids), (recv_w, send_w)], [C] * G, [C] * G)
         self._mark()
         partial = self.ops.local(self.layer, recv_x, recv_ids, recv_w, self.combine_dtype, limit)
         self._mark()
@@ -223,7 +246,7 @@ class Exl3ExpertParallel(torch.nn.Module):
             back = partial
         else:
             back = torch.empty_like(partial)
-            dist.all_to_all_single(back, partial, group=self.group)
+            self._exchange([(back, partial)], [C] * G, [C] * G)
         self._mark()
         y = self.ops.combine(back, pair_idx, T, G, x.dtype, n_valid, out=out)
         self._mark()
