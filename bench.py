@@ -56,6 +56,7 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time the expert-parallel step eagerly")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep"],
                     help="decode = configs[1] (the default, reported line); prefill = configs[2]; "
                          "ep = configs[4]")
@@ -474,24 +475,58 @@ def run_ep(args, rank, local_rank, world, which):
         x, ids, w = batches[i % NB]
         ep(x, w, ids, out=out)
 
+    def max_over_ranks(v, op=None):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=op or dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # decode-sized steps are launch-bound: capture the whole EP step (dispatch,
+    # NCCL transfers, local forward, combine) in one CUDA graph; the fixed-
+    # capacity exchange has no host synchronisation, so it is capturable.
+    # Every rank must agree, so capture success is reduced over the ranks.
+    graph = None
+    sx, sid, sw = (t.clone() for t in batches[0])
+    if which == "decode" and not args.no_graph:
+        ok, why = 1.0, ""
+        try:
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    ep(sx, sw, sid, out=out)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                ep(sx, sw, sid, out=out)
+        except Exception as ex:  # capture unsupported here: time the eager step
+            ok, why, graph = 0.0, str(ex)[:200], None
+        if max_over_ranks(ok, dist.ReduceOp.MIN if world > 1 else None) < 1.0:
+            graph = None
+            if why:
+                print(f"[bench] EP graph capture failed: {why}", file=sys.stderr)
+
     def timed(n):
         evs = []
         for i in range(n):
             flush.zero_()
+            if graph is not None:
+                x, ids, w = batches[i % NB]
+                sx.copy_(x)
+                sid.copy_(ids)
+                sw.copy_(w)
             a0 = torch.cuda.Event(enable_timing=True)
             a1 = torch.cuda.Event(enable_timing=True)
             a0.record()
-            step(i)
+            if graph is not None:
+                graph.replay()
+            else:
+                step(i)
             a1.record()
             evs.append((a0, a1))
         return evs
-
-    def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
     timed(args.warmup)
     torch.cuda.synchronize(dev)
@@ -574,6 +609,9 @@ def run_ep(args, rank, local_rank, world, which):
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs))
     launches = 2 + nloc + 1
+    graph_used = graph is not None
+    del graph
+    torch.cuda.synchronize(dev)
     return {
         "metric": METRIC if which == "decode" else f"MoE layer prefill tokens/s ({c['name']})",
         "value": Tt * args.steps / (total_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -584,7 +622,8 @@ def run_ep(args, rank, local_rank, world, which):
                    "experts_per_rank": epr, "topk": k, "hidden": H_, "intermediate": I_,
                    "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single, fixed capacity %d rows/rank" % Tr,
                    "l2": "256 MB L2 flush before every step (untimed)",
-                   "timing": "CUDA events per step around the eager EP step, max over ranks"},
+                   "timing": ("CUDA events per step around one CUDA-graph replay of the EP step" if graph_used
+                              else "CUDA events per step around the eager EP step") + ", max over ranks"},
         "us_per_layer": step_s * 1e6, "phases_us": {"ep": eph, "local": lph}, "roofline": roof,
         "local_routes_per_rank": routes,
         "e2e": {"value": Tt * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",

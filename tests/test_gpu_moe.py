@@ -93,7 +93,10 @@ def test_prefill_gemm_256_row_tiles(native, cuda, tokens):
                                     hidden=512, inter=384, k_choices=(2, 3, 4), k_probs=None)
     want = oracle.moe_eager(x, ids, w, _dense(pack))
     _close(_run(layer, cuda, x, ids, w, dtype=torch.float32), want)
-    _close(_run(layer, cuda, x, ids, w, dtype=torch.bfloat16), want)
+    # bf16 activations in, fp32 rows out (a bf16 output would add half a bf16
+    # ulp of rounding, above 2e-2 RMS for the largest outputs of this shape)
+    f32 = torch.empty(x.shape[0], x.shape[1], dtype=torch.float32, device=cuda)
+    _close(_run(layer, cuda, x, ids, w, dtype=torch.bfloat16, out=f32), want)
 
 
 def test_prefill_gemm_path_mixed_k_mul1_limit(native, cuda):

@@ -125,7 +125,7 @@ int exl3_linear(const void* x, int x_dtype, int64_t m, const void* trellis, cons
     if (in_f > INT32_MAX || out_f > INT32_MAX || m * in_f > (int64_t(1) << 40))
         return fail(EXL3_ERR_ARG, "exl3_linear: dimensions exceed kernel indexing");
     exl3::MoePlan p;
-    if (!exl3::plan_moe(p, m, 1, int(in_f), int(out_f), 1, K, true, exl3::num_sms_current()))
+    if (!exl3::plan_moe(p, m, 1, int(in_f), int(out_f), 1, K, true, exl3::num_sms_current(), true, cb))
         return fail(EXL3_ERR_ARG, "exl3_linear: unsupported geometry");
     if (!ws || ws_bytes < p.total)
         return fail(EXL3_ERR_WORKSPACE, "exl3_linear: workspace of %zu bytes required (got %zu)", p.total,
@@ -195,7 +195,7 @@ int exl3_moe_forward(const void* x, int x_dtype, int64_t tokens, int64_t hidden,
     if (tokens == 0) return EXL3_OK;
     exl3::MoePlan p;
     if (!exl3::plan_moe(p, tokens, topk, int(hidden), int(inter), n_local, kmax, false,
-                        exl3::num_sms_current()))
+                        exl3::num_sms_current(), true, cb))
         return fail(EXL3_ERR_ARG, "%s: unsupported geometry", who);
     if (!ws || ws_bytes < p.total)
         return fail(EXL3_ERR_WORKSPACE, "%s: workspace of %zu bytes required (got %zu)", who, p.total,
@@ -250,7 +250,8 @@ int exl3_batched_linear(const void* x, int x_dtype, int64_t m, const int64_t* tr
     if (n_table < 1 || n_table > 2048) return fail(EXL3_ERR_ARG, "%s: table length must be in 1..2048", who);
     if (n_active < 1 || m < 1) return fail(EXL3_ERR_ARG, "%s: need m >= 1 and at least one expert", who);
     exl3::MoePlan p;
-    if (!exl3::plan_moe(p, m, n_active, int(in_f), int(out_f), n_table, K, true, exl3::num_sms_current(), false))
+    if (!exl3::plan_moe(p, m, n_active, int(in_f), int(out_f), n_table, K, true, exl3::num_sms_current(), false,
+                        cb))
         return fail(EXL3_ERR_ARG, "%s: unsupported geometry", who);
     if (!ws || ws_bytes < p.total)
         return fail(EXL3_ERR_WORKSPACE, "%s: workspace of %zu bytes required (got %zu)", who, p.total, ws_bytes);
@@ -281,7 +282,7 @@ int exl3_fat_gemm(const void* a, int64_t m, const void* packed, const void* svh,
     if (m == 0) return EXL3_OK;
     exl3::MoePlan p;
     if (in_f > INT32_MAX || out_f > INT32_MAX ||
-        !exl3::plan_moe(p, m, 1, int(in_f), int(out_f), 1, K, true, exl3::num_sms_current()))
+        !exl3::plan_moe(p, m, 1, int(in_f), int(out_f), 1, K, true, exl3::num_sms_current(), true, cb))
         return fail(EXL3_ERR_ARG, "exl3_fat_gemm: unsupported geometry");
     if (!ws || ws_bytes < p.total)
         return fail(EXL3_ERR_WORKSPACE, "exl3_fat_gemm: workspace of %zu bytes required (got %zu)", p.total,

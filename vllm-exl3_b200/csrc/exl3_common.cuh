@@ -170,6 +170,43 @@ __device__ __forceinline__ void decode_tile_afrag(const uint32_t* __restrict__ t
     a[3] = decode_pair<CB>(w[6], w[7]);
 }
 
+// MCG / 3INST hash of one 16-bit window, stopped before the final add: the
+// fp16x2 word {lo, hi} whose sum is the decoded weight.
+template <int CB>
+__device__ __forceinline__ uint32_t hash_word(uint32_t w) {
+    uint32_t x;
+    if constexpr (CB == CB_MCG) x = w * 0xCBAC1FEDu;
+    else x = w * 89226354u + 64248484u;
+    return (x & 0x8fff8fffu) ^ 0x3b603b60u;
+}
+
+// MCG / 3INST for the MMA: the lane's eight windows hashed but not summed
+// (h[j] = {lo, hi} of value j).  Multiplied against an activation duplicated
+// along K (both halves meet the same x), the tensor core forms
+// lo*x + hi*x = (lo + hi)*x exactly in its fp32 accumulation, so the integer
+// work per weight drops by the add and the fp16x2 repacking.  The weight is
+// then used unrounded; the reference rounds lo + hi to fp16 first, a
+// difference of at most half an fp16 ulp per weight.  Bit-exact fp16
+// weights remain the job of the reconstruct path.
+template <int K, int CB>
+__device__ __forceinline__ void decode_tile_words(const uint32_t* __restrict__ tile, int lane,
+                                                  uint32_t (&h)[8]) {
+    uint32_t w[8];
+    tile_windows<K>(tile, lane, w);
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] = hash_word<CB>(w[j]);
+}
+
+// Position (fp16 element) of the first of the two copies of activation k
+// (0..127) inside one 128-feature block of the duplicated layout used with
+// decode_tile_words: per 16-feature k-tile 32 elements, two halves of 16,
+// each holding k-pairs c = 0..7 for k = 2c (c < 4) or 2(c - 4) + 1 (c >= 4)
+// -- the K order in which the lane's words meet the mma.m16n8k16 A fragment.
+__device__ __forceinline__ int dup_pos(int k) {
+    const int kl = k & 15;
+    return (k >> 4) * 32 + (kl >> 3) * 16 + 2 * (((kl & 7) >> 1) + 4 * (kl & 1));
+}
+
 // Same decode, returning the eight fp16 values in j order as four fp16x2
 // registers {j0,j1}, {j2,j3}, {j4,j5}, {j6,j7}.
 template <int K, int CB>

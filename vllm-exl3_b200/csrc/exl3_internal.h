@@ -36,6 +36,7 @@ struct MoePlan {
     int n_local = 0;
     int kmax = 8;
     bool linear = false;  // one projection (dense linear, batched expert linear): no activation
+    bool dup = true;      // GEMV activations in the duplicated layout (MCG / 3INST)
     int64_t routes = 0;   // t_max * topk
     int64_t rpad = 0;     // sorted rows incl. per-expert padding to 16
     int64_t smax = 0;     // max work slots
@@ -57,9 +58,11 @@ struct MoePlan {
     size_t total = 0;
 };
 
-// Fill a plan; returns false if the geometry is unsupported.
+// Fill a plan; returns false if the geometry is unsupported.  cb is the
+// codebook of the call (its GEMV activation layout), or -1 for a size query
+// that must cover every codebook.
 bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_local, int kmax,
-              bool linear, int num_sms, bool allow_gemm = true);
+              bool linear, int num_sms, bool allow_gemm = true, int cb = -1);
 
 struct MoeCall {
     const void* x = nullptr;

@@ -48,6 +48,12 @@ constexpr int kFastRankExperts = 256;  // per-warp histogram ranking up to this 
 constexpr int kYsPitch = 132;          // fp32 pitch of the epilogue tile (conflict-free fragment stores)
 constexpr int kXPitch = 136;           // fp16 pitch of a rotated-input row (272 B: ldmatrix conflict-free)
 constexpr int kXSlice = 16 * kXPitch * 2;  // bytes of one 16-row x 128-column input slice
+// MCG / 3INST: every activation stored twice in dup_pos order (256 + 8 pad,
+// 528 B rows: still ldmatrix conflict-free), see decode_tile_words
+constexpr int kXPitchD = 264;
+constexpr int kXSliceD = 16 * kXPitchD * 2;
+__host__ __device__ constexpr int x_pitch(bool dup) { return dup ? kXPitchD : kXPitch; }
+__host__ __device__ constexpr int x_slice(bool dup) { return dup ? kXSliceD : kXSlice; }
 constexpr int kCW = 8;                 // consumer warps: one per 16-column tile of a 128-column block
 constexpr int kGemvThreads = (kCW + 1) * 32;
 
@@ -295,6 +301,7 @@ struct RotArgs {
     int* status;
     int prerotated;  // x already rotated (fp16): copy into the padded layout only
     int rowmajor;    // GEMM path: [proj][row][in] fp16, no padding
+    int dup;         // GEMV path, MCG / 3INST: duplicated layout (dup_pos)
 };
 
 
@@ -329,14 +336,20 @@ __global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a) {
             v[i] = a.prerotated ? xv : xv * __half2float(suh[c]);
         }
         __half* dst = a.rowmajor ? a.xr + (int64_t(pj) * a.rpad + p) * a.in_f + kb * 128
-                                 : a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * kXPitch;
+                                 : a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * x_pitch(a.dup);
         if (!a.prerotated) {
             fwht128_warp(v, lane);
             #pragma unroll
             for (int i = 0; i < 4; ++i) v[i] *= kHadNorm;
         }
-        #pragma unroll
-        for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2half_rn(v[i]);
+        if (a.dup) {
+            #pragma unroll
+            for (int i = 0; i < 4; ++i)
+                *reinterpret_cast<__half2*>(dst + dup_pos(lane + 32 * i)) = __half2half2(__float2half_rn(v[i]));
+        } else {
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2half_rn(v[i]);
+        }
     }
 }
 
@@ -469,8 +482,8 @@ struct GemvSmem {
 __host__ __device__ inline size_t gemv_trellis_bytes(int nproj, int kmax) {
     return size_t(nproj) * kKtPerStage * 256 * kmax;
 }
-__host__ __device__ inline size_t gemv_stage_bytes(int nproj, int kmax) {
-    return (gemv_trellis_bytes(nproj, kmax) + size_t(nproj) * kXSlice + 127) & ~size_t(127);
+__host__ __device__ inline size_t gemv_stage_bytes(int nproj, int kmax, bool dup) {
+    return (gemv_trellis_bytes(nproj, kmax) + size_t(nproj) * x_slice(dup) + 127) & ~size_t(127);
 }
 __host__ __device__ inline size_t gemv_fixed_bytes(int nproj, int stages) {
     const size_t bars = (size_t(stages) * 2 * 8 + 8 * 4 + 127) & ~size_t(127);
@@ -547,6 +560,31 @@ __device__ __forceinline__ void stage_mma(const uint32_t* __restrict__ tiles, ui
                                           bool two, float (&acc)[NP][2][4]) {
     constexpr int ROW = 64 * K;                // words per k-tile row (8 tiles of 8K words)
     constexpr int REGION = kKtPerStage * ROW;  // words per projection region
+    if constexpr (CB != CB_MUL1) {
+        // unsummed {lo, hi} words against the duplicated activations: two
+        // k16 MMAs per k-tile (k-pairs of j = 0,1,4,5 then j = 2,3,6,7)
+        #pragma unroll
+        for (int kk = 0; kk < kKtPerStage; ++kk) {
+            uint32_t h[NP][8];
+            #pragma unroll
+            for (int p = 0; p < NP; ++p) decode_tile_words<K, CB>(tiles + p * REGION + kk * ROW, lane, h[p]);
+            #pragma unroll
+            for (int p = 0; p < NP; ++p) {
+                uint32_t b[4], c[4];
+                ldmatrix_x4(b, xs + p * kXSliceD + kk * 64);
+                ldmatrix_x4(c, xs + p * kXSliceD + kk * 64 + 32);
+                const uint32_t a0[4] = {h[p][0], h[p][4], h[p][1], h[p][5]};
+                const uint32_t a1[4] = {h[p][2], h[p][6], h[p][3], h[p][7]};
+                mma_16816(acc[p][0], a0, b[0], b[1]);
+                mma_16816(acc[p][0], a1, c[0], c[1]);
+                if (two) {
+                    mma_16816(acc[p][1], a0, b[2], b[3]);
+                    mma_16816(acc[p][1], a1, c[2], c[3]);
+                }
+            }
+        }
+        return;
+    }
     #pragma unroll
     for (int kk = 0; kk < kKtPerStage; ++kk) {
         uint32_t af[NP][4];
@@ -584,9 +622,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
 gemv_kernel(const __grid_constant__ GemvArgs a) {
     constexpr int NCT = kCW * 32;
     extern __shared__ __align__(128) char smem_raw[];
+    constexpr bool DUP = CB != CB_MUL1;  // duplicated activation layout
+    constexpr int XP = x_pitch(DUP), XS = x_slice(DUP);
     const int S = a.stages;
     GemvSmem sm = gemv_smem(smem_raw, NPROJ, S);
-    const size_t stage_bytes = gemv_stage_bytes(NPROJ, a.kmax);
+    const size_t stage_bytes = gemv_stage_bytes(NPROJ, a.kmax, DUP);
     const size_t xs_off = gemv_trellis_bytes(NPROJ, a.kmax);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     volatile int* abort_flag = sm.flags;
@@ -626,7 +666,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 const uint32_t ph = (q / uint32_t(S)) & 1u;
                 if (!guarded_wait(&sm.empty[s], ph ^ 1u, a.status, abort_flag)) break;
                 char* st = sm.stages + size_t(s) * stage_bytes;
-                uint32_t bytes = NPROJ * kXSlice;
+                uint32_t bytes = NPROJ * XS;
                 #pragma unroll
                 for (int p = 0; p < NPROJ; ++p)
                     if (ok[p]) bytes += kKtPerStage * 256 * Kp[p];
@@ -647,8 +687,8 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 const int kb = kt / kKtPerStage;
                 #pragma unroll
                 for (int p = 0; p < NPROJ; ++p) {
-                    const __half* src = a.xin + ((int64_t(p) * nkb + kb) * a.rpad + I.p0) * kXPitch;
-                    bulk_g2s(st + xs_off + size_t(p) * kXSlice, src, uint32_t(kXSlice), &sm.full[s]);
+                    const __half* src = a.xin + ((int64_t(p) * nkb + kb) * a.rpad + I.p0) * XP;
+                    bulk_g2s(st + xs_off + size_t(p) * XS, src, uint32_t(XS), &sm.full[s]);
                 }
             }
         }
@@ -665,7 +705,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
     const int cw = warp;  // 16-column tile of the 128-column block
     // per-lane ldmatrix row address inside an input slice (rows padded to 272 B)
     const int brow = (lane & 7) + ((lane >> 4) << 3);
-    const uint32_t xs_lane = uint32_t(brow * kXPitch * 2 + ((lane >> 3) & 1) * 16);
+    const uint32_t xs_lane = uint32_t(brow * XP * 2 + ((lane >> 3) & 1) * 16);
     uint32_t q = 0;
     for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
         const ItemInfo I = gemv_item(a, it);
@@ -703,7 +743,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                             const uint32_t* tiles =
                                 reinterpret_cast<const uint32_t*>(st + region) + cw * 8 * Kp[p];
                             float (&accp)[1][2][4] = *reinterpret_cast<float (*)[1][2][4]>(&acc[p]);
-                            stage_mma_k<CB, 1>(Kp[p], tiles, xs + p * kXSlice, lane, two, accp);
+                            stage_mma_k<CB, 1>(Kp[p], tiles, xs + p * XS, lane, two, accp);
                             region += size_t(kKtPerStage) * 256 * Kp[p];
                         }
                     }
@@ -798,9 +838,16 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 }
                 fwht128_warp(x, lane);
                 const int64_t p = I.p0 + r;
-                __half* dst = a.a2 + (int64_t(I.cb) * a.rpad + p) * kXPitch;
-                #pragma unroll
-                for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2half_rn(x[i] * kHadNorm);
+                __half* dst = a.a2 + (int64_t(I.cb) * a.rpad + p) * XP;
+                if constexpr (DUP) {
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        *reinterpret_cast<__half2*>(dst + dup_pos(lane + 32 * i)) =
+                            __half2half2(__float2half_rn(x[i] * kHadNorm));
+                } else {
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2half_rn(x[i] * kHadNorm);
+                }
             }
         } else if constexpr (EPI == EPI_DOWN) {
             for (int r = cw; r < I.rows; r += kCW) {
@@ -886,9 +933,9 @@ combine_kernel(const int* __restrict__ route_pos, const float* __restrict__ yd, 
 static constexpr size_t kSmemPerSm = 228 * 1024;
 static constexpr int kCtasPerSm = 2;
 
-static void pick_stages(int nproj, int kmax, int& stages, size_t& smem) {
+static void pick_stages(int nproj, int kmax, bool dup, int& stages, size_t& smem) {
     const size_t per_cta = kSmemPerSm / kCtasPerSm - 1024;
-    const size_t sb = gemv_stage_bytes(nproj, kmax);
+    const size_t sb = gemv_stage_bytes(nproj, kmax, dup);
     int s = 8;
     while (s > 2 && gemv_fixed_bytes(nproj, s) + size_t(s) * sb > per_cta) --s;
     stages = s;
@@ -907,7 +954,7 @@ static void pick_split(int64_t groups_est, int grid, int nkt, int& nsplit, int& 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_local, int kmax,
-              bool linear, int num_sms, bool allow_gemm) {
+              bool linear, int num_sms, bool allow_gemm, int cb) {
     if (t_max < 1 || topk < 1 || hidden < 128 || hidden % 128 || n_local < 1 || n_local > kMaxLocal)
         return false;
     if (inter < 128 || inter % 128) return false;
@@ -927,12 +974,13 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
 
     const int grid = num_sms * kCtasPerSm;
     p.ncb1 = inter / 128;
-    pick_stages(linear ? 1 : 2, kmax, p.stages1, p.smem1);
+    p.dup = cb != CB_MUL1;  // unknown codebook (-1): size for the larger layout
+    pick_stages(linear ? 1 : 2, kmax, p.dup, p.stages1, p.smem1);
     p.grid1 = grid;
     pick_split(p.smax * p.ncb1, grid, hidden / 16, p.nsplit1, p.ktps1);
     if (!linear) {
         p.ncb2 = hidden / 128;
-        pick_stages(1, kmax, p.stages2, p.smem2);
+        pick_stages(1, kmax, p.dup, p.stages2, p.smem2);
         p.grid2 = grid;
         pick_split(act_max * p.ncb2, grid, inter / 16, p.nsplit2, p.ktps2);
     }
@@ -974,8 +1022,8 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
         p.off_cnt1 = p.off_cnt2 = take(0);
         p.nsplit1 = p.nsplit2 = 1;
     } else {
-        p.off_xr = take(size_t(nproj1) * (hidden / 128) * p.rpad * kXPitch * 2);
-        p.off_a2 = take(linear ? 0 : size_t(inter / 128) * p.rpad * kXPitch * 2);
+        p.off_xr = take(size_t(nproj1) * (hidden / 128) * p.rpad * x_pitch(p.dup) * 2);
+        p.off_a2 = take(linear ? 0 : size_t(inter / 128) * p.rpad * x_pitch(p.dup) * 2);
         p.off_yd = take(linear ? 0 : size_t(p.rpad) * hidden * 4);
         p.off_part1 = take(p.nsplit1 > 1 ? size_t(p.smax) * p.ncb1 * p.nsplit1 * kCW * nproj1 * 256 * 4 : 0);
         p.off_part2 = take(!linear && p.nsplit2 > 1 ? size_t(p.smax) * p.ncb2 * p.nsplit2 * kCW * 256 * 4 : 0);
@@ -1095,7 +1143,6 @@ static cudaError_t run_moe_gemm(const MoePlan& p, const MoeCall& c, const WsPtrs
     t.down = c.down;
     t.limit = c.limit;
     t.act = c.act;
-    t.sorted_exp = w.sorted_exp;
     if ((e = run_tc_gemm(c.cb, mt, t, w.xr + size_t(p.rpad) * p.hidden, p.rpad, p.t128max * t.ncb, p.tc_smem,
                          s)) != cudaSuccess)
         return e;
@@ -1119,6 +1166,8 @@ static cudaError_t run_moe_gemm(const MoePlan& p, const MoeCall& c, const WsPtrs
 }
 
 cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s) {
+    // the GEMV activation layout is fixed by the codebook the plan was made for
+    if (!p.gemm && p.dup != (c.cb != CB_MUL1)) return cudaErrorInvalidValue;
     WsPtrs w = ws_ptrs(p, ws);
     if (!p.gemm) {
         w.ntiles128 = nullptr;
@@ -1164,6 +1213,7 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     ra.status = w.status;
     ra.prerotated = c.prerotated ? 1 : 0;
     ra.rowmajor = p.gemm ? 1 : 0;
+    ra.dup = p.dup ? 1 : 0;
     if (p.gemm) {
         if (c.x_dtype == DT_F32) launch_rotate_rows<DT_F32>(ra, w.sorted_exp, nsm * 8, s);
         else if (c.x_dtype == DT_F16) launch_rotate_rows<DT_F16>(ra, w.sorted_exp, nsm * 8, s);

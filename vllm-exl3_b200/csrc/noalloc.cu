@@ -90,7 +90,7 @@ extern "C" int exl3_linear_noalloc(const void* x, int x_dtype, int64_t m, const 
     if (m < 0) return noalloc_fail(EXL3_ERR_ARG, "%s: m must be >= 0", who);
     if (m == 0) return EXL3_OK;
     exl3::MoePlan p;
-    if (!exl3::plan_moe(p, m, 1, int(in_f), int(out_f), 1, K, true, exl3::num_sms_current()))
+    if (!exl3::plan_moe(p, m, 1, int(in_f), int(out_f), 1, K, true, exl3::num_sms_current(), true, cb))
         return noalloc_fail(EXL3_ERR_ARG, "%s: unsupported geometry", who);
     if (p.total > size_t(EXL3_LINEAR_NOALLOC_SCRATCH_BYTES))
         return noalloc_fail(EXL3_ERR_ARG,

@@ -235,6 +235,22 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
             }
             named_bar_sync(1, 8 * 32);
             const int rows_h = min(128, rows - 128 * h);
+            // UPACT: the gate rows are read from global memory; keep two rows
+            // in flight ahead of the one being processed (latency hiding)
+            float gq[2][4];
+            float su[4] = {0.f, 0.f, 0.f, 0.f};
+            if (a.epi == TC_EPI_UPACT) {
+                const __half* sup = proj_suh(a.down, e);  // every row of the tile is expert e
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) su[i] = sup ? __half2float(sup[cb * 128 + lane + 32 * i]) : 0.f;
+                #pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int rr = d + 8 * j;
+                    const float* gr = a.g_rows + (p0 + 128 * h + rr) * int64_t(a.out_f) + cb * 128;
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) gq[j][i] = rr < rows_h ? gr[lane + 32 * i] : 0.f;
+                }
+            }
             for (int r = d; r < rows_h; r += 8) {
                 float x[4];
                 #pragma unroll
@@ -263,19 +279,27 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                     // x = up; SwiGLU (+clamp) with the gate row, fp16 like the
                     // reference's act.half(), o suh_down, the down input's
                     // 128-point rotation (this column block is one Hadamard block)
-                    const float* gr = a.g_rows + p * a.out_f + cb * 128;
-                    const __half* su = proj_suh(a.down, a.sorted_exp[p]);
+                    float gv[4];
                     #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        float g = gr[lane + 32 * i], u = x[i];
+                        gv[i] = gq[0][i];
+                        gq[0][i] = gq[1][i];
+                    }
+                    if (r + 16 < rows_h) {
+                        const float* gr = a.g_rows + (p + 16) * a.out_f + cb * 128;
+                        #pragma unroll
+                        for (int i = 0; i < 4; ++i) gq[1][i] = gr[lane + 32 * i];
+                    }
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        float g = gv[i], u = x[i];
                         if (a.limit > 0.f) {
                             g = fminf(g, a.limit);
                             u = fminf(fmaxf(u, -a.limit), a.limit);
                         }
                         const float act = a.act == 3 ? (u + 1.0f) * g / (1.0f + expf(-1.702f * g))
                                                      : g / (1.0f + expf(-g)) * u;
-                        x[i] = __half2float(__float2half_rn(act)) *
-                               (su ? __half2float(su[cb * 128 + lane + 32 * i]) : 0.f);
+                        x[i] = __half2float(__float2half_rn(act)) * su[i];
                     }
                     fwht128_warp(x, lane);
                     __half* dst = a.x2 + p * a.out_f + cb * 128;

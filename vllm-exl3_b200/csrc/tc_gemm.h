@@ -34,7 +34,6 @@ struct TcArgs {
     ProjRef down;         // suh of the down projection
     float limit;          // SwiGLU clamp (0 = off)
     int act;              // 0 SiLU, 3 SwiGLU-OAI
-    const int* sorted_exp;
 };
 
 
