@@ -18,18 +18,22 @@
 
 namespace exl3 {
 
-// K-major operand, 128-byte swizzle: 8-row atoms of 128-byte rows, atoms
-// 1024 bytes apart (SBO), LBO unused (1).  `addr` must be 1024-byte aligned
-// at the atom origin; a K offset inside the 128-byte row is added to `addr`.
-__device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_addr) {
+// K-major operand with a SWB-byte swizzle (SWB = 128: layout type 2; SWB =
+// 64: layout type 4): 8-row atoms of SWB-byte rows, atoms 8*SWB bytes apart
+// (SBO), LBO unused (1).  `addr` must be aligned to the atom (8*SWB bytes) at
+// the atom origin; a K offset inside the row is added to `addr`.
+template <int SWB>
+__device__ __forceinline__ uint64_t umma_desc_k_sw(uint32_t smem_addr) {
+    static_assert(SWB == 64 || SWB == 128, "64- or 128-byte swizzle");
     uint64_t d = 0;
     d |= uint64_t((smem_addr >> 4) & 0x3FFF);
-    d |= uint64_t(1) << 16;                  // LBO (ignored for swizzled K-major)
-    d |= uint64_t(1024 >> 4) << 32;          // SBO: 8 rows x 128 B
-    d |= uint64_t(1) << 46;                  // version 1 (sm_100)
-    d |= uint64_t(2) << 61;                  // SWIZZLE_128B
+    d |= uint64_t(1) << 16;                          // LBO (ignored for swizzled K-major)
+    d |= uint64_t((8 * SWB) >> 4) << 32;             // SBO: 8 rows x SWB bytes
+    d |= uint64_t(1) << 46;                          // version 1 (sm_100)
+    d |= uint64_t(SWB == 128 ? 2 : 4) << 61;         // SWIZZLE_128B / SWIZZLE_64B
     return d;
 }
+__device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_addr) { return umma_desc_k_sw<128>(smem_addr); }
 
 __host__ __device__ constexpr uint32_t umma_idesc_f16_f32(int M, int N) {
     return (1u << 4)                          // D = f32
@@ -98,9 +102,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
 
 // Byte offset of fp16 element (row, k) in a K-major 128-byte-swizzled tile
 // of 64-element rows (the layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B
-// and UMMA reads with layout type 2).
+// and UMMA reads with layout type 2): 16-byte chunk ^= row % 8.
 __device__ __forceinline__ uint32_t sw128_offset(int row, int k) {
     return uint32_t((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
+}
+
+// The same for 64-byte swizzled 32-element rows (CU_TENSOR_MAP_SWIZZLE_64B,
+// UMMA layout type 4): address bits 4-5 ^= bits 7-8, i.e. 16-byte chunk ^=
+// (row / 2) % 4 inside 512-byte atoms of 8 rows.
+__device__ __forceinline__ uint32_t sw64_offset(int row, int k) {
+    return uint32_t((row >> 3) * 512 + (row & 7) * 64 + ((((k >> 3) ^ (row >> 1)) & 3) << 4) + (k & 7) * 2);
 }
 
 // In-thread 128-point FWHT (strides 1..64), v in registers.

@@ -9,22 +9,24 @@
 // exl3_fat_gemm(_scatter) (csrc/exl3_fat_gemm.cu:65-305: 128x128 mma.sync
 // tiles, K4 MCG only).
 //
-// One CTA computes one 128-row x 128-column output tile of one expert
-// (rows = that expert's routes, sorted and padded by the prep kernel; columns =
-// one 128-point Hadamard block), looping over K in stages of 64:
-//   warp 0   producer: TMA 2-D load of the 128x64 activation tile (128-byte
-//            swizzle) + 1-D bulk copy of the 4 k-tile rows of compressed trellis
+// One CTA computes one work tile (128 or 256 rows of one expert; rows =
+// that expert's routes, sorted and padded by the prep kernel) x one
+// 128-column output block (= one 128-point Hadamard block), looping over K
+// in stages of 64:
+//   warp 0   producer: TMA 2-D load of the 128x64 activation box per 128-row
+//            half (128-byte swizzle) + 1-D bulk copies of the stage's four
+//            k-tile rows of compressed trellis
 //   warp 1   TMEM allocator and the single MMA-issuing thread:
-//            tcgen05.mma kind::f16 M128 N128 K16 x4 per stage, fp32 in TMEM;
-//            tcgen05.commit frees the stage
-//   warps 2-9 decoders: each decodes its 16-column slice of the stage's 4 x 8
-//            tiles in registers and stores fp16 pairs straight into the
+//            tcgen05.mma kind::f16 M128 N128 K16, four per stage and half,
+//            fp32 in TMEM; tcgen05.commit frees the stage
+//   warps 2-9 decoders: each decodes its 16-column slice of the stage's
+//            4 x 8 tiles in registers and stores fp16 pairs straight into the
 //            K-major 128-byte-swizzled layout UMMA reads (conflict-free)
-//   epilogue warps 2-5 move the accumulator (tcgen05.ld, one row per thread)
-//            into the now idle stage memory; warps 2-9 then run a warp-wide
-//            128-point FWHT per row, * 1/sqrt128 * svh, and store rows
-//            coalesced (fp32 rows, * route weight, or the caller's dtype /
-//            scatter)
+//   epilogue warps 2-5 move each 128-row accumulator half (tcgen05.ld, one
+//            row per thread) into the now idle stage memory; warps 2-9 then
+//            run a warp-wide 128-point FWHT per row, * 1/sqrt128 * svh, and
+//            store rows coalesced (fp32 rows, * route weight, the caller's
+//            dtype / scatter, or the fused SwiGLU + down-input rotation)
 // Two CTAs per SM, so one CTA's prologue/epilogue overlaps the other's main
 // loop and 16 decoder warps share the SM.  Every mbarrier wait is bounded; no
 // multicast anywhere.
@@ -41,10 +43,19 @@
 namespace exl3 {
 
 constexpr int kTcThreads = 320;
+// K per stage 64 (128-byte swizzled rows).  32-deep stages (64-byte swizzle,
+// twice as many stages in the same memory) measured slower on B200: the
+// per-stage barrier and commit overhead outweighs the deeper pipeline.
 constexpr int kTcM = 128, kTcN = 128, kTcK = 64;
 constexpr int kTcKt = kTcK / 16;            // k-tiles per stage
-constexpr int kTcABytes = kTcM * kTcK * 2;  // 16 KB
+constexpr int kTcSwB = kTcK * 2;            // swizzle span = row bytes
+constexpr int kTcABytes = kTcM * kTcK * 2;  // 16 KB per 128-row half
 constexpr int kTcBBytes = kTcN * kTcK * 2;  // 16 KB
+
+__device__ __forceinline__ uint32_t tc_b_offset(int row, int k) {
+    if constexpr (kTcSwB == 128) return sw128_offset(row, k);
+    else return sw64_offset(row, k);
+}
 
 // Stage layout: mt activation halves of 128 rows (16 KB each, one TMA box
 // apiece), the decoded 128 x 64 weight tile (16 KB), the raw trellis words.
@@ -64,10 +75,10 @@ __device__ __forceinline__ void tc_decode_slice(const char* raw, char* bsm, int 
         uint32_t v[4];
         decode_tile_pairs<K, CB>(tile, lane, v);
         const int n0 = 16 * d + g, k0 = 16 * kk + 2 * t;
-        *reinterpret_cast<uint32_t*>(bsm + sw128_offset(n0, k0)) = v[0];
-        *reinterpret_cast<uint32_t*>(bsm + sw128_offset(n0, k0 + 8)) = v[1];
-        *reinterpret_cast<uint32_t*>(bsm + sw128_offset(n0 + 8, k0)) = v[2];
-        *reinterpret_cast<uint32_t*>(bsm + sw128_offset(n0 + 8, k0 + 8)) = v[3];
+        *reinterpret_cast<uint32_t*>(bsm + tc_b_offset(n0, k0)) = v[0];
+        *reinterpret_cast<uint32_t*>(bsm + tc_b_offset(n0, k0 + 8)) = v[1];
+        *reinterpret_cast<uint32_t*>(bsm + tc_b_offset(n0 + 8, k0)) = v[2];
+        *reinterpret_cast<uint32_t*>(bsm + tc_b_offset(n0 + 8, k0 + 8)) = v[3];
     }
 }
 
@@ -176,9 +187,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                 const uint32_t bbase = abase + kBOff;
                 #pragma unroll
                 for (int k4 = 0; k4 < kTcK / 16; ++k4) {
-                    const uint64_t bdesc = umma_desc_k_sw128(bbase + 32 * k4);
+                    const uint64_t bdesc = umma_desc_k_sw<kTcSwB>(bbase + 32 * k4);
                     for (int h = 0; h < nh; ++h)
-                        umma_f16(taddr + uint32_t(kTcN * h), umma_desc_k_sw128(abase + h * kTcABytes + 32 * k4), bdesc,
+                        umma_f16(taddr + uint32_t(kTcN * h), umma_desc_k_sw<kTcSwB>(abase + h * kTcABytes + 32 * k4), bdesc,
                                  idesc, (ks | k4) != 0);
                 }
                 umma_commit(&empty[s]);
@@ -199,7 +210,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                 // zero weights: the MMA then adds nothing for this stage
                 for (int i = lane; i < 16 * kTcK / 2; i += 32) {
                     const int n = 16 * d + i / (kTcK / 2), k = 2 * (i % (kTcK / 2));
-                    *reinterpret_cast<uint32_t*>(bsm + sw128_offset(n, k)) = 0u;
+                    *reinterpret_cast<uint32_t*>(bsm + tc_b_offset(n, k)) = 0u;
                 }
             }
             fence_async_smem();
@@ -341,7 +352,7 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// fp16 row-major [rows][cols] -> 128 x 64 boxes, 128-byte swizzle
+// fp16 row-major [rows][cols] -> boxes of 128 rows x kTcK columns, kTcSwB-byte swizzle
 static cudaError_t make_act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
@@ -350,7 +361,8 @@ static cudaError_t make_act_map(CUtensorMap* m, const void* base, int64_t rows, 
     const cuuint32_t box[2] = {kTcK, kTcM};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          kTcSwB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
