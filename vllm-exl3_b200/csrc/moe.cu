@@ -615,6 +615,27 @@ __device__ __forceinline__ void stage_mma_k(int K, const uint32_t* tiles, uint32
     }
 }
 
+// A work item's stages when every projection has bit width K (the usual
+// case): returns the advanced stage counter.
+template <int K, int CB, int NP>
+__device__ __forceinline__ uint32_t gemv_same_k_loop(const GemvSmem& sm, int S, size_t stage_bytes, size_t xs_off,
+                                                     uint32_t xs_lane, int cw, int kt0, int kt1, uint32_t q, bool two,
+                                                     float (&acc)[NP][2][4], int* status, volatile int* abort_flag,
+                                                     int lane) {
+    for (int kt = kt0; kt < kt1; kt += kKtPerStage, ++q) {
+        const int s = int(q % uint32_t(S));
+        const uint32_t ph = (q / uint32_t(S)) & 1u;
+        if (guarded_wait(&sm.full[s], ph, status, abort_flag)) {
+            const char* st = sm.stages + size_t(s) * stage_bytes;
+            const uint32_t xs = smem_u32(st + xs_off) + xs_lane;
+            stage_mma<K, CB, NP>(reinterpret_cast<const uint32_t*>(st) + cw * 8 * K, xs, lane, two, acc);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[s]);
+    }
+    return q;
+}
+
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
 template <int NPROJ, int EPI, int CB>
@@ -725,17 +746,31 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
         for (int p = 0; p < NPROJ; ++p)
             #pragma unroll
             for (int i = 0; i < 8; ++i) acc[p][i >> 2][i & 3] = 0.f;
-        for (int kt = I.kt0; kt < I.kt1; kt += kKtPerStage, ++q) {
+        // the common case (every projection at one K) runs a loop specialised
+        // for that K: the switch on K happens once per item, not per stage
+        #define EXL3_GEMV_SAME(KK)                                                                           \
+            q = gemv_same_k_loop<KK, CB, NPROJ>(sm, S, stage_bytes, xs_off, xs_lane, cw, I.kt0, I.kt1, q, two, \
+                                                acc, a.status, abort_flag, lane)
+        if (same) {
+            switch (Kp[0]) {
+                case 2: EXL3_GEMV_SAME(2); break;
+                case 3: EXL3_GEMV_SAME(3); break;
+                case 4: EXL3_GEMV_SAME(4); break;
+                case 5: EXL3_GEMV_SAME(5); break;
+                case 6: EXL3_GEMV_SAME(6); break;
+                case 7: EXL3_GEMV_SAME(7); break;
+                default: EXL3_GEMV_SAME(8); break;
+            }
+        }
+        #undef EXL3_GEMV_SAME
+        for (int kt = I.kt0; !same && kt < I.kt1; kt += kKtPerStage, ++q) {
             const int s = int(q % uint32_t(S));
             const uint32_t ph = (q / uint32_t(S)) & 1u;
             const bool landed = guarded_wait(&sm.full[s], ph, a.status, abort_flag);
             if (landed) {
                 const char* st = sm.stages + size_t(s) * stage_bytes;
                 const uint32_t xs = smem_u32(st + xs_off) + xs_lane;
-                if (same) {
-                    const uint32_t* tiles = reinterpret_cast<const uint32_t*>(st) + cw * 8 * Kp[0];
-                    stage_mma_k<CB, NPROJ>(Kp[0], tiles, xs, lane, two, acc);
-                } else {
+                {
                     size_t region = 0;
                     #pragma unroll
                     for (int p = 0; p < NPROJ; ++p) {

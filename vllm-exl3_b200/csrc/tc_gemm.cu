@@ -82,25 +82,39 @@ __device__ __forceinline__ void tc_decode_slice(const char* raw, char* bsm, int 
     }
 }
 
-template <int CB>
-__device__ __forceinline__ void tc_decode_slice_k(int K, const char* raw, char* bsm, int d, int lane) {
-    switch (K) {
-        case 2: tc_decode_slice<2, CB>(raw, bsm, d, lane); break;
-        case 3: tc_decode_slice<3, CB>(raw, bsm, d, lane); break;
-        case 4: tc_decode_slice<4, CB>(raw, bsm, d, lane); break;
-        case 5: tc_decode_slice<5, CB>(raw, bsm, d, lane); break;
-        case 6: tc_decode_slice<6, CB>(raw, bsm, d, lane); break;
-        case 7: tc_decode_slice<7, CB>(raw, bsm, d, lane); break;
-        case 8: tc_decode_slice<8, CB>(raw, bsm, d, lane); break;
-        default: break;
-    }
-}
-
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* status, volatile int* abort_flag) {
     if (*abort_flag) return false;
     if (mbar_wait(bar, parity, status)) return true;
     *abort_flag = 1;
     return false;
+}
+
+// One decoder warp's whole K loop for a fixed bit width: the switch on the
+// expert's K happens once per tile, not once per stage (an indirect branch
+// per stage showed up as branch-resolve stalls).  K = 0: weights unusable,
+// every stage's slice is zeroed so the MMA adds nothing.
+template <int K, int CB>
+__device__ __noinline__ void tc_decoder_loop(char* smem, size_t stage_bytes, int S, int nst, int boff, int rawoff,
+                                             uint64_t* full, uint64_t* dec, int* status, volatile int* abort_flag,
+                                             int d, int lane) {
+    for (int ks = 0; ks < nst; ++ks) {
+        const int s = ks % S;
+        const uint32_t ph = uint32_t(ks / S) & 1u;
+        const bool landed = tc_wait(&full[s], ph, status, abort_flag);
+        char* st = smem + size_t(s) * stage_bytes;
+        char* bsm = st + boff;
+        if (K != 0 && landed) {
+            tc_decode_slice<(K != 0 ? K : 2), CB>(st + rawoff, bsm, d, lane);
+        } else {
+            for (int i = lane; i < 16 * kTcK / 2; i += 32) {
+                const int n = 16 * d + i / (kTcK / 2), k = 2 * (i % (kTcK / 2));
+                *reinterpret_cast<uint32_t*>(bsm + tc_b_offset(n, k)) = 0u;
+            }
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dec[s]);
+    }
 }
 
 constexpr int kTcEpiPitch = 129;  // fp32 pitch of the epilogue tile (conflict-free row and column sweeps)
@@ -198,25 +212,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
         }
     } else {
         const int d = warp - 2;  // 16-column tile of the 128-column block
-        for (int ks = 0; ks < nst; ++ks) {
-            const int s = ks % S;
-            const uint32_t ph = uint32_t(ks / S) & 1u;
-            const bool landed = tc_wait(&full[s], ph, a.status, abort_flag);
-            char* st = smem + size_t(s) * stage_bytes;
-            char* bsm = st + kBOff;
-            if (landed && ok) {
-                tc_decode_slice_k<CB>(K, st + kRawOff, bsm, d, lane);
-            } else {
-                // zero weights: the MMA then adds nothing for this stage
-                for (int i = lane; i < 16 * kTcK / 2; i += 32) {
-                    const int n = 16 * d + i / (kTcK / 2), k = 2 * (i % (kTcK / 2));
-                    *reinterpret_cast<uint32_t*>(bsm + tc_b_offset(n, k)) = 0u;
-                }
-            }
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&dec[s]);
+        const int kd = ok ? K : 0;
+        #define EXL3_TC_DEC(KK) \
+            tc_decoder_loop<KK, CB>(smem, stage_bytes, S, nst, kBOff, kRawOff, full, dec, a.status, abort_flag, d, lane)
+        switch (kd) {
+            case 2: EXL3_TC_DEC(2); break;
+            case 3: EXL3_TC_DEC(3); break;
+            case 4: EXL3_TC_DEC(4); break;
+            case 5: EXL3_TC_DEC(5); break;
+            case 6: EXL3_TC_DEC(6); break;
+            case 7: EXL3_TC_DEC(7); break;
+            case 8: EXL3_TC_DEC(8); break;
+            default: EXL3_TC_DEC(0); break;
         }
+        #undef EXL3_TC_DEC
 
         // ---------------------------- epilogue ----------------------------
         // the stage memory is free once every MMA has completed (accf); one
