@@ -63,9 +63,13 @@ __device__ __forceinline__ uint32_t decode_pair(uint32_t wa, uint32_t wb) {
     if constexpr (CB == CB_MUL1) {
         const uint32_t xa = wa * 0x83DCD12Du;
         const uint32_t xb = wb * 0x83DCD12Du;
-        const uint32_t sa = __dp4a(xa, 0x01010101u, 0x6400u);
-        const uint32_t sb = __dp4a(xb, 0x01010101u, 0x6400u);
-        const uint32_t s = __byte_perm(sa, sb, 0x5410);
+        // sa = {0x6400 + bytesum(xa), 0x6400}, sb = bytesum(xb) (<= 1020, no
+        // carries): s = {lo: 0x6400 + sum_a, hi: 0x6400 + sum_b}, packed by a
+        // multiply-add on the FMA pipe instead of a byte permute on the ALU
+        const uint32_t sa = __dp4a(xa, 0x01010101u, 0x64006400u);
+        const uint32_t sb = __dp4a(xb, 0x01010101u, 0u);
+        uint32_t s;
+        asm("mad.lo.u32 %0, %1, 65536, %2;" : "=r"(s) : "r"(sb), "r"(sa));
         uint32_t r;
         asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(s), "r"(0x1eee1eeeu), "r"(0xc931c931u));
         return r;

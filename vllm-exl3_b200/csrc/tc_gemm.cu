@@ -64,21 +64,45 @@ __host__ __device__ inline size_t tc_stage_bytes(int kmax, int mt) {
     return (size_t(mt) * kTcABytes + kTcBBytes + tc_raw_bytes(kmax) + 1023) & ~size_t(1023);
 }
 
+// Per-lane byte offsets of a decoder's stores into the swizzled weight tile.
+// Lane (g, t) of column tile d writes, per k-tile kk, the fp16 pairs
+// (n0, k0), (n0, k0 + 8), (n0 + 8, k0), (n0 + 8, k0 + 8) with n0 = 16d + g,
+// k0 = 16kk + 2t.  k0 >> 3 is even, so k0 + 8 only flips bit 0 of the
+// swizzled 16-byte chunk (offset ^ 16), and n0 + 8 is the next 8-row atom
+// (+ 8 * kTcSwB): two offsets per kk cover all four stores.
+struct TcStoreOffsets {
+    uint32_t a[kTcKt], b[kTcKt];  // (n0, k0) and (n0, k0 + 8)
+};
+
+__device__ __forceinline__ TcStoreOffsets tc_store_offsets(int d, int lane) {
+    TcStoreOffsets o;
+    const int n0 = 16 * d + (lane >> 2);
+    #pragma unroll
+    for (int kk = 0; kk < kTcKt; ++kk) {
+        const int k0 = 16 * kk + 2 * (lane & 3);
+        o.a[kk] = tc_b_offset(n0, k0);
+        o.b[kk] = tc_b_offset(n0, k0 + 8);
+    }
+    return o;
+}
+
 template <int K, int CB>
-__device__ __forceinline__ void tc_decode_slice(const char* raw, char* bsm, int d, int lane) {
+__device__ __forceinline__ void tc_decode_slice(const char* raw, char* bsm, int d, int lane,
+                                                const TcStoreOffsets& so) {
     // k-tiles kk of this stage, 16-column tile d: values j of lane l sit at
     // n = 16d + l/4 (+8 for j >= 4), k = 16kk + 2(l%4) (+1 for odd j, +8 for j&2)
-    const int g = lane >> 2, t = lane & 3;
+    constexpr int kAtom = 8 * kTcSwB;  // bytes of 8 rows
     #pragma unroll
     for (int kk = 0; kk < kTcKt; ++kk) {
         const uint32_t* tile = reinterpret_cast<const uint32_t*>(raw) + (kk * 8 + d) * (8 * K);
         uint32_t v[4];
         decode_tile_pairs<K, CB>(tile, lane, v);
-        const int n0 = 16 * d + g, k0 = 16 * kk + 2 * t;
-        *reinterpret_cast<uint32_t*>(bsm + tc_b_offset(n0, k0)) = v[0];
-        *reinterpret_cast<uint32_t*>(bsm + tc_b_offset(n0, k0 + 8)) = v[1];
-        *reinterpret_cast<uint32_t*>(bsm + tc_b_offset(n0 + 8, k0)) = v[2];
-        *reinterpret_cast<uint32_t*>(bsm + tc_b_offset(n0 + 8, k0 + 8)) = v[3];
+        char* pa = bsm + so.a[kk];
+        char* pb = bsm + so.b[kk];
+        *reinterpret_cast<uint32_t*>(pa) = v[0];
+        *reinterpret_cast<uint32_t*>(pb) = v[1];
+        *reinterpret_cast<uint32_t*>(pa + kAtom) = v[2];
+        *reinterpret_cast<uint32_t*>(pb + kAtom) = v[3];
     }
 }
 
@@ -97,6 +121,7 @@ template <int K, int CB>
 __device__ __noinline__ void tc_decoder_loop(char* smem, size_t stage_bytes, int S, int nst, int boff, int rawoff,
                                              uint64_t* full, uint64_t* dec, int* status, volatile int* abort_flag,
                                              int d, int lane) {
+    const TcStoreOffsets so = tc_store_offsets(d, lane);
     for (int ks = 0; ks < nst; ++ks) {
         const int s = ks % S;
         const uint32_t ph = uint32_t(ks / S) & 1u;
@@ -104,7 +129,7 @@ __device__ __noinline__ void tc_decoder_loop(char* smem, size_t stage_bytes, int
         char* st = smem + size_t(s) * stage_bytes;
         char* bsm = st + boff;
         if (K != 0 && landed) {
-            tc_decode_slice<(K != 0 ? K : 2), CB>(st + rawoff, bsm, d, lane);
+            tc_decode_slice<(K != 0 ? K : 2), CB>(st + rawoff, bsm, d, lane, so);
         } else {
             for (int i = lane; i < 16 * kTcK / 2; i += 32) {
                 const int n = 16 * d + i / (kTcK / 2), k = 2 * (i % (kTcK / 2));
