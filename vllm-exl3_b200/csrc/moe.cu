@@ -305,54 +305,6 @@ struct RotArgs {
 };
 
 
-__global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a) {
-    // one warp per (sorted row, projection, 128-block)
-    const int lane = threadIdx.x & 31;
-    const int nkb = a.in_f / 128;
-    const int64_t per_slot = int64_t(16) * a.nproj * nkb;
-    const int64_t total = int64_t(*a.nslots) * per_slot;
-    for (int64_t it = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; it < total;
-         it += (int64_t(gridDim.x) * blockDim.x) >> 5) {
-        const int64_t s = it / per_slot;
-        const int rem = int(it % per_slot);
-        const int row = rem / (a.nproj * nkb);
-        const int pj = (rem / nkb) % a.nproj;
-        const int kb = rem % nkb;
-        const int4 sl = a.slots[s];
-        if (row >= sl.z) continue;
-        const int64_t p = sl.y + row;
-        const int tok = a.sorted_tok[p];
-        const __half* suh = a.prerotated ? nullptr : proj_suh(a.proj[pj], sl.x);
-        if ((suh == nullptr && !a.prerotated) || tok < 0) {
-            if (lane == 0) set_status(a.status, tok < 0 ? DEV_BAD_ROUTE : DEV_NULL_PTR);
-            continue;
-        }
-        float v[4];
-        #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int c = kb * 128 + lane + 32 * i;
-            // the reference casts activations to fp16 first (exl3.py:2384, 2856)
-            const float xv = __half2float(__float2half_rn(load_as_float(a.x, int64_t(tok) * a.in_f + c, a.x_dtype)));
-            v[i] = a.prerotated ? xv : xv * __half2float(suh[c]);
-        }
-        __half* dst = a.rowmajor ? a.xr + (int64_t(pj) * a.rpad + p) * a.in_f + kb * 128
-                                 : a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * x_pitch(a.dup);
-        if (!a.prerotated) {
-            fwht128_warp(v, lane);
-            #pragma unroll
-            for (int i = 0; i < 4; ++i) v[i] *= kHadNorm;
-        }
-        if (a.dup) {
-            #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                *reinterpret_cast<__half2*>(dst + dup_pos(lane + 32 * i)) = __half2half2(__float2half_rn(v[i]));
-        } else {
-            #pragma unroll
-            for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2half_rn(v[i]);
-        }
-    }
-}
-
 // Four consecutive activations as float; VEC = one 8- or 16-byte load.
 template <int XDT, bool VEC>
 __device__ __forceinline__ void load_x4(const void* x, int64_t i, float (&v)[4]) {
@@ -427,6 +379,75 @@ __global__ void __launch_bounds__(256) rotate_rows_kernel(const RotArgs a, const
             }
         }
     }
+}
+
+// GEMV path: one warp per (sorted row in use, 128-block), every projection
+// from one read of the row; lanes hold 4 consecutive features; output fp16
+// [proj][in/128][row][pitch], plain or in the duplicated MMA order (dup).
+// Padding rows are left unwritten: each token row is its own MMA column,
+// so they only reach output columns that are never stored.
+template <int XDT, bool VEC>
+__global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a, const int* __restrict__ sorted_exp) {
+    const int lane = threadIdx.x & 31;
+    const int nkb = a.in_f / 128;
+    const int XPi = x_pitch(a.dup);
+    const int64_t total = min(int64_t(a.nslots[1]), int64_t(a.rpad)) * nkb;
+    for (int64_t it = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; it < total;
+         it += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+        const int64_t p = it / nkb;
+        const int kb = int(it % nkb);
+        const int tok = a.sorted_tok[p];
+        if (tok < 0) continue;  // padding row
+        const __half* suh[2] = {nullptr, nullptr};
+        if (!a.prerotated) {
+            const int e = sorted_exp[p];
+            bool bad = false;
+            for (int pj = 0; pj < a.nproj; ++pj) {
+                suh[pj] = proj_suh(a.proj[pj], e);
+                bad = bad || suh[pj] == nullptr;
+            }
+            if (bad) {
+                if (lane == 0) set_status(a.status, DEV_NULL_PTR);
+                continue;
+            }
+        }
+        const int c0 = kb * 128 + 4 * lane;
+        float xv[4];
+        // the reference casts activations to fp16 first (exl3.py:2384, 2856)
+        load_x4<XDT, VEC>(a.x, int64_t(tok) * a.in_f + c0, xv);
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) xv[i] = __half2float(__float2half_rn(xv[i]));
+        for (int pj = 0; pj < a.nproj; ++pj) {
+            float v[4] = {xv[0], xv[1], xv[2], xv[3]};
+            if (!a.prerotated) {
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] *= __half2float(suh[pj][c0 + i]);
+                fwht128_warp_contig(v, lane);
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] *= kHadNorm;
+            }
+            __half* dst = a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * XPi;
+            if (a.dup) {
+                #pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    *reinterpret_cast<__half2*>(dst + dup_pos(4 * lane + i)) = __half2half2(__float2half_rn(v[i]));
+            } else {
+                const __half2 h01 = __floats2half2_rn(v[0], v[1]);
+                const __half2 h23 = __floats2half2_rn(v[2], v[3]);
+                uint2 o;
+                o.x = *reinterpret_cast<const uint32_t*>(&h01);
+                o.y = *reinterpret_cast<const uint32_t*>(&h23);
+                *reinterpret_cast<uint2*>(dst + 4 * lane) = o;
+            }
+        }
+    }
+}
+
+template <int XDT>
+static void launch_rotate(const RotArgs& ra, const int* sorted_exp, int grid, cudaStream_t s) {
+    const bool vec = (reinterpret_cast<uintptr_t>(ra.x) & 15) == 0;
+    if (vec) rotate_kernel<XDT, true><<<grid, 256, 0, s>>>(ra, sorted_exp);
+    else rotate_kernel<XDT, false><<<grid, 256, 0, s>>>(ra, sorted_exp);
 }
 
 template <int XDT>
@@ -978,6 +999,9 @@ static void pick_stages(int nproj, int kmax, bool dup, int& stages, size_t& smem
 }
 
 static void pick_split(int64_t groups_est, int grid, int nkt, int& nsplit, int& ktps) {
+    // at least 2 waves of items.  (A 4-wave target once the groups fill a
+    // wave trims the last partial wave at T = 64 but measured slower at
+    // T = 8 and 32, where the split-K reduction costs more than the tail.)
     const int64_t target = 2 * int64_t(grid);
     int ns = 1;
     if (groups_est < target) ns = int((target + groups_est - 1) / groups_est);
@@ -1254,7 +1278,11 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
         else if (c.x_dtype == DT_F16) launch_rotate_rows<DT_F16>(ra, w.sorted_exp, nsm * 8, s);
         else launch_rotate_rows<DT_BF16>(ra, w.sorted_exp, nsm * 8, s);
     }
-    else rotate_kernel<<<nsm * 8, 256, 0, s>>>(ra);
+    else {
+        if (c.x_dtype == DT_F32) launch_rotate<DT_F32>(ra, w.sorted_exp, nsm * 8, s);
+        else if (c.x_dtype == DT_F16) launch_rotate<DT_F16>(ra, w.sorted_exp, nsm * 8, s);
+        else launch_rotate<DT_BF16>(ra, w.sorted_exp, nsm * 8, s);
+    }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     prof_mark(s);
     if (p.gemm) return run_moe_gemm(p, c, w, nsm, s);
