@@ -22,9 +22,9 @@ namespace {
 
 constexpr int kRawBytes = 4 * 256 * 8;  // four k-tile rows at K <= 8
 
-template <int K, int CB, bool FULL>
-__global__ void __launch_bounds__(256, 2) decode_slice_bench(const uint32_t* __restrict__ g, uint32_t* out,
-                                                              int iters) {
+template <int K, int CB, bool FULL, int MINB>
+__global__ void __launch_bounds__(256, MINB) decode_slice_bench(const uint32_t* __restrict__ g, uint32_t* out,
+                                                                 int iters) {
     __shared__ __align__(1024) char raw[kRawBytes];
     __shared__ __align__(1024) char bsm[16384];
     for (int i = threadIdx.x; i < kRawBytes / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(raw)[i] = g[i];
@@ -61,15 +61,15 @@ __global__ void __launch_bounds__(256, 2) decode_slice_bench(const uint32_t* __r
     out[blockIdx.x * blockDim.x + threadIdx.x] = acc;  // keeps the work live
 }
 
-template <int K, int CB, bool FULL>
+template <int K, int CB, bool FULL, int MINB = 2>
 bool run(const uint32_t* g, uint32_t* o, const char* name) {
     constexpr int kCtas = 296, kIters = 2048;
     cudaEvent_t a, b;
     cudaEventCreate(&a);
     cudaEventCreate(&b);
-    decode_slice_bench<K, CB, FULL><<<kCtas, 256>>>(g, o, 16);  // warm-up
+    decode_slice_bench<K, CB, FULL, MINB><<<kCtas, 256>>>(g, o, 16);  // warm-up
     cudaEventRecord(a);
-    decode_slice_bench<K, CB, FULL><<<kCtas, 256>>>(g, o, kIters);
+    decode_slice_bench<K, CB, FULL, MINB><<<kCtas, 256>>>(g, o, kIters);
     cudaEventRecord(b);
     if (cudaEventSynchronize(b) != cudaSuccess) return false;
     float ms = 0.f;

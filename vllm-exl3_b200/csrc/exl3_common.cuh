@@ -327,16 +327,30 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps (woken when the phase completes, or after at most the hint) instead
+// of spinning, so waiting warps leave the issue slots to the working ones.
+constexpr uint32_t kWaitSuspendNs = 1000000;  // 1 ms upper bound per try
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n .reg .pred p;\n"
-        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
         " selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitSuspendNs)
         : "memory");
     return ok != 0;
+}
+
+// Next slot of an S-deep ring; the phase parity flips on wrap-around
+// (kept incrementally so no loop divides by the runtime depth).
+__device__ __forceinline__ void ring_next(int& s, uint32_t& ph, int S) {
+    if (++s == S) {
+        s = 0;
+        ph ^= 1u;
+    }
 }
 
 // Returns false (and records the timeout) if the phase did not complete in

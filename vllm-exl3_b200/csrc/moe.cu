@@ -637,15 +637,13 @@ __device__ __forceinline__ void stage_mma_k(int K, const uint32_t* tiles, uint32
 }
 
 // A work item's stages when every projection has bit width K (the usual
-// case): returns the advanced stage counter.
+// case); advances the ring position (s, ph).
 template <int K, int CB, int NP>
-__device__ __forceinline__ uint32_t gemv_same_k_loop(const GemvSmem& sm, int S, size_t stage_bytes, size_t xs_off,
-                                                     uint32_t xs_lane, int cw, int kt0, int kt1, uint32_t q, bool two,
-                                                     float (&acc)[NP][2][4], int* status, volatile int* abort_flag,
-                                                     int lane) {
-    for (int kt = kt0; kt < kt1; kt += kKtPerStage, ++q) {
-        const int s = int(q % uint32_t(S));
-        const uint32_t ph = (q / uint32_t(S)) & 1u;
+__device__ __forceinline__ void gemv_same_k_loop(const GemvSmem& sm, int S, size_t stage_bytes, size_t xs_off,
+                                                 uint32_t xs_lane, int cw, int kt0, int kt1, int& s, uint32_t& ph,
+                                                 bool two, float (&acc)[NP][2][4], int* status,
+                                                 volatile int* abort_flag, int lane) {
+    for (int kt = kt0; kt < kt1; kt += kKtPerStage, ring_next(s, ph, S)) {
         if (guarded_wait(&sm.full[s], ph, status, abort_flag)) {
             const char* st = sm.stages + size_t(s) * stage_bytes;
             const uint32_t xs = smem_u32(st + xs_off) + xs_lane;
@@ -654,7 +652,6 @@ __device__ __forceinline__ uint32_t gemv_same_k_loop(const GemvSmem& sm, int S, 
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[s]);
     }
-    return q;
 }
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
@@ -691,7 +688,9 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
     if (warp == kCW) {
         // ------------------------------ producer ------------------------------
         if (lane != 0) return;
-        uint32_t q = 0;
+        uint32_t q = 0;   // stages issued
+        int ps = 0;       // ring slot and parity of stage q
+        uint32_t pph = 0u;
         for (int64_t it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
             const ItemInfo I = gemv_item(a, it);
             bool ok[NPROJ];
@@ -703,10 +702,9 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 Kp[p] = proj_k(a.proj[p], I.e);
                 tp[p] = proj_trellis(a.proj[p], I.e);
             }
-            for (int kt = I.kt0; kt < I.kt1; kt += kKtPerStage, ++q) {
-                const int s = int(q % uint32_t(S));
-                const uint32_t ph = (q / uint32_t(S)) & 1u;
-                if (!guarded_wait(&sm.empty[s], ph ^ 1u, a.status, abort_flag)) break;
+            for (int kt = I.kt0; kt < I.kt1; kt += kKtPerStage, ++q, ring_next(ps, pph, S)) {
+                const int s = ps;
+                if (!guarded_wait(&sm.empty[s], pph ^ 1u, a.status, abort_flag)) break;
                 char* st = sm.stages + size_t(s) * stage_bytes;
                 uint32_t bytes = NPROJ * XS;
                 #pragma unroll
@@ -748,7 +746,8 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
     // per-lane ldmatrix row address inside an input slice (rows padded to 272 B)
     const int brow = (lane & 7) + ((lane >> 4) << 3);
     const uint32_t xs_lane = uint32_t(brow * XP * 2 + ((lane >> 3) & 1) * 16);
-    uint32_t q = 0;
+    int cs = 0;  // ring slot and parity of the next stage
+    uint32_t cph = 0u;
     for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
         const ItemInfo I = gemv_item(a, it);
         bool ok[NPROJ];
@@ -770,8 +769,8 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
         // the common case (every projection at one K) runs a loop specialised
         // for that K: the switch on K happens once per item, not per stage
         #define EXL3_GEMV_SAME(KK)                                                                           \
-            q = gemv_same_k_loop<KK, CB, NPROJ>(sm, S, stage_bytes, xs_off, xs_lane, cw, I.kt0, I.kt1, q, two, \
-                                                acc, a.status, abort_flag, lane)
+            gemv_same_k_loop<KK, CB, NPROJ>(sm, S, stage_bytes, xs_off, xs_lane, cw, I.kt0, I.kt1, cs, cph, two, \
+                                            acc, a.status, abort_flag, lane)
         if (same) {
             switch (Kp[0]) {
                 case 2: EXL3_GEMV_SAME(2); break;
@@ -784,10 +783,9 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             }
         }
         #undef EXL3_GEMV_SAME
-        for (int kt = I.kt0; !same && kt < I.kt1; kt += kKtPerStage, ++q) {
-            const int s = int(q % uint32_t(S));
-            const uint32_t ph = (q / uint32_t(S)) & 1u;
-            const bool landed = guarded_wait(&sm.full[s], ph, a.status, abort_flag);
+        for (int kt = I.kt0; !same && kt < I.kt1; kt += kKtPerStage, ring_next(cs, cph, S)) {
+            const int s = cs;
+            const bool landed = guarded_wait(&sm.full[s], cph, a.status, abort_flag);
             if (landed) {
                 const char* st = sm.stages + size_t(s) * stage_bytes;
                 const uint32_t xs = smem_u32(st + xs_off) + xs_lane;

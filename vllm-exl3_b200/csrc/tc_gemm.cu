@@ -122,9 +122,9 @@ __device__ __noinline__ void tc_decoder_loop(char* smem, size_t stage_bytes, int
                                              uint64_t* full, uint64_t* dec, int* status, volatile int* abort_flag,
                                              int d, int lane) {
     const TcStoreOffsets so = tc_store_offsets(d, lane);
-    for (int ks = 0; ks < nst; ++ks) {
-        const int s = ks % S;
-        const uint32_t ph = uint32_t(ks / S) & 1u;
+    int s = 0;         // stage slot and the parity of its current use
+    uint32_t ph = 0u;
+    for (int ks = 0; ks < nst; ++ks, ring_next(s, ph, S)) {
         const bool landed = tc_wait(&full[s], ph, status, abort_flag);
         char* st = smem + size_t(s) * stage_bytes;
         char* bsm = st + boff;
@@ -195,9 +195,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
 
     if (warp == 0) {
         if (lane == 0) {
-            for (int ks = 0; ks < nst; ++ks) {
-                const int s = ks % S;
-                const uint32_t ph = uint32_t(ks / S) & 1u;
+            int s = 0;
+            uint32_t ph = 0u;
+            for (int ks = 0; ks < nst; ++ks, ring_next(s, ph, S)) {
                 if (!tc_wait(&empty[s], ph ^ 1u, a.status, abort_flag)) break;
                 char* st = smem + size_t(s) * stage_bytes;
                 const uint32_t rawb = ok ? uint32_t(kTcKt * 256 * K) : 0u;
@@ -216,9 +216,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_f16_f32(kTcM, kTcN);
-            for (int ks = 0; ks < nst; ++ks) {
-                const int s = ks % S;
-                const uint32_t ph = uint32_t(ks / S) & 1u;
+            int s = 0;
+            uint32_t ph = 0u;
+            for (int ks = 0; ks < nst; ++ks, ring_next(s, ph, S)) {
                 if (!tc_wait(&full[s], ph, a.status, abort_flag)) break;
                 if (!tc_wait(&dec[s], ph, a.status, abort_flag)) break;
                 tc_fence_after();
