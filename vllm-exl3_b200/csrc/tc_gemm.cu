@@ -118,7 +118,7 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* sta
 // per stage showed up as branch-resolve stalls).  K = 0: weights unusable,
 // every stage's slice is zeroed so the MMA adds nothing.
 template <int K, int CB>
-__device__ __noinline__ void tc_decoder_loop(char* smem, size_t stage_bytes, int S, int nst, int boff, int rawoff,
+__device__ __forceinline__ void tc_decoder_loop(char* smem, size_t stage_bytes, int S, int nst, int boff, int rawoff,
                                              uint64_t* full, uint64_t* dec, int* status, volatile int* abort_flag,
                                              int d, int lane) {
     const TcStoreOffsets so = tc_store_offsets(d, lane);
