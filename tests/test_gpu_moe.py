@@ -99,6 +99,26 @@ def test_prefill_gemm_256_row_tiles(native, cuda, tokens):
     _close(_run(layer, cuda, x, ids, w, dtype=torch.bfloat16, out=f32), want)
 
 
+@pytest.mark.parametrize("n_valid", [None, 1030])
+def test_large_batch_split_prep(native, cuda, n_valid):
+    """>= 8192 routes: the routing prep runs as chunk histograms, a one-CTA
+    layout pass and a chunked stable placement; the result must equal the
+    eager loop, including the padded n_valid rows."""
+    import torch
+    pack, layer, x, ids, w = _setup(cuda, "cfg2", seed=123, tokens=1100, n_experts=16, hidden=256,
+                                    inter=256, k_choices=(2, 3), k_probs=None)
+    want = oracle.moe_eager(x, ids, w, _dense(pack))
+    kw = {}
+    if n_valid is not None:
+        kw["n_valid"] = torch.tensor([n_valid], dtype=torch.int32, device=cuda)
+        want[n_valid:] = 0.0
+    f32 = torch.empty(x.shape[0], x.shape[1], dtype=torch.float32, device=cuda)
+    got = _run(layer, cuda, x, ids, w, dtype=torch.bfloat16, out=f32, **kw)
+    if n_valid is not None:
+        assert np.all(got[n_valid:] == 0)
+    _close(got, want)
+
+
 def test_prefill_gemm_path_mixed_k_mul1_limit(native, cuda):
     import torch
     pack, layer, x, ids, w = _setup(cuda, "cfg3", seed=77, tokens=256, n_experts=10, hidden=384,

@@ -47,6 +47,7 @@ struct MoePlan {
     // prefill path: tcgen05 grouped GEMM over 128-row expert tiles
     bool gemm = false;
     int tile_m = 128;      // rows per GEMM work tile: 128 or 256
+    int prep_chunks = 0;   // > 0: routing prep split over this many CTAs (large batches)
     int64_t t128max = 0;   // max work tiles
     int tc_stages = 0;
     size_t tc_smem = 0;
@@ -54,7 +55,7 @@ struct MoePlan {
     size_t off_status = 0, off_nslots = 0, off_slots = 0, off_route_pos = 0, off_sorted_tok = 0,
            off_sorted_route = 0, off_ntiles128 = 0, off_tiles128 = 0, off_g = 0, off_u = 0, off_x2 = 0,
            off_sorted_exp = 0, off_sorted_w = 0, off_xr = 0, off_a2 = 0, off_yd = 0,
-           off_part1 = 0, off_part2 = 0, off_cnt1 = 0, off_cnt2 = 0;
+           off_part1 = 0, off_part2 = 0, off_cnt1 = 0, off_cnt2 = 0, off_hist = 0;
     size_t total = 0;
 };
 

@@ -45,6 +45,8 @@ enum Act : int { ACT_SILU = 0, ACT_SWIGLU_OAI = 3 };
 constexpr int kPrepThreads = 1024;
 constexpr int kMaxLocal = 2048;
 constexpr int kFastRankExperts = 256;  // per-warp histogram ranking up to this many experts
+constexpr int kPrepChunk = 2048;       // routes per CTA when the prep is split over CTAs
+constexpr int64_t kPrepSplitRoutes = 4 * kPrepChunk;  // split the prep from this many routes on
 constexpr int kYsPitch = 132;          // fp32 pitch of the epilogue tile (conflict-free fragment stores)
 constexpr int kXPitch = 136;           // fp16 pitch of a rotated-input row (272 B: ldmatrix conflict-free)
 constexpr int kXSlice = 16 * kXPitch * 2;  // bytes of one 16-row x 128-column input slice
@@ -78,6 +80,7 @@ struct WsPtrs {
     float* g;
     float* u;
     __half* x2;
+    int* hist;  // split prep: [chunk][expert] counts, then first rows
 };
 
 static WsPtrs ws_ptrs(const MoePlan& p, void* ws) {
@@ -103,6 +106,7 @@ static WsPtrs ws_ptrs(const MoePlan& p, void* ws) {
     w.g = reinterpret_cast<float*>(b + p.off_g);
     w.u = reinterpret_cast<float*>(b + p.off_u);
     w.x2 = reinterpret_cast<__half*>(b + p.off_x2);
+    w.hist = reinterpret_cast<int*>(b + p.off_hist);
     return w;
 }
 
@@ -163,28 +167,20 @@ __device__ int block_excl_scan(int v, int* total, int* sh32) {
     return warp_prefix + x - v;
 }
 
-__global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
-    __shared__ int cnt[kMaxLocal];
-    __shared__ int poff[kMaxLocal];
-    __shared__ unsigned short wcnt[kPrepThreads / 32][kFastRankExperts];
-    __shared__ int sh32[32];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int E = a.n_local;
-    int64_t T = a.t_max;
-    if (a.n_valid) T = min(T, int64_t(max(0, *a.n_valid)));
-    const int64_t R = T * a.topk, Rmax = a.t_max * a.topk;
-
-    for (int i = tid; i < a.cnt1_n; i += kPrepThreads) a.w.cnt1[i] = 0;
-    for (int i = tid; i < a.cnt2_n; i += kPrepThreads) a.w.cnt2[i] = 0;
-    for (int e = tid; e < E; e += kPrepThreads) cnt[e] = 0;
-    __syncthreads();
-    for (int64_t r = tid; r < R; r += kPrepThreads) {
+// Histogram of local experts over routes [r0, r1) into shared cnt[].
+__device__ __forceinline__ void prep_histogram(const PrepArgs& a, int64_t r0, int64_t r1, int* cnt) {
+    for (int64_t r = r0 + threadIdx.x; r < r1; r += kPrepThreads) {
         const int e = local_expert(a, r);
         if (e >= 0) atomicAdd(&cnt[e], 1);
     }
-    __syncthreads();
+}
 
-    // padded row offsets and slot offsets
+// From per-expert route counts: each expert's first sorted row (rows padded
+// to 16) in poff[], the slot and work-tile tables, the padding rows and the
+// totals.  Whole CTA; ends synchronised.
+__device__ void prep_layout(const PrepArgs& a, const int* cnt, int* poff, int* sh32) {
+    const int tid = threadIdx.x;
+    const int E = a.n_local;
     const int per = (E + kPrepThreads - 1) / kPrepThreads;
     const int e0 = min(E, tid * per), e1 = min(E, e0 + per);
     const int TR = a.tile_rows;
@@ -222,44 +218,48 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
         if (a.w.ntiles128) *a.w.ntiles128 = tot_t;
     }
     __syncthreads();
-    for (int e = tid; e < E; e += kPrepThreads) cnt[e] = poff[e];  // running position (general path)
-    __syncthreads();
+}
 
-    // stable placement: route order within each expert.  Running start of
-    // each expert: poff[e] (fast path) or cnt[e] (general path).
+// Stable placement of routes [r0, r1): route order within each expert.
+// run[e] holds each expert's next sorted row and is advanced; chunk[] is
+// scratch (per-expert totals of one 1024-route step, fast path).
+__device__ void prep_place(const PrepArgs& a, int64_t r0, int64_t r1, int64_t Rmax, int* run, int* chunk,
+                           unsigned short (*wcnt)[kFastRankExperts]) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int E = a.n_local;
     const bool fast = E <= kFastRankExperts;
-    for (int64_t base = 0; base < R; base += kPrepThreads) {
+    for (int64_t base = r0; base < r1; base += kPrepThreads) {
         const int64_t r = base + tid;
-        const int e = r < R ? local_expert(a, r) : -1;
+        const int e = r < r1 ? local_expert(a, r) : -1;
         const unsigned mask = __match_any_sync(0xffffffffu, e);
         const int rank = __popc(mask & ((1u << lane) - 1u));
         const int leader = __ffs(mask) - 1;
         int p = -1;
         if (fast) {
             // per-warp counts -> exclusive prefix over warps per expert (in
-            // wcnt), chunk totals in cnt; three barriers per 1024 routes
+            // wcnt), step totals in chunk; three barriers per 1024 routes
             for (int i = tid; i < (kPrepThreads / 32) * kFastRankExperts; i += kPrepThreads)
                 (&wcnt[0][0])[i] = 0;
             __syncthreads();
             if (e >= 0 && lane == leader) wcnt[warp][e] = (unsigned short)__popc(mask);
             __syncthreads();
             for (int x = tid; x < E; x += kPrepThreads) {
-                int run = 0;
+                int acc = 0;
                 for (int w = 0; w < kPrepThreads / 32; ++w) {
                     const int c = wcnt[w][x];
-                    wcnt[w][x] = (unsigned short)run;
-                    run += c;
+                    wcnt[w][x] = (unsigned short)acc;
+                    acc += c;
                 }
-                cnt[x] = run;
+                chunk[x] = acc;
             }
             __syncthreads();
-            if (e >= 0) p = poff[e] + int(wcnt[warp][e]) + rank;
+            if (e >= 0) p = run[e] + int(wcnt[warp][e]) + rank;
         } else {
             int my_base = 0;
             for (int w = 0; w < kPrepThreads / 32; ++w) {
                 if (warp == w && e >= 0 && lane == leader) {
-                    my_base = cnt[e];
-                    cnt[e] += __popc(mask);
+                    my_base = run[e];
+                    run[e] += __popc(mask);
                 }
                 __syncthreads();
             }
@@ -272,16 +272,99 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
             a.w.sorted_route[p] = int(r);
             a.w.sorted_exp[p] = e;
             a.w.sorted_w[p] = (a.linear || a.batched) ? 1.f : load_as_float(a.weights, r, a.w_dtype);
-        } else if (r < Rmax) {
+        } else if (r < r1 && r < Rmax) {
             a.w.route_pos[r] = -1;
         }
         if (fast) {
             __syncthreads();
-            for (int x = tid; x < E; x += kPrepThreads) poff[x] += cnt[x];
+            for (int x = tid; x < E; x += kPrepThreads) run[x] += chunk[x];
             __syncthreads();
         }
     }
+}
+
+__device__ __forceinline__ int64_t prep_routes(const PrepArgs& a) {
+    int64_t T = a.t_max;
+    if (a.n_valid) T = min(T, int64_t(max(0, *a.n_valid)));
+    return T * a.topk;
+}
+
+// Small batches: the whole prep in one CTA.
+__global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
+    __shared__ int cnt[kMaxLocal];
+    __shared__ int poff[kMaxLocal];
+    __shared__ unsigned short wcnt[kPrepThreads / 32][kFastRankExperts];
+    __shared__ int sh32[32];
+    const int tid = threadIdx.x;
+    const int E = a.n_local;
+    const int64_t R = prep_routes(a), Rmax = a.t_max * a.topk;
+
+    for (int i = tid; i < a.cnt1_n; i += kPrepThreads) a.w.cnt1[i] = 0;
+    for (int i = tid; i < a.cnt2_n; i += kPrepThreads) a.w.cnt2[i] = 0;
+    for (int e = tid; e < E; e += kPrepThreads) cnt[e] = 0;
+    __syncthreads();
+    prep_histogram(a, 0, R, cnt);
+    __syncthreads();
+    prep_layout(a, cnt, poff, sh32);
+    for (int e = tid; e < E; e += kPrepThreads) cnt[e] = poff[e];  // running positions
+    __syncthreads();
+    prep_place(a, 0, R, Rmax, cnt, poff, wcnt);
     for (int64_t r = R + tid; r < Rmax; r += kPrepThreads) a.w.route_pos[r] = -1;
+}
+
+// Large batches: the same prep split over chunks of kPrepChunk routes.
+// 1. per-chunk expert histograms hist[chunk][expert]
+__global__ void __launch_bounds__(kPrepThreads) prep_count_kernel(const PrepArgs a) {
+    __shared__ int cnt[kMaxLocal];
+    const int E = a.n_local;
+    const int64_t R = prep_routes(a);
+    const int64_t r0 = int64_t(blockIdx.x) * kPrepChunk, r1 = min(R, r0 + kPrepChunk);
+    for (int e = threadIdx.x; e < E; e += kPrepThreads) cnt[e] = 0;
+    __syncthreads();
+    prep_histogram(a, r0, r1, cnt);
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += kPrepThreads) a.w.hist[int64_t(blockIdx.x) * E + e] = cnt[e];
+}
+
+// 2. one CTA: totals, layout, and each chunk's first row per expert (in place of its histogram)
+__global__ void __launch_bounds__(kPrepThreads) prep_plan_kernel(const PrepArgs a, int nchunks) {
+    __shared__ int cnt[kMaxLocal];
+    __shared__ int poff[kMaxLocal];
+    __shared__ int sh32[32];
+    const int tid = threadIdx.x;
+    const int E = a.n_local;
+    const int64_t R = prep_routes(a), Rmax = a.t_max * a.topk;
+    for (int i = tid; i < a.cnt1_n; i += kPrepThreads) a.w.cnt1[i] = 0;
+    for (int i = tid; i < a.cnt2_n; i += kPrepThreads) a.w.cnt2[i] = 0;
+    for (int e = tid; e < E; e += kPrepThreads) {
+        int n = 0;
+        for (int c = 0; c < nchunks; ++c) n += a.w.hist[int64_t(c) * E + e];
+        cnt[e] = n;
+    }
+    __syncthreads();
+    prep_layout(a, cnt, poff, sh32);
+    for (int e = tid; e < E; e += kPrepThreads) {
+        int run = poff[e];
+        for (int c = 0; c < nchunks; ++c) {
+            const int v = a.w.hist[int64_t(c) * E + e];
+            a.w.hist[int64_t(c) * E + e] = run;
+            run += v;
+        }
+    }
+    for (int64_t r = R + tid; r < Rmax; r += kPrepThreads) a.w.route_pos[r] = -1;
+}
+
+// 3. per chunk: stable placement from the chunk's first rows
+__global__ void __launch_bounds__(kPrepThreads) prep_place_kernel(const PrepArgs a) {
+    __shared__ int run[kMaxLocal];
+    __shared__ int chunk[kMaxLocal];
+    __shared__ unsigned short wcnt[kPrepThreads / 32][kFastRankExperts];
+    const int E = a.n_local;
+    const int64_t R = prep_routes(a), Rmax = a.t_max * a.topk;
+    const int64_t r0 = int64_t(blockIdx.x) * kPrepChunk, r1 = min(R, r0 + kPrepChunk);
+    for (int e = threadIdx.x; e < E; e += kPrepThreads) run[e] = a.w.hist[int64_t(blockIdx.x) * E + e];
+    __syncthreads();
+    prep_place(a, r0, r1, Rmax, run, chunk, wcnt);
 }
 
 // ---------------------------------------------------------------------------
@@ -305,156 +388,159 @@ struct RotArgs {
 };
 
 
-// Four consecutive activations as float; VEC = one 8- or 16-byte load.
+// Two consecutive activations (even index) as fp16x2, rounded like the
+// reference's cast of the activations to fp16 (exl3.py:2384, 2856).
 template <int XDT, bool VEC>
-__device__ __forceinline__ void load_x4(const void* x, int64_t i, float (&v)[4]) {
-    if constexpr (VEC && XDT == DT_F32) {
-        const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + i);
-        v[0] = f.x, v[1] = f.y, v[2] = f.z, v[3] = f.w;
-    } else if constexpr (VEC && XDT == DT_F16) {
-        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + i);
-        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-        v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
-    } else if constexpr (VEC && XDT == DT_BF16) {
-        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + i);
-        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-        v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+__device__ __forceinline__ uint32_t load_x2_h(const void* x, int64_t i) {
+    if constexpr (VEC && XDT == DT_F16)
+        return *reinterpret_cast<const uint32_t*>(static_cast<const __half*>(x) + i);
+    __half2 h;
+    if constexpr (VEC && XDT == DT_BF16) {
+        const uint32_t u = *reinterpret_cast<const uint32_t*>(static_cast<const uint16_t*>(x) + i);
+        h = __float22half2_rn(__bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u)));
+    } else if constexpr (VEC && XDT == DT_F32) {
+        h = __float22half2_rn(*reinterpret_cast<const float2*>(static_cast<const float*>(x) + i));
     } else {
+        h = __floats2half2_rn(load_as_float(x, i, XDT), load_as_float(x, i + 1, XDT));
+    }
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Input rotation on tensor cores: H128 = H8 (x) H16, so one warp rotates 16 sorted
+// rows x one 128-block as (a) eight mma.m16n8k16 of the fp16 rows' 16-feature
+// blocks against diag(suh_block) H16 (exact +-suh operands, fp32
+// accumulation: the strides 1..8 of the transform) and (b) an 8-point
+// butterfly across the eight blocks held in each thread's accumulators (the
+// strides 16, 32, 64) -- no shuffles.  Rows are grouped 16 at a time from a
+// 16-aligned start, so a group never straddles two experts (each expert's
+// rows are padded to 16); padding rows enter as zeros and are not stored.
+// Output: GEMM path (rowmajor) fp16 [proj][row][in]; GEMV path fp16
+// [proj][in/128][row][pitch], each feature stored twice in the dup_pos
+// order for MCG / 3INST (dup).
+__device__ __forceinline__ void rot_store2(__half* row, int f, bool dup, float v0, float v1) {
+    if (dup) {
+        *reinterpret_cast<__half2*>(row + dup_pos(f)) = __half2half2(__float2half_rn(v0));
+        *reinterpret_cast<__half2*>(row + dup_pos(f + 1)) = __half2half2(__float2half_rn(v1));
+    } else {
+        *reinterpret_cast<__half2*>(row + f) = __floats2half2_rn(v0, v1);
+    }
+}
+
+template <int XDT, bool VEC>
+__global__ void __launch_bounds__(256, 2) rotate_rows_mma_kernel(const RotArgs a, const int* __restrict__ sorted_exp) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int nkb = a.in_f / 128;
+    const int64_t ngroups = min(int64_t(a.nslots[1]), int64_t(a.rpad)) / 16;
+    // H16 signs of this thread's B-fragment entries: rows k in {2t, 2t+1,
+    // 2t+8, 2t+9}, columns n = 8j + g
+    __half2 hs[2][2];
+    #pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int n = 8 * j + g;
         #pragma unroll
-        for (int k = 0; k < 4; ++k) v[k] = load_as_float(x, i + k, XDT);
-    }
-}
-
-// GEMM path: one warp per sorted row; the row is read once and rotated for
-// every projection (gate and up have their own suh); lanes hold 4
-// consecutive features; output fp16 row-major [proj][row][in].
-template <int XDT, bool VEC>
-__global__ void __launch_bounds__(256) rotate_rows_kernel(const RotArgs a, const int* __restrict__ sorted_exp) {
-    const int lane = threadIdx.x & 31;
-    const int nkb = a.in_f / 128;
-    const int64_t nrows = min(int64_t(a.nslots[1]), int64_t(a.rpad));  // rows in use only
-    for (int64_t p = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; p < nrows;
-         p += (int64_t(gridDim.x) * blockDim.x) >> 5) {
-        const int tok = a.sorted_tok[p];
-        if (tok < 0) continue;  // padding row
-        const __half* suh[2] = {nullptr, nullptr};
-        if (!a.prerotated) {
-            const int e = sorted_exp[p];
-            bool bad = false;
-            for (int pj = 0; pj < a.nproj; ++pj) {
-                suh[pj] = proj_suh(a.proj[pj], e);
-                bad = bad || suh[pj] == nullptr;
-            }
-            if (bad) {
-                if (lane == 0) set_status(a.status, DEV_NULL_PTR);
-                continue;
-            }
-        }
-        const int64_t xrow = int64_t(tok) * a.in_f;
-        #pragma unroll 2
-        for (int kb = 0; kb < nkb; ++kb) {
-            const int c0 = kb * 128 + 4 * lane;
-            float xv[4];
-            load_x4<XDT, VEC>(a.x, xrow + c0, xv);
-            #pragma unroll
-            for (int i = 0; i < 4; ++i) xv[i] = __half2float(__float2half_rn(xv[i]));
-            for (int pj = 0; pj < a.nproj; ++pj) {
-                float v[4] = {xv[0], xv[1], xv[2], xv[3]};
-                if (!a.prerotated) {
-                    // suh comes from the caller's tables: only 2-byte alignment is guaranteed
-                    #pragma unroll
-                    for (int i = 0; i < 4; ++i) v[i] *= __half2float(suh[pj][c0 + i]);
-                    fwht128_warp_contig(v, lane);
-                    #pragma unroll
-                    for (int i = 0; i < 4; ++i) v[i] *= kHadNorm;
-                }
-                const __half2 h01 = __floats2half2_rn(v[0], v[1]);
-                const __half2 h23 = __floats2half2_rn(v[2], v[3]);
-                uint2 o;
-                o.x = *reinterpret_cast<const uint32_t*>(&h01);
-                o.y = *reinterpret_cast<const uint32_t*>(&h23);
-                *reinterpret_cast<uint2*>(a.xr + (int64_t(pj) * a.rpad + p) * a.in_f + c0) = o;
-            }
+        for (int q = 0; q < 2; ++q) {
+            const int k = 2 * t + 8 * q;
+            hs[j][q] = __floats2half2_rn((__popc(k & n) & 1) ? -1.f : 1.f, (__popc((k + 1) & n) & 1) ? -1.f : 1.f);
         }
     }
-}
-
-// GEMV path: one warp per (sorted row in use, 128-block), every projection
-// from one read of the row; lanes hold 4 consecutive features; output fp16
-// [proj][in/128][row][pitch], plain or in the duplicated MMA order (dup).
-// Padding rows are left unwritten: each token row is its own MMA column,
-// so they only reach output columns that are never stored.
-template <int XDT, bool VEC>
-__global__ void __launch_bounds__(256) rotate_kernel(const RotArgs a, const int* __restrict__ sorted_exp) {
-    const int lane = threadIdx.x & 31;
-    const int nkb = a.in_f / 128;
-    const int XPi = x_pitch(a.dup);
-    const int64_t total = min(int64_t(a.nslots[1]), int64_t(a.rpad)) * nkb;
-    for (int64_t it = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; it < total;
+    for (int64_t it = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; it < ngroups * nkb;
          it += (int64_t(gridDim.x) * blockDim.x) >> 5) {
-        const int64_t p = it / nkb;
+        const int64_t p0 = (it / nkb) * 16;
         const int kb = int(it % nkb);
-        const int tok = a.sorted_tok[p];
-        if (tok < 0) continue;  // padding row
-        const __half* suh[2] = {nullptr, nullptr};
-        if (!a.prerotated) {
-            const int e = sorted_exp[p];
-            bool bad = false;
-            for (int pj = 0; pj < a.nproj; ++pj) {
-                suh[pj] = proj_suh(a.proj[pj], e);
-                bad = bad || suh[pj] == nullptr;
-            }
-            if (bad) {
+        const int tok0 = a.sorted_tok[p0 + g], tok1 = a.sorted_tok[p0 + g + 8];
+        const int e = sorted_exp[p0];
+        uint32_t af[8][4];
+        #pragma unroll
+        for (int blk = 0; blk < 8; ++blk) {
+            const int c = kb * 128 + 16 * blk + 2 * t;
+            af[blk][0] = tok0 >= 0 ? load_x2_h<XDT, VEC>(a.x, int64_t(tok0) * a.in_f + c) : 0u;
+            af[blk][1] = tok1 >= 0 ? load_x2_h<XDT, VEC>(a.x, int64_t(tok1) * a.in_f + c) : 0u;
+            af[blk][2] = tok0 >= 0 ? load_x2_h<XDT, VEC>(a.x, int64_t(tok0) * a.in_f + c + 8) : 0u;
+            af[blk][3] = tok1 >= 0 ? load_x2_h<XDT, VEC>(a.x, int64_t(tok1) * a.in_f + c + 8) : 0u;
+        }
+        // row pointers of output block kb for projection pj (features relative to the block)
+        const int XPi = x_pitch(a.dup);
+        auto out_row = [&](int pj, int64_t p) -> __half* {
+            return a.rowmajor ? a.xr + (int64_t(pj) * a.rpad + p) * a.in_f + kb * 128
+                              : a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * XPi;
+        };
+        const bool dup = !a.rowmajor && a.dup;
+        if (a.prerotated) {
+            // input already rotated (the fat GEMM's contract): copy the fp16 rows
+            __half* out0 = out_row(0, p0 + g);
+            __half* out1 = out_row(0, p0 + g + 8);
+            #pragma unroll
+            for (int blk = 0; blk < 8; ++blk)
+                #pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const int f = 16 * blk + 8 * q + 2 * t;
+                    if (tok0 >= 0) {
+                        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&af[blk][2 * q]));
+                        rot_store2(out0, f, dup, v.x, v.y);
+                    }
+                    if (tok1 >= 0) {
+                        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&af[blk][2 * q + 1]));
+                        rot_store2(out1, f, dup, v.x, v.y);
+                    }
+                }
+            continue;
+        }
+        for (int pj = 0; pj < a.nproj; ++pj) {
+            const __half* suh = proj_suh(a.proj[pj], e);
+            if (suh == nullptr) {
                 if (lane == 0) set_status(a.status, DEV_NULL_PTR);
                 continue;
             }
-        }
-        const int c0 = kb * 128 + 4 * lane;
-        float xv[4];
-        // the reference casts activations to fp16 first (exl3.py:2384, 2856)
-        load_x4<XDT, VEC>(a.x, int64_t(tok) * a.in_f + c0, xv);
-        #pragma unroll
-        for (int i = 0; i < 4; ++i) xv[i] = __half2float(__float2half_rn(xv[i]));
-        for (int pj = 0; pj < a.nproj; ++pj) {
-            float v[4] = {xv[0], xv[1], xv[2], xv[3]};
-            if (!a.prerotated) {
+            float d[8][2][4];
+            #pragma unroll
+            for (int blk = 0; blk < 8; ++blk) {
+                const int k0 = kb * 128 + 16 * blk + 2 * t;
+                // suh comes from the caller's tables: only 2-byte alignment is guaranteed
+                const __half2 s01 = __halves2half2(suh[k0], suh[k0 + 1]);
+                const __half2 s89 = __halves2half2(suh[k0 + 8], suh[k0 + 9]);
                 #pragma unroll
-                for (int i = 0; i < 4; ++i) v[i] *= __half2float(suh[pj][c0 + i]);
-                fwht128_warp_contig(v, lane);
-                #pragma unroll
-                for (int i = 0; i < 4; ++i) v[i] *= kHadNorm;
+                for (int j = 0; j < 2; ++j) {
+                    const __half2 b0 = __hmul2(s01, hs[j][0]), b1 = __hmul2(s89, hs[j][1]);
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) d[blk][j][i] = 0.f;
+                    mma_16816(d[blk][j], af[blk], *reinterpret_cast<const uint32_t*>(&b0),
+                              *reinterpret_cast<const uint32_t*>(&b1));
+                }
             }
-            __half* dst = a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * XPi;
-            if (a.dup) {
+            // strides 16, 32, 64: butterflies across the blocks, fp32
+            #pragma unroll
+            for (int st = 1; st < 8; st <<= 1)
                 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    *reinterpret_cast<__half2*>(dst + dup_pos(4 * lane + i)) = __half2half2(__float2half_rn(v[i]));
-            } else {
-                const __half2 h01 = __floats2half2_rn(v[0], v[1]);
-                const __half2 h23 = __floats2half2_rn(v[2], v[3]);
-                uint2 o;
-                o.x = *reinterpret_cast<const uint32_t*>(&h01);
-                o.y = *reinterpret_cast<const uint32_t*>(&h23);
-                *reinterpret_cast<uint2*>(dst + 4 * lane) = o;
-            }
+                for (int blk = 0; blk < 8; ++blk)
+                    if ((blk & st) == 0)
+                        #pragma unroll
+                        for (int j = 0; j < 2; ++j)
+                            #pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const float u = d[blk][j][i], v = d[blk + st][j][i];
+                                d[blk][j][i] = __fadd_rn(u, v);
+                                d[blk + st][j][i] = __fsub_rn(u, v);
+                            }
+            // D fragment (j, i): row g (i < 2) or g + 8, feature 16 blk + 8 j + 2 t + (i & 1)
+            __half* out0 = out_row(pj, p0 + g);
+            __half* out1 = out_row(pj, p0 + g + 8);
+            #pragma unroll
+            for (int blk = 0; blk < 8; ++blk)
+                #pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int f = 16 * blk + 8 * j + 2 * t;
+                    if (tok0 >= 0) rot_store2(out0, f, dup, d[blk][j][0] * kHadNorm, d[blk][j][1] * kHadNorm);
+                    if (tok1 >= 0) rot_store2(out1, f, dup, d[blk][j][2] * kHadNorm, d[blk][j][3] * kHadNorm);
+                }
         }
     }
-}
-
-template <int XDT>
-static void launch_rotate(const RotArgs& ra, const int* sorted_exp, int grid, cudaStream_t s) {
-    const bool vec = (reinterpret_cast<uintptr_t>(ra.x) & 15) == 0;
-    if (vec) rotate_kernel<XDT, true><<<grid, 256, 0, s>>>(ra, sorted_exp);
-    else rotate_kernel<XDT, false><<<grid, 256, 0, s>>>(ra, sorted_exp);
 }
 
 template <int XDT>
 static void launch_rotate_rows(const RotArgs& ra, const int* sorted_exp, int grid, cudaStream_t s) {
     const bool vec = (reinterpret_cast<uintptr_t>(ra.x) & 15) == 0;
-    if (vec) rotate_rows_kernel<XDT, true><<<grid, 256, 0, s>>>(ra, sorted_exp);
-    else rotate_rows_kernel<XDT, false><<<grid, 256, 0, s>>>(ra, sorted_exp);
+    if (vec) rotate_rows_mma_kernel<XDT, true><<<grid, 256, 0, s>>>(ra, sorted_exp);
+    else rotate_rows_mma_kernel<XDT, false><<<grid, 256, 0, s>>>(ra, sorted_exp);
 }
 
 // ---------------------------------------------------------------------------
@@ -604,19 +690,19 @@ __device__ __forceinline__ void stage_mma(const uint32_t* __restrict__ tiles, ui
                 }
             }
         }
-        return;
-    }
-    #pragma unroll
-    for (int kk = 0; kk < kKtPerStage; ++kk) {
-        uint32_t af[NP][4];
+    } else {
         #pragma unroll
-        for (int p = 0; p < NP; ++p) decode_tile_afrag<K, CB>(tiles + p * REGION + kk * ROW, lane, af[p]);
-        #pragma unroll
-        for (int p = 0; p < NP; ++p) {
-            uint32_t b[4];
-            ldmatrix_x4(b, xs + p * kXSlice + kk * 32);
-            mma_16816(acc[p][0], af[p], b[0], b[1]);
-            if (two) mma_16816(acc[p][1], af[p], b[2], b[3]);
+        for (int kk = 0; kk < kKtPerStage; ++kk) {
+            uint32_t af[NP][4];
+            #pragma unroll
+            for (int p = 0; p < NP; ++p) decode_tile_afrag<K, CB>(tiles + p * REGION + kk * ROW, lane, af[p]);
+            #pragma unroll
+            for (int p = 0; p < NP; ++p) {
+                uint32_t b[4];
+                ldmatrix_x4(b, xs + p * kXSlice + kk * 32);
+                mma_16816(acc[p][0], af[p], b[0], b[1]);
+                if (two) mma_16816(acc[p][1], af[p], b[2], b[3]);
+            }
         }
     }
 }
@@ -1067,6 +1153,8 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     p.off_sorted_exp = take(size_t(p.rpad) * 4);
     p.off_sorted_w = take(size_t(p.rpad) * 4);
     const int nproj1 = linear ? 1 : 2;
+    p.prep_chunks = p.routes >= kPrepSplitRoutes ? int((p.routes + kPrepChunk - 1) / kPrepChunk) : 0;
+    p.off_hist = take(size_t(p.prep_chunks) * n_local * 4);
     p.off_ntiles128 = take(p.gemm ? 64 : 0);
     p.off_tiles128 = take(p.gemm ? size_t(p.t128max) * 16 : 0);
     if (p.gemm) {
@@ -1250,7 +1338,13 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     pa.tile_rows = p.tile_m;
     pa.w = w;
     prof_begin(s);
-    prep_kernel<<<1, kPrepThreads, 0, s>>>(pa);
+    if (p.prep_chunks > 0) {
+        prep_count_kernel<<<p.prep_chunks, kPrepThreads, 0, s>>>(pa);
+        prep_plan_kernel<<<1, kPrepThreads, 0, s>>>(pa, p.prep_chunks);
+        prep_place_kernel<<<p.prep_chunks, kPrepThreads, 0, s>>>(pa);
+    } else {
+        prep_kernel<<<1, kPrepThreads, 0, s>>>(pa);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     prof_mark(s);
@@ -1277,9 +1371,9 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
         else launch_rotate_rows<DT_BF16>(ra, w.sorted_exp, nsm * 8, s);
     }
     else {
-        if (c.x_dtype == DT_F32) launch_rotate<DT_F32>(ra, w.sorted_exp, nsm * 8, s);
-        else if (c.x_dtype == DT_F16) launch_rotate<DT_F16>(ra, w.sorted_exp, nsm * 8, s);
-        else launch_rotate<DT_BF16>(ra, w.sorted_exp, nsm * 8, s);
+        if (c.x_dtype == DT_F32) launch_rotate_rows<DT_F32>(ra, w.sorted_exp, nsm * 8, s);
+        else if (c.x_dtype == DT_F16) launch_rotate_rows<DT_F16>(ra, w.sorted_exp, nsm * 8, s);
+        else launch_rotate_rows<DT_BF16>(ra, w.sorted_exp, nsm * 8, s);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     prof_mark(s);
