@@ -426,8 +426,10 @@ __device__ __forceinline__ void rot_store2(__half* row, int f, bool dup, float v
     }
 }
 
-template <int XDT, bool VEC>
-__global__ void __launch_bounds__(256, 2) rotate_rows_mma_kernel(const RotArgs a, const int* __restrict__ sorted_exp) {
+enum RotLayout : int { ROT_ROWMAJOR = 0, ROT_PITCH = 1, ROT_DUP = 2 };
+
+template <int XDT, bool VEC, int LAYOUT>
+__global__ void __launch_bounds__(256) rotate_rows_mma_kernel(const RotArgs a, const int* __restrict__ sorted_exp) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int nkb = a.in_f / 128;
     const int64_t ngroups = min(int64_t(a.nslots[1]), int64_t(a.rpad)) / 16;
@@ -459,12 +461,11 @@ __global__ void __launch_bounds__(256, 2) rotate_rows_mma_kernel(const RotArgs a
             af[blk][3] = tok1 >= 0 ? load_x2_h<XDT, VEC>(a.x, int64_t(tok1) * a.in_f + c + 8) : 0u;
         }
         // row pointers of output block kb for projection pj (features relative to the block)
-        const int XPi = x_pitch(a.dup);
+        constexpr bool dup = LAYOUT == ROT_DUP;
         auto out_row = [&](int pj, int64_t p) -> __half* {
-            return a.rowmajor ? a.xr + (int64_t(pj) * a.rpad + p) * a.in_f + kb * 128
-                              : a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * XPi;
+            if constexpr (LAYOUT == ROT_ROWMAJOR) return a.xr + (int64_t(pj) * a.rpad + p) * a.in_f + kb * 128;
+            else return a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * x_pitch(dup);
         };
-        const bool dup = !a.rowmajor && a.dup;
         if (a.prerotated) {
             // input already rotated (the fat GEMM's contract): copy the fp16 rows
             __half* out0 = out_row(0, p0 + g);
@@ -536,11 +537,18 @@ __global__ void __launch_bounds__(256, 2) rotate_rows_mma_kernel(const RotArgs a
     }
 }
 
+template <int XDT, int LAYOUT>
+static void launch_rotate_layout(const RotArgs& ra, const int* sorted_exp, int grid, cudaStream_t s) {
+    const bool vec = (reinterpret_cast<uintptr_t>(ra.x) & 15) == 0;
+    if (vec) rotate_rows_mma_kernel<XDT, true, LAYOUT><<<grid, 256, 0, s>>>(ra, sorted_exp);
+    else rotate_rows_mma_kernel<XDT, false, LAYOUT><<<grid, 256, 0, s>>>(ra, sorted_exp);
+}
+
 template <int XDT>
 static void launch_rotate_rows(const RotArgs& ra, const int* sorted_exp, int grid, cudaStream_t s) {
-    const bool vec = (reinterpret_cast<uintptr_t>(ra.x) & 15) == 0;
-    if (vec) rotate_rows_mma_kernel<XDT, true><<<grid, 256, 0, s>>>(ra, sorted_exp);
-    else rotate_rows_mma_kernel<XDT, false><<<grid, 256, 0, s>>>(ra, sorted_exp);
+    if (ra.rowmajor) launch_rotate_layout<XDT, ROT_ROWMAJOR>(ra, sorted_exp, grid, s);
+    else if (ra.dup) launch_rotate_layout<XDT, ROT_DUP>(ra, sorted_exp, grid, s);
+    else launch_rotate_layout<XDT, ROT_PITCH>(ra, sorted_exp, grid, s);
 }
 
 // ---------------------------------------------------------------------------
