@@ -49,7 +49,7 @@ struct MoePlan {
     int tile_m = 128;      // rows per GEMM work tile: 128 or 256
     int prep_chunks = 0;   // > 0: routing prep split over this many CTAs (large batches)
     int64_t t128max = 0;   // max work tiles
-    int tc_sa = 0, tc_sb = 0, tc_sr = 0;  // GEMM ring depths: activations, decoded weights, raw words
+    int tc_stages = 0;
     size_t tc_smem = 0;
     // offsets
     size_t off_status = 0, off_nslots = 0, off_slots = 0, off_route_pos = 0, off_sorted_tok = 0,
@@ -127,9 +127,9 @@ cudaError_t run_ep_combine(const void* partial, int pdt, const int32_t* pair_idx
                            int hidden, const int32_t* n_valid, void* out, int odt, cudaStream_t s);
 
 int num_sms_current();
-// ring depths and dynamic smem of the (one CTA per SM) GEMM for mt 128-row
-// halves per tile; false if the rings do not fit
-bool tc_pick_rings(int kmax, int mt, int& sa, int& sb, int& sr, size_t& smem);
+// stages and dynamic smem of the GEMM for mt 128-row halves per tile; false
+// if two stages do not fit at two CTAs per SM
+bool tc_pick_stages(int kmax, int mt, int& stages, size_t& smem);
 void profile_enable(bool on, long long delay_cycles);
 int profile_read(float* ms, int max_phases);
 

@@ -1142,8 +1142,8 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     // tile) once experts average >= 192 rows and two such stages fit
     p.gemm = allow_gemm && p.routes >= 32 * act_max;
     p.tile_m = 128;
-    if (p.routes >= 192 * act_max && tc_pick_rings(kmax, 2, p.tc_sa, p.tc_sb, p.tc_sr, p.tc_smem)) p.tile_m = 256;
-    else tc_pick_rings(kmax, 1, p.tc_sa, p.tc_sb, p.tc_sr, p.tc_smem);
+    if (p.routes >= 192 * act_max && tc_pick_stages(kmax, 2, p.tc_stages, p.tc_smem)) p.tile_m = 256;
+    else tc_pick_stages(kmax, 1, p.tc_stages, p.tc_smem);
     p.t128max = p.routes / p.tile_m + act_max + 1;
 
     size_t o = 0;
@@ -1258,9 +1258,7 @@ static cudaError_t run_moe_gemm(const MoePlan& p, const MoeCall& c, const WsPtrs
     TcArgs t{};
     t.status = w.status;
     t.kmax = p.kmax;
-    t.sa = p.tc_sa;
-    t.sb = p.tc_sb;
-    t.sr = p.tc_sr;
+    t.stages = p.tc_stages;
     t.ntiles = w.ntiles128;
     t.tiles = w.tiles128;
     t.sorted_w = w.sorted_w;

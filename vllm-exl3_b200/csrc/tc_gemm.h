@@ -17,8 +17,7 @@ enum TcEpi : int { TC_EPI_ROWS = 0, TC_EPI_DOWN = 1, TC_EPI_LINEAR = 2, TC_EPI_U
 struct TcArgs {
     int* status;
     ProjRef proj;
-    int in_f, out_f, ncb, kmax;
-    int sa, sb, sr;  // ring depths: activation tiles, decoded weight tiles, raw trellis words
+    int in_f, out_f, ncb, kmax, stages;
     const int* ntiles;
     const int4* tiles;  // {expert, first sorted row, rows <= 128 * mt, 0}
     int epi;
