@@ -19,8 +19,11 @@ copied in and the output copied back inside the timed region.
 
 N > 1: expert parallelism (exl3_b200.ep): rank g holds experts
 [g*128/N, (g+1)*128/N) and T tokens of its own (weak scaling); a step is
-dispatch, NCCL all-to-all, the local fused forward, all-to-all back and the
-per-token combine, timed per step and taken as the max over ranks.
+dispatch (the library's kernels store each pair row straight into its
+owner's IPC-mapped window over NVLink; --ep-transport nccl uses NCCL
+instead), the local fused forward, the partial rows stored back, and the
+per-token combine, one CUDA graph per step, timed per step and taken as the
+max over ranks.
 --workload ep: configs[4] (256 experts, H7168 I2048, 8192 tokens split over
 the ranks: strong scaling), same EP step at any N.  --workload prefill:
 configs[2] on one GPU (tcgen05 grouped GEMM path).  --impl reference: rank 0 times the
@@ -65,6 +68,8 @@ def parse():
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="time the expert-parallel step eagerly")
+    ap.add_argument("--ep-transport", default="nvlink", choices=["nvlink", "nccl"],
+                    help="expert-parallel exchange: the library's NVLink peer-store kernels or NCCL")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep"],
                     help="decode = configs[1] (the default, reported line); prefill = configs[2]; "
                          "ep = configs[4]")
@@ -460,7 +465,7 @@ def run_ep(args, rank, local_rank, world, which):
     kbits = [e["gate"].K for e in pack.experts]
     layer = moe.layer_from_pack(pack, dev)
     del pack
-    ep = Exl3ExpertParallel(layer, E_, capacity=Tr)
+    ep = Exl3ExpertParallel(layer, E_, capacity=Tr, transport=args.ep_transport)
     NB = 4 if which == "decode" else 2
     batches, local_routes, local_experts = [], [], []
     for b in range(NB):
@@ -616,10 +621,11 @@ def run_ep(args, rank, local_rank, world, which):
     evs = e2e(args.steps)
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs))
-    launches = 2 + nloc + 1
+    launches = (2 + nloc + 1) if args.ep_transport == "nccl" else (3 + 1 + nloc + 2 + 1 + 2)
     graph_used = graph is not None
     del graph
     torch.cuda.synchronize(dev)
+    ep.close()
     return {
         "metric": METRIC if which == "decode" else f"MoE layer prefill tokens/s ({c['name']})",
         "value": Tt * args.steps / (total_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -628,7 +634,10 @@ def run_ep(args, rank, local_rank, world, which):
         "dtype": "fp16 MMA, fp32 accumulate (int trellis decode); bf16 rows out, fp32 partials back", "data": "synthetic",
         "config": {"workload": f"{c['name']}, T={Tt} tokens/step ({Tr} per rank)", "experts": E_,
                    "experts_per_rank": epr, "topk": k, "hidden": H_, "intermediate": I_,
-                   "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single, fixed capacity %d rows/rank" % Tr,
+                   "parallelism": f"ep{world}",
+                   "exchange": ("NVLink peer stores into IPC-mapped windows (library kernels), per-step flags"
+                                if args.ep_transport == "nvlink" else "NCCL grouped send/recv")
+                   + ", fixed capacity %d rows/rank" % Tr,
                    "l2": "256 MB L2 flush before every step (untimed)",
                    "timing": ("CUDA events per step around one CUDA-graph replay of the EP step" if graph_used
                               else "CUDA events per step around the eager EP step") + ", max over ranks"},

@@ -182,6 +182,57 @@ int exl3_ep_dispatch(const void* x, int x_dtype, int64_t tokens, int64_t hidden,
 int exl3_ep_combine(const void* partial, int partial_dtype, const int32_t* pair_idx, int64_t tokens, int world,
                     int64_t hidden, const int32_t* n_valid, void* out, int out_dtype, void* stream);
 
+/* Expert-parallel exchange over NVLink peer memory (no counterpart in the
+ * reference; replaces the NCCL all-to-all around exl3_ep_dispatch /
+ * exl3_ep_combine with direct stores into the peers' memory).
+ *
+ * Every rank allocates a window of exl3_ep_window_size bytes (the same
+ * geometry on all ranks: world, capacity rows per rank pair, hidden, topk,
+ * the dtypes of the token rows and of the partial rows), exports it with
+ * exl3_ep_ipc_handle and maps its peers' windows with exl3_ep_ipc_open;
+ * `peers` is a device int64 array of `world` window addresses as seen from
+ * this GPU (its own entry = its own window).  A layer step on every rank:
+ *   exl3_ep_p2p_dispatch  pair the tokens with their owners (as
+ *                         exl3_ep_dispatch with a capacity) and store each
+ *                         pair's row, local ids and weights into its owner's
+ *                         window, then raise this step's arrival flag there;
+ *   exl3_ep_p2p_wait(0)   wait until every peer's rows have arrived;
+ *   exl3_moe_forward      on the window's received rows (world * capacity
+ *                         rows at exl3_ep_window_recv, ids -1 marking empty
+ *                         slots) into a partial buffer;
+ *   exl3_ep_p2p_return    store each source's partial rows back into its
+ *                         window and raise the return flag there;
+ *   exl3_ep_p2p_wait(1)   wait until every owner's partial rows are back;
+ *   exl3_ep_p2p_combine   per-token sum over owners in rank order (as
+ *                         exl3_ep_combine), then advance the step counter.
+ * Flags carry the step number, so nothing is reset between steps and the
+ * whole step can be captured in a CUDA graph; a step completes the round
+ * trip before the next begins, so each direction needs one buffer.  Waits
+ * are bounded (about 2 s): a timeout records status 4 in the window's
+ * status word (read it with exl3_device_status(window + 4)) instead of
+ * hanging.  Allocation and IPC calls are synchronous; make them before any
+ * stream capture. */
+size_t exl3_ep_window_size(int world, int64_t capacity, int64_t hidden, int topk, int x_dtype, int partial_dtype);
+int exl3_ep_window_alloc(size_t bytes, void** window);
+int exl3_ep_window_free(void* window);
+int exl3_ep_ipc_handle(const void* window, void* handle /* 64 bytes */);
+int exl3_ep_ipc_open(const void* handle, void** mapped);
+int exl3_ep_ipc_close(void* mapped);
+int exl3_ep_p2p_dispatch(const void* x, int x_dtype, int64_t tokens, int64_t hidden, const void* topk_ids,
+                         int ids_dtype, const void* topk_weights, int w_dtype, int topk, int64_t n_global,
+                         int world, int rank, int64_t capacity, const int32_t* n_valid, void* window,
+                         const int64_t* peers, int partial_dtype, int32_t* pair_idx, void* stream);
+int exl3_ep_p2p_wait(void* window, int world, int phase, void* stream);
+int exl3_ep_p2p_return(const void* partial, int partial_dtype, int world, int rank, int64_t capacity,
+                       int64_t hidden, int topk, int x_dtype, void* window, const int64_t* peers, void* stream);
+int exl3_ep_p2p_combine(void* window, int world, int rank, int64_t capacity, int64_t hidden, int topk,
+                        int x_dtype, int partial_dtype, const int32_t* pair_idx, int64_t tokens,
+                        const int32_t* n_valid, void* out, int out_dtype, void* stream);
+/* Byte offsets of the received rows, local ids (int32) and weights (fp32)
+ * inside a window of that geometry (what exl3_moe_forward reads). */
+int exl3_ep_window_recv(int world, int64_t capacity, int64_t hidden, int topk, int x_dtype, int partial_dtype,
+                        size_t* x_off, size_t* ids_off, size_t* w_off);
+
 /* Phase timing for benchmarks (no reference counterpart; the reference times
  * its kernels with CUDA events in tools/bench_moe_decode.py:24-55).  While
  * enabled, exl3_moe_forward and exl3_linear first launch a spin of

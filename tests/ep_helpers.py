@@ -193,11 +193,13 @@ def nccl_worker(rank: int, world: int, port: int, cfg: dict, result_q) -> None:
         x = synthetic.activations(rng, cfg["T"] * world, cfg["H"])
         ids, w = synthetic.softmax_topk(rng, cfg["T"] * world, cfg["E"], cfg["topk"])
         sl = slice(rank * cfg["T"], (rank + 1) * cfg["T"])
-        ep = Exl3ExpertParallel(layer, cfg["E"], combine_dtype=torch.float32, capacity=cfg.get("capacity"))
+        ep = Exl3ExpertParallel(layer, cfg["E"], combine_dtype=torch.float32, capacity=cfg.get("capacity"),
+                                transport=cfg.get("transport", "nccl"))
         y = ep(torch.from_numpy(x[sl]).to(torch.bfloat16).to(dev), torch.from_numpy(w[sl]).to(dev),
                torch.from_numpy(ids[sl]).to(dev))
         torch.cuda.synchronize(dev)
         result_q.put((rank, y.float().cpu().numpy(), ep.last_counts))
+        ep.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()

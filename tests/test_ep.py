@@ -232,15 +232,140 @@ def test_ep_world1_module_matches_layer(native, cuda, cap):
     _close(got[:17], want[:17], rel=1e-3)
 
 
+def _nvlink_emulated_step(layers, wins, x, ids, w, E, G, C, out_dtype):
+    """G ranks' NVLink steps on one GPU, phase by phase across the ranks (all
+    dispatches, then every rank's wait + local forward + return, then every
+    rank's wait + combine): no wait ever depends on a later launch."""
+    import torch
+    from exl3_b200 import _native as _n
+    from exl3_b200.moe import moe_forward_ptrs
+    lib = _n.load()
+    T = x.shape[0] // G
+    H = x.shape[1]
+    topk = ids.shape[1]
+    dev = x.device
+    stream = _n.stream_of(x)
+    pidx = [torch.empty(C, G, dtype=torch.int32, device=dev) for _ in range(G)]
+    part = [torch.empty(G * C, H, dtype=torch.float32, device=dev) for _ in range(G)]
+    outs = [torch.empty(T, H, dtype=out_dtype, device=dev) for _ in range(G)]
+    for r in range(G):
+        xr, ir, wr = x[r * T:(r + 1) * T], ids[r * T:(r + 1) * T], w[r * T:(r + 1) * T]
+        _n.check(lib.exl3_ep_p2p_dispatch(xr.data_ptr(), _n.dtype_code(xr), T, H, ir.data_ptr(),
+                                          _n.dtype_code(ir), wr.data_ptr(), _n.dtype_code(wr), topk, E, G, r, C,
+                                          None, wins[r].window, wins[r].peers.data_ptr(), _n.DT_F32,
+                                          pidx[r].data_ptr(), stream))
+    for r in range(G):
+        _n.check(lib.exl3_ep_p2p_wait(wins[r].window, G, 0, stream))
+        moe_forward_ptrs(layers[r], dev, wins[r].recv_x, _n.dtype_code(x), G * C, wins[r].recv_ids, _n.DT_I32,
+                         wins[r].recv_w, _n.DT_F32, topk, part[r].data_ptr(), _n.DT_F32)
+        _n.check(lib.exl3_ep_p2p_return(part[r].data_ptr(), _n.DT_F32, G, r, C, H, topk, _n.dtype_code(x),
+                                        wins[r].window, wins[r].peers.data_ptr(), stream))
+    for r in range(G):
+        _n.check(lib.exl3_ep_p2p_wait(wins[r].window, G, 1, stream))
+        _n.check(lib.exl3_ep_p2p_combine(wins[r].window, G, r, C, H, topk, _n.dtype_code(x), _n.DT_F32,
+                                         pidx[r].data_ptr(), T, None, outs[r].data_ptr(), _n.dtype_code(outs[r]),
+                                         stream))
+    return torch.cat(outs)
+
+
 @pytest.mark.gpu
-@pytest.mark.parametrize("capacity", [None, 40])
-def test_ep_nccl_two_gpus(native, capacity):
+@pytest.mark.parametrize("G", [2, 4])
+def test_ep_nvlink_emulated_ranks(native, cuda, G):
+    """The NVLink transport's kernels (window stores, flags, waits, return,
+    combine) for G ranks emulated on one GPU, two consecutive steps (the
+    flags carry the step number), against the single-GPU layer and the
+    oracle."""
+    import torch
+    from exl3_b200 import moe, synthetic
+    from exl3_b200.ep import NvlinkEpWindow
+    E, H, I, topk, Tr = 16, 512, 256, 4, 24
+    C = Tr
+    pack = synthetic.make_moe_pack(31, E, H, I, synthetic.CB_MCG, (2, 3, 4))
+    full = moe.layer_from_pack(pack, cuda)
+    epr = E // G
+    layers = [moe.layer_from_pack(synthetic.MoEPack(H, I, pack.codebook, pack.experts[r * epr:(r + 1) * epr]), cuda)
+              for r in range(G)]
+    wins = [NvlinkEpWindow(G, r, C, H, topk, torch.bfloat16, torch.float32, cuda, exchange=False) for r in range(G)]
+    addrs = [wn.window for wn in wins]
+    for wn in wins:
+        wn.set_peers(addrs)
+    try:
+        dense = ep_helpers.dense_experts(pack, 0, E)
+        for step in range(2):
+            rng = np.random.default_rng(50 + step)
+            xs = synthetic.activations(rng, Tr * G, H)
+            ids, w = synthetic.softmax_topk(rng, Tr * G, E, topk)
+            x = torch.from_numpy(xs).to(torch.bfloat16).to(cuda)
+            idt, wt = torch.from_numpy(ids).to(cuda), torch.from_numpy(w).to(cuda)
+            got = _nvlink_emulated_step(layers, wins, x, idt, wt, E, G, C, torch.float32).cpu().numpy()
+            single = torch.empty(x.shape[0], H, dtype=torch.float32, device=cuda)
+            full.apply(x, wt, idt, out=single)
+            _close(got, single.cpu().numpy())
+            _close(got, oracle.moe_eager(x.float().cpu().numpy(), ids, w, dense))
+            assert all(wn.status() == 0 for wn in wins)
+    finally:
+        for wn in wins:
+            wn.close()
+
+
+@pytest.mark.gpu
+def test_ep_nvlink_wait_times_out_with_status(native, cuda):
+    """A peer that never signals: the bounded wait gives up (about 2 s) and
+    records status 4 in the window instead of spinning on."""
+    import time
+
+    import torch
+    from exl3_b200 import _native as _n
+    from exl3_b200.ep import NvlinkEpWindow
+    wins = [NvlinkEpWindow(2, r, 8, 128, 2, torch.float16, torch.float32, cuda, exchange=False) for r in range(2)]
+    for wn in wins:
+        wn.set_peers([wins[0].window, wins[1].window])
+    try:
+        lib = _n.load()
+        t0 = time.time()
+        _n.check(lib.exl3_ep_p2p_wait(wins[0].window, 2, 0, _n.stream_of(wins[0].peers)))
+        torch.cuda.synchronize(cuda)
+        assert time.time() - t0 < 30
+        assert wins[0].status() == 4
+        assert wins[0].status() == 0  # cleared
+    finally:
+        for wn in wins:
+            wn.close()
+
+
+@pytest.mark.gpu
+def test_ep_nvlink_world1_module(native, cuda):
+    import torch
+    from exl3_b200 import moe, synthetic
+    from exl3_b200.ep import Exl3ExpertParallel
+    pack = synthetic.make_moe_pack(6, 8, 256, 128, synthetic.CB_MCG, (4,))
+    layer = moe.layer_from_pack(pack, cuda)
+    ep = Exl3ExpertParallel(layer, 8, combine_dtype=torch.float32, capacity=48, transport="nvlink")
+    try:
+        for step in range(3):
+            rng = np.random.default_rng(10 + step)
+            x = torch.from_numpy(synthetic.activations(rng, 40, 256)).to(torch.bfloat16).to(cuda)
+            ids, w = synthetic.softmax_topk(rng, 40, 8, 2)
+            idt, wt = torch.from_numpy(ids).to(cuda), torch.from_numpy(w).to(cuda)
+            f32 = torch.empty(40, 256, dtype=torch.float32, device=cuda)
+            got = ep(x, wt, idt, out=f32).cpu().numpy()
+            want = torch.empty_like(f32)
+            layer.apply(x, wt, idt, out=want)
+            _close(got, want.cpu().numpy(), rel=1e-3)
+            assert ep.window(x.dtype, 2, 256).status() == 0
+    finally:
+        ep.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("capacity,transport", [(None, "nccl"), (40, "nccl"), (40, "nvlink")])
+def test_ep_nccl_two_gpus(native, capacity, transport):
     """Two ranks over NCCL on two GPUs (skipped on a one-GPU box)."""
     import torch
     from exl3_b200 import synthetic
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    cfg = dict(seed=17, E=16, H=512, I=256, topk=4, T=40, capacity=capacity)
+    cfg = dict(seed=17, E=16, H=512, I=256, topk=4, T=40, capacity=capacity, transport=transport)
     world = 2
     got = {r: y for r, y, _c in _run_ranks(ep_helpers.nccl_worker, world, cfg, 120)}
     pack = synthetic.make_moe_pack(cfg["seed"], cfg["E"], cfg["H"], cfg["I"], synthetic.CB_MCG, (2, 3, 4))

@@ -5,6 +5,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 #include "../../include/exl3_b200.h"
@@ -371,6 +372,178 @@ int exl3_ep_combine(const void* partial, int partial_dtype, const int32_t* pair_
     cudaError_t e = exl3::run_ep_combine(partial, partial_dtype, pair_idx, tokens, world, int(hidden), n_valid, out,
                                          out_dtype, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? EXL3_OK : cuda_fail(e, who);
+}
+
+size_t exl3_ep_window_size(int world, int64_t capacity, int64_t hidden, int topk, int x_dtype, int partial_dtype) {
+    if (world < 1 || world > exl3::kEpMaxWorld || capacity < 1 || hidden <= 0 || hidden % 128 || topk < 1 ||
+        topk > 64 || !float_dtype(x_dtype) || !float_dtype(partial_dtype))
+        return 0;
+    return exl3::ep_window(world, capacity, hidden, topk, x_dtype == EXL3_DT_F32 ? 4 : 2,
+                           partial_dtype == EXL3_DT_F32 ? 4 : 2)
+        .total;
+}
+
+int exl3_ep_window_alloc(size_t bytes, void** window) {
+    if (!window || bytes == 0) return fail(EXL3_ERR_ARG, "exl3_ep_window_alloc: bad arguments");
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        return cuda_fail(e, "exl3_ep_window_alloc");
+    }
+    *window = p;
+    return EXL3_OK;
+}
+
+int exl3_ep_window_free(void* window) {
+    if (!window) return EXL3_OK;
+    cudaError_t e = cudaFree(window);
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, "exl3_ep_window_free");
+}
+
+int exl3_ep_ipc_handle(const void* window, void* handle) {
+    if (!window || !handle) return fail(EXL3_ERR_ARG, "exl3_ep_ipc_handle: null argument");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(window));
+    if (e != cudaSuccess) return cuda_fail(e, "exl3_ep_ipc_handle");
+    memcpy(handle, &h, sizeof(h));
+    return EXL3_OK;
+}
+
+int exl3_ep_ipc_open(const void* handle, void** mapped) {
+    if (!handle || !mapped) return fail(EXL3_ERR_ARG, "exl3_ep_ipc_open: null argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(mapped, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, "exl3_ep_ipc_open");
+}
+
+int exl3_ep_ipc_close(void* mapped) {
+    if (!mapped) return EXL3_OK;
+    cudaError_t e = cudaIpcCloseMemHandle(mapped);
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, "exl3_ep_ipc_close");
+}
+
+static int ep_p2p_common(const char* who, int world, int rank, int64_t capacity, int64_t hidden, int topk, int x_dtype,
+                         int partial_dtype, const void* window, const int64_t* peers) {
+    if (!window || !peers) return fail(EXL3_ERR_ARG, "%s: null window/peers", who);
+    if (world < 1 || world > exl3::kEpMaxWorld || rank < 0 || rank >= world)
+        return fail(EXL3_ERR_ARG, "%s: bad world/rank", who);
+    if (capacity < 1 || capacity * int64_t(world) > INT32_MAX) return fail(EXL3_ERR_ARG, "%s: bad capacity", who);
+    if (hidden <= 0 || hidden % 128 || hidden > INT32_MAX)
+        return fail(EXL3_ERR_ARG, "%s: hidden width must be a positive multiple of 128", who);
+    if (topk < 1 || topk > 64) return fail(EXL3_ERR_ARG, "%s: topk must be in 1..64", who);
+    if (!float_dtype(x_dtype) || !float_dtype(partial_dtype)) return fail(EXL3_ERR_ARG, "%s: bad dtype", who);
+    if (!aligned(window, 256)) return fail(EXL3_ERR_ARG, "%s: window must be 256-byte aligned", who);
+    return EXL3_OK;
+}
+
+static exl3::EpP2pCall ep_p2p_call(int phase, int world, int rank, int64_t capacity, int64_t hidden, int topk,
+                                   int x_dtype, int partial_dtype, void* window, const int64_t* peers) {
+    exl3::EpP2pCall c;
+    c.phase = phase;
+    c.world = world;
+    c.rank = rank;
+    c.capacity = capacity;
+    c.hidden = hidden;
+    c.topk = topk;
+    c.x_esize = x_dtype == EXL3_DT_F32 ? 4 : 2;
+    c.p_esize = partial_dtype == EXL3_DT_F32 ? 4 : 2;
+    c.p_dtype = partial_dtype;
+    c.window = window;
+    c.peers = peers;
+    return c;
+}
+
+int exl3_ep_p2p_dispatch(const void* x, int x_dtype, int64_t tokens, int64_t hidden, const void* ids, int ids_dtype,
+                         const void* weights, int w_dtype, int topk, int64_t n_global, int world, int rank,
+                         int64_t capacity, const int32_t* n_valid, void* window, const int64_t* peers,
+                         int partial_dtype, int32_t* pair_idx, void* stream) {
+    const char* who = "exl3_ep_p2p_dispatch";
+    if (int rc = ep_p2p_common(who, world, rank, capacity, hidden, topk, x_dtype, partial_dtype, window, peers))
+        return rc;
+    if (!x || !ids || !weights || !pair_idx) return fail(EXL3_ERR_ARG, "%s: null argument", who);
+    if (ids_dtype != EXL3_DT_I32 && ids_dtype != EXL3_DT_I64)
+        return fail(EXL3_ERR_ARG, "%s: expert ids must be int32 or int64", who);
+    if (!float_dtype(w_dtype)) return fail(EXL3_ERR_ARG, "%s: bad weights dtype", who);
+    if (n_global < world || n_global % world)
+        return fail(EXL3_ERR_ARG, "%s: %lld experts do not split evenly over %d ranks", who, (long long)n_global,
+                    world);
+    if (tokens < 0 || tokens > capacity) return fail(EXL3_ERR_ARG, "%s: tokens must be in [0, capacity]", who);
+    if (!aligned(x, 16)) return fail(EXL3_ERR_ARG, "%s: x must be 16-byte aligned", who);
+    exl3::EpP2pCall c = ep_p2p_call(exl3::EP_P2P_DISPATCH, world, rank, capacity, hidden, topk, x_dtype,
+                                    partial_dtype, window, peers);
+    c.x = x;
+    c.tokens = tokens;
+    c.ids = ids;
+    c.ids_dtype = ids_dtype;
+    c.weights = weights;
+    c.w_dtype = w_dtype;
+    c.n_global = n_global;
+    c.n_valid = n_valid;
+    c.pair_idx = pair_idx;
+    cudaError_t e = exl3::run_ep_p2p(c, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, who);
+}
+
+int exl3_ep_p2p_wait(void* window, int world, int phase, void* stream) {
+    const char* who = "exl3_ep_p2p_wait";
+    if (!window || world < 1 || world > exl3::kEpMaxWorld || (phase != 0 && phase != 1))
+        return fail(EXL3_ERR_ARG, "%s: bad arguments", who);
+    exl3::EpP2pCall c;
+    c.phase = phase == 0 ? exl3::EP_P2P_WAIT_ARRIVE : exl3::EP_P2P_WAIT_RETURN;
+    c.world = world;
+    c.window = window;
+    cudaError_t e = exl3::run_ep_p2p(c, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, who);
+}
+
+int exl3_ep_p2p_return(const void* partial, int partial_dtype, int world, int rank, int64_t capacity, int64_t hidden,
+                       int topk, int x_dtype, void* window, const int64_t* peers, void* stream) {
+    const char* who = "exl3_ep_p2p_return";
+    if (int rc = ep_p2p_common(who, world, rank, capacity, hidden, topk, x_dtype, partial_dtype, window, peers))
+        return rc;
+    if (!partial || !aligned(partial, 16)) return fail(EXL3_ERR_ARG, "%s: partial must be 16-byte aligned", who);
+    exl3::EpP2pCall c = ep_p2p_call(exl3::EP_P2P_RETURN, world, rank, capacity, hidden, topk, x_dtype,
+                                    partial_dtype, window, peers);
+    c.partial = partial;
+    cudaError_t e = exl3::run_ep_p2p(c, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, who);
+}
+
+int exl3_ep_p2p_combine(void* window, int world, int rank, int64_t capacity, int64_t hidden, int topk, int x_dtype,
+                        int partial_dtype, const int32_t* pair_idx, int64_t tokens, const int32_t* n_valid, void* out,
+                        int out_dtype, void* stream) {
+    const char* who = "exl3_ep_p2p_combine";
+    static const int64_t dummy = 0;
+    if (int rc = ep_p2p_common(who, world, rank, capacity, hidden, topk, x_dtype, partial_dtype, window, &dummy))
+        return rc;
+    if (!pair_idx || !out || !aligned(out, 16)) return fail(EXL3_ERR_ARG, "%s: bad pair_idx/out", who);
+    if (!float_dtype(out_dtype)) return fail(EXL3_ERR_ARG, "%s: bad out dtype", who);
+    if (tokens < 0 || tokens > capacity) return fail(EXL3_ERR_ARG, "%s: tokens must be in [0, capacity]", who);
+    exl3::EpP2pCall c = ep_p2p_call(exl3::EP_P2P_COMBINE, world, rank, capacity, hidden, topk, x_dtype,
+                                    partial_dtype, window, nullptr);
+    c.pair_idx = const_cast<int32_t*>(pair_idx);
+    c.tokens = tokens;
+    c.n_valid = n_valid;
+    c.out = out;
+    c.out_dtype = out_dtype;
+    cudaError_t e = exl3::run_ep_p2p(c, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, who);
+}
+
+int exl3_ep_window_recv(int world, int64_t capacity, int64_t hidden, int topk, int x_dtype, int partial_dtype,
+                        size_t* x_off, size_t* ids_off, size_t* w_off) {
+    if (!x_off || !ids_off || !w_off ||
+        exl3_ep_window_size(world, capacity, hidden, topk, x_dtype, partial_dtype) == 0)
+        return fail(EXL3_ERR_ARG, "exl3_ep_window_recv: bad geometry");
+    const exl3::EpWindow L = exl3::ep_window(world, capacity, hidden, topk, x_dtype == EXL3_DT_F32 ? 4 : 2,
+                                             partial_dtype == EXL3_DT_F32 ? 4 : 2);
+    *x_off = L.recv_x;
+    *ids_off = L.recv_ids;
+    *w_off = L.recv_w;
+    return EXL3_OK;
 }
 
 int exl3_profile_enable(int on, long long delay_cycles) {

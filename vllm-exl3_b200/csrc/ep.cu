@@ -242,7 +242,186 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const void* __restrict_
     }
 }
 
+// ---------------------------------------------------------------------------
+// NVLink transport: every rank owns a window (same geometry everywhere) that
+// its peers map through CUDA IPC.  Sources store pair rows straight into the
+// owners' windows and raise a per-step flag; owners run the local forward on
+// their window and store the partial rows back into the sources' windows.
+// A step completes the whole round trip before the next one starts (a
+// source's next dispatch follows its combine, which waited for every owner's
+// return, which followed that owner's forward), so one buffer per direction
+// suffices and every pointer is fixed: a step can be captured in a graph.
+// Flags hold the step number (monotonic), read from the window's own epoch.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+struct EpP2pArgs {
+    const uint4* x;
+    int64_t row_vecs;  // 16-byte vectors per x row
+    int world, rank, topk;
+    int64_t cap;
+    EpWindow L;
+    char* window;
+    const int64_t* peers;
+};
+
+// source: pair slots (g, idx) of the capacity layout -> owner g's window at
+// [rank * cap + idx]; empty slots carry ids -1 / weight 0 (rows untouched)
+__global__ void __launch_bounds__(256) ep_p2p_scatter_kernel(const EpP2pArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int32_t* counts = reinterpret_cast<const int32_t*>(a.window + a.L.send_counts);
+    const int32_t* tok = reinterpret_cast<const int32_t*>(a.window + a.L.send_tok);
+    const int32_t* sid = reinterpret_cast<const int32_t*>(a.window + a.L.send_ids);
+    const float* sw = reinterpret_cast<const float*>(a.window + a.L.send_w);
+    const int64_t total = int64_t(a.world) * a.cap;
+    const int64_t nw = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t it = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; it < total; it += nw) {
+        const int g = int(it / a.cap);
+        const int64_t idx = it % a.cap;
+        char* dst = reinterpret_cast<char*>(a.peers[g]);
+        const int64_t slot = int64_t(a.rank) * a.cap + idx;
+        int32_t* did = reinterpret_cast<int32_t*>(dst + a.L.recv_ids) + slot * a.topk;
+        float* dw = reinterpret_cast<float*>(dst + a.L.recv_w) + slot * a.topk;
+        if (idx < counts[g]) {
+            const uint4* src = a.x + int64_t(tok[it]) * a.row_vecs;
+            uint4* dx = reinterpret_cast<uint4*>(dst + a.L.recv_x) + slot * a.row_vecs;
+            for (int64_t v = lane; v < a.row_vecs; v += 32) dx[v] = src[v];
+            for (int k = lane; k < a.topk; k += 32) {
+                did[k] = sid[it * a.topk + k];
+                dw[k] = sw[it * a.topk + k];
+            }
+        } else {
+            for (int k = lane; k < a.topk; k += 32) {
+                did[k] = -1;
+                dw[k] = 0.f;
+            }
+        }
+    }
+    __threadfence_system();  // this thread's peer stores are visible system-wide before the flag kernel runs
+}
+
+// owner: its partial rows of source g's pairs -> source g's window at [rank * cap + idx]
+__global__ void __launch_bounds__(256) ep_p2p_return_kernel(const uint4* __restrict__ partial, int64_t row_vecs,
+                                                            const EpP2pArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int32_t* counts = reinterpret_cast<const int32_t*>(a.window + a.L.counts);  // pairs from each source
+    const int64_t total = int64_t(a.world) * a.cap;
+    const int64_t nw = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t it = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; it < total; it += nw) {
+        const int g = int(it / a.cap);
+        const int64_t idx = it % a.cap;
+        if (idx >= counts[g]) continue;
+        char* dst = reinterpret_cast<char*>(a.peers[g]);
+        uint4* db = reinterpret_cast<uint4*>(dst + a.L.back) + (int64_t(a.rank) * a.cap + idx) * row_vecs;
+        const uint4* src = partial + it * row_vecs;
+        for (int64_t v = lane; v < row_vecs; v += 32) db[v] = src[v];
+    }
+    __threadfence_system();
+}
+
+// raise this step's flag (arrival or return) on every peer; with counts,
+// first tell each owner how many pairs it gets from this rank
+__global__ void ep_p2p_signal_kernel(const int64_t* peers, int world, int rank, size_t flag_off, size_t counts_off,
+                                     const int32_t* send_counts, const uint32_t* epoch) {
+    const int g = threadIdx.x;
+    if (g >= world) return;
+    char* dst = reinterpret_cast<char*>(peers[g]);
+    if (send_counts) reinterpret_cast<volatile int32_t*>(dst + counts_off)[rank] = send_counts[g];
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<uint32_t*>(dst + flag_off) + rank, *epoch + 1u);
+}
+
+// wait (bounded) until every peer raised this step's flag in our window;
+// on timeout record DEV_WAIT_TIMEOUT in the window's status word and return
+__global__ void ep_p2p_wait_kernel(char* window, int world, size_t flag_off) {
+    const int g = threadIdx.x;
+    if (g >= world) return;
+    const uint32_t target = *reinterpret_cast<const uint32_t*>(window + kEpCtlEpoch) + 1u;
+    const uint32_t* flag = reinterpret_cast<const uint32_t*>(window + flag_off) + g;
+    const long long t0 = clock64();
+    while (int32_t(ld_acquire_sys(flag) - target) < 0) {
+        if (clock64() - t0 > kWaitBudgetCycles) {
+            atomicCAS(reinterpret_cast<int*>(window + kEpCtlStatus), 0, DEV_WAIT_TIMEOUT);
+            return;
+        }
+        __nanosleep(200);
+    }
+}
+
+__global__ void ep_p2p_epoch_kernel(char* window) {
+    uint32_t* e = reinterpret_cast<uint32_t*>(window + kEpCtlEpoch);
+    *e = *e + 1u;
+}
+
 }  // namespace
+
+cudaError_t run_ep_p2p(const EpP2pCall& c, cudaStream_t s) {
+    const EpWindow L = ep_window(c.world, c.capacity, c.hidden, c.topk, c.x_esize, c.p_esize);
+    char* win = static_cast<char*>(c.window);
+    EpP2pArgs a;
+    a.world = c.world;
+    a.rank = c.rank;
+    a.topk = c.topk;
+    a.cap = c.capacity;
+    a.L = L;
+    a.window = win;
+    a.peers = c.peers;
+    const int64_t slots = int64_t(c.world) * c.capacity;
+    const int grid = int(std::max<int64_t>(1, std::min<int64_t>((slots + 7) / 8, int64_t(num_sms_current()) * 8)));
+    cudaError_t e = cudaSuccess;
+    if (c.phase == EP_P2P_DISPATCH) {
+        EpPlanArgs p;
+        p.ids = c.ids;
+        p.ids_dtype = c.ids_dtype;
+        p.weights = c.weights;
+        p.w_dtype = c.w_dtype;
+        p.tokens = c.tokens;
+        p.topk = c.topk;
+        p.n_global = c.n_global;
+        p.world = c.world;
+        p.n_valid = c.n_valid;
+        p.send_ids = reinterpret_cast<int32_t*>(win + L.send_ids);
+        p.send_w = reinterpret_cast<float*>(win + L.send_w);
+        p.send_tok = reinterpret_cast<int32_t*>(win + L.send_tok);
+        p.pair_idx = c.pair_idx;
+        p.send_counts = reinterpret_cast<int32_t*>(win + L.send_counts);
+        p.capacity = c.capacity;
+        ep_plan_kernel<<<1, kEpPlanThreads, 0, s>>>(p);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        a.x = static_cast<const uint4*>(c.x);
+        a.row_vecs = c.hidden * int64_t(c.x_esize) / 16;
+        ep_p2p_scatter_kernel<<<grid, 256, 0, s>>>(a);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        ep_p2p_signal_kernel<<<1, 64, 0, s>>>(c.peers, c.world, c.rank, L.arrive, L.counts, p.send_counts,
+                                               reinterpret_cast<const uint32_t*>(win + kEpCtlEpoch));
+    } else if (c.phase == EP_P2P_WAIT_ARRIVE || c.phase == EP_P2P_WAIT_RETURN) {
+        ep_p2p_wait_kernel<<<1, 64, 0, s>>>(win, c.world, c.phase == EP_P2P_WAIT_ARRIVE ? L.arrive : L.ret);
+    } else if (c.phase == EP_P2P_RETURN) {
+        ep_p2p_return_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(c.partial),
+                                                  c.hidden * int64_t(c.p_esize) / 16, a);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        ep_p2p_signal_kernel<<<1, 64, 0, s>>>(c.peers, c.world, c.rank, L.ret, 0, nullptr,
+                                               reinterpret_cast<const uint32_t*>(win + kEpCtlEpoch));
+    } else if (c.phase == EP_P2P_COMBINE) {
+        if (c.tokens > 0) {
+            const int cgrid = int(std::max<int64_t>(1, std::min<int64_t>((c.tokens + 7) / 8, int64_t(num_sms_current()) * 8)));
+            ep_combine_kernel<<<cgrid, 256, 0, s>>>(win + L.back, c.p_dtype, c.pair_idx, c.tokens, c.world, c.hidden,
+                                                    c.n_valid, c.out, c.out_dtype);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        }
+        ep_p2p_epoch_kernel<<<1, 1, 0, s>>>(win);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
 
 cudaError_t run_ep_dispatch(const EpDispatchCall& c, cudaStream_t s) {
     EpPlanArgs a;

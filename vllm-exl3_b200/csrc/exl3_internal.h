@@ -123,6 +123,58 @@ struct EpDispatchCall {
 };
 
 cudaError_t run_ep_dispatch(const EpDispatchCall& c, cudaStream_t s);
+
+// NVLink transport window of one rank (byte offsets; same geometry on every
+// rank).  Control word 0: step epoch; word 1: status.  Peers write arrive[],
+// counts[], ret[], recv_*[] and back[]; the send_* scratch is local.
+constexpr size_t kEpCtlEpoch = 0, kEpCtlStatus = 4;
+struct EpWindow {
+    size_t arrive, counts, ret, send_counts, recv_x, recv_ids, recv_w, back, send_tok, send_ids, send_w, total;
+};
+__host__ __device__ inline EpWindow ep_window(int world, int64_t cap, int64_t hidden, int topk, int xsize,
+                                             int psize) {
+    auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+    const size_t slots = size_t(world) * size_t(cap);
+    EpWindow L;
+    L.arrive = 256;
+    L.counts = L.arrive + 256;
+    L.ret = L.counts + 256;
+    L.send_counts = L.ret + 256;
+    L.recv_x = L.send_counts + 256;
+    L.recv_ids = up(L.recv_x + slots * size_t(hidden) * xsize);
+    L.recv_w = up(L.recv_ids + slots * topk * 4);
+    L.back = up(L.recv_w + slots * topk * 4);
+    L.send_tok = up(L.back + slots * size_t(hidden) * psize);
+    L.send_ids = up(L.send_tok + slots * 4);
+    L.send_w = up(L.send_ids + slots * topk * 4);
+    L.total = up(L.send_w + slots * topk * 4);
+    return L;
+}
+
+enum EpP2pPhase : int { EP_P2P_DISPATCH = 0, EP_P2P_WAIT_ARRIVE = 1, EP_P2P_RETURN = 2, EP_P2P_WAIT_RETURN = 3,
+                        EP_P2P_COMBINE = 4 };
+struct EpP2pCall {
+    int phase = 0;
+    int world = 1, rank = 0, topk = 0;
+    int64_t capacity = 0, hidden = 0, tokens = 0, n_global = 0;
+    int x_esize = 2, p_esize = 4, p_dtype = 0;
+    void* window = nullptr;
+    const int64_t* peers = nullptr;
+    // dispatch
+    const void* x = nullptr;
+    const void* ids = nullptr;
+    int ids_dtype = 3;
+    const void* weights = nullptr;
+    int w_dtype = 0;
+    const int32_t* n_valid = nullptr;
+    int32_t* pair_idx = nullptr;
+    // return
+    const void* partial = nullptr;
+    // combine
+    void* out = nullptr;
+    int out_dtype = 0;
+};
+cudaError_t run_ep_p2p(const EpP2pCall& c, cudaStream_t s);
 cudaError_t run_ep_combine(const void* partial, int pdt, const int32_t* pair_idx, int64_t tokens, int world,
                            int hidden, const int32_t* n_valid, void* out, int odt, cudaStream_t s);
 

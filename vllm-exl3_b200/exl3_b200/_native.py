@@ -59,6 +59,18 @@ SIGNATURES = {
     "exl3_linear_noalloc": (I32, [P, I32, I64, P, P, P, I64, I64, I32, I32, P, I32, P]),
     "exl3_ep_dispatch": (I32, [P, I32, I64, I64, P, I32, P, I32, I32, I64, I32, P, P, P, P, P, P, P, I64, P]),
     "exl3_ep_combine": (I32, [P, I32, P, I64, I32, I64, P, P, I32, P]),
+    "exl3_ep_window_size": (SZ, [I32, I64, I64, I32, I32, I32]),
+    "exl3_ep_window_alloc": (I32, [SZ, ctypes.POINTER(P)]),
+    "exl3_ep_window_free": (I32, [P]),
+    "exl3_ep_ipc_handle": (I32, [P, P]),
+    "exl3_ep_ipc_open": (I32, [P, ctypes.POINTER(P)]),
+    "exl3_ep_ipc_close": (I32, [P]),
+    "exl3_ep_p2p_dispatch": (I32, [P, I32, I64, I64, P, I32, P, I32, I32, I64, I32, I32, I64, P, P, P, I32, P, P]),
+    "exl3_ep_p2p_wait": (I32, [P, I32, I32, P]),
+    "exl3_ep_p2p_return": (I32, [P, I32, I32, I32, I64, I64, I32, I32, P, P, P]),
+    "exl3_ep_p2p_combine": (I32, [P, I32, I32, I64, I64, I32, I32, I32, P, I64, P, P, I32, P]),
+    "exl3_ep_window_recv": (I32, [I32, I64, I64, I32, I32, I32, ctypes.POINTER(SZ), ctypes.POINTER(SZ),
+                                  ctypes.POINTER(SZ)]),
     "exl3_profile_enable": (I32, [I32, ctypes.c_longlong]),
     "exl3_profile_read": (I32, [ctypes.POINTER(F32), I32, ctypes.POINTER(I32)]),
 }

@@ -21,7 +21,9 @@ token exchange to vLLM's all-to-all backends.  One layer step:
    deterministic, no atomics.
 
 A token whose routes fall on one rank crosses the network once, not once per
-route.  The compute steps go through an ``ops`` object; the default
+route.  ``transport="nvlink"`` replaces the NCCL transfers with the library's
+own kernels storing straight into the peers' memory (CUDA IPC windows,
+per-step flags; see include/exl3_b200.h).  The compute steps go through an ``ops`` object; the default
 :class:`NativeEpOps` calls the C ABI and raises without a GPU.  Tests inject
 CPU stand-ins to exercise the exchange logic on gloo ranks.
 """
@@ -31,8 +33,10 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
+import ctypes
+
 from . import _native as _n
-from .moe import apply_exl3_experts
+from .moe import apply_exl3_experts, moe_forward_ptrs
 
 
 class NativeEpOps:
@@ -82,6 +86,81 @@ class NativeEpOps:
         return out
 
 
+class NvlinkEpWindow:
+    """This rank's NVLink exchange window and its peers' windows.
+
+    The window (``exl3_ep_window_size`` bytes, allocated by the library so
+    it can be exported) receives the rows other ranks route here and the
+    partial rows they return; ``peers`` is a device int64 array of every
+    rank's window address as mapped on this GPU (CUDA IPC).  With
+    ``peer_windows`` given (single-process emulation of several ranks on
+    one GPU) no IPC is done and those addresses are used directly.
+    """
+
+    def __init__(self, world: int, rank: int, capacity: int, hidden: int, topk: int, x_dtype: torch.dtype,
+                 partial_dtype: torch.dtype, device: torch.device, group=None, exchange: bool = True):
+        self.lib = _n.load()
+        self.world, self.rank, self.capacity, self.hidden, self.topk = world, rank, capacity, hidden, topk
+        self.x_code = _n._DTYPE_CODE[x_dtype]
+        self.p_code = _n._DTYPE_CODE[partial_dtype]
+        self.device = device
+        geom = (world, capacity, hidden, topk, self.x_code, self.p_code)
+        self.nbytes = int(self.lib.exl3_ep_window_size(*geom))
+        if self.nbytes == 0:
+            raise ValueError("unsupported expert-parallel window geometry")
+        ptr = _n.P()
+        with torch.cuda.device(device):
+            _n.check(self.lib.exl3_ep_window_alloc(self.nbytes, ctypes.byref(ptr)), "exl3_ep_window_alloc")
+        self.window = int(ptr.value)
+        xo, io, wo = _n.SZ(), _n.SZ(), _n.SZ()
+        _n.check(self.lib.exl3_ep_window_recv(*geom, ctypes.byref(xo), ctypes.byref(io), ctypes.byref(wo)),
+                 "exl3_ep_window_recv")
+        self.recv_x, self.recv_ids, self.recv_w = self.window + xo.value, self.window + io.value, self.window + wo.value
+        self.mapped: list[int] = []
+        self.peers = None
+        if exchange:
+            self._exchange(group)
+
+    def _exchange(self, group) -> None:
+        handle = (ctypes.c_char * 64)()
+        _n.check(self.lib.exl3_ep_ipc_handle(self.window, handle), "exl3_ep_ipc_handle")
+        handles = [bytes(handle)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        addrs = []
+        with torch.cuda.device(self.device):
+            for g in range(self.world):
+                if g == self.rank:
+                    addrs.append(self.window)
+                    continue
+                m = _n.P()
+                buf = (ctypes.c_char * 64).from_buffer_copy(handles[g])
+                _n.check(self.lib.exl3_ep_ipc_open(buf, ctypes.byref(m)), "exl3_ep_ipc_open")
+                self.mapped.append(int(m.value))
+                addrs.append(int(m.value))
+        self.set_peers(addrs)
+
+    def set_peers(self, addrs: list[int]) -> None:
+        self.peers = torch.tensor(addrs, dtype=torch.int64, device=self.device)
+
+    def status(self, clear: bool = True) -> int:
+        """The window's device status word (4 = a peer wait timed out)."""
+        v = _n.I32(0)
+        _n.check(self.lib.exl3_device_status(self.window + 4, int(clear), _n.stream_of(self.peers),
+                                             ctypes.byref(v)), "exl3_device_status")
+        return int(v.value)
+
+    def close(self) -> None:
+        with torch.cuda.device(self.device):
+            for m in self.mapped:
+                self.lib.exl3_ep_ipc_close(m)
+            self.mapped = []
+            if self.window:
+                self.lib.exl3_ep_window_free(self.window)
+                self.window = 0
+
+
 class Exl3ExpertParallel(torch.nn.Module):
     """Routed-expert layer sharded by experts over a process group.
 
@@ -102,7 +181,7 @@ class Exl3ExpertParallel(torch.nn.Module):
     """
 
     def __init__(self, local_layer, n_global: int, group=None, combine_dtype: torch.dtype = torch.float32,
-                 ops=None, capacity: int | None = None):
+                 ops=None, capacity: int | None = None, transport: str = "nccl"):
         super().__init__()
         self.layer = local_layer
         self.group = group
@@ -124,6 +203,14 @@ class Exl3ExpertParallel(torch.nn.Module):
         if capacity is not None and capacity < 1:
             raise ValueError("capacity must be a positive row count")
         self.capacity = None if capacity is None else int(capacity)
+        if transport not in ("nccl", "nvlink"):
+            raise ValueError("transport must be 'nccl' or 'nvlink'")
+        if transport == "nvlink" and (self.capacity is None or ops is not None):
+            raise ValueError("the NVLink transport needs a capacity and the native kernels")
+        self.transport = transport
+        self._win: NvlinkEpWindow | None = None
+        self._pair_idx = None
+        self._partial = None
         self.last_counts: tuple[list[int], list[int]] | None = None
         self.profile = False  # record CUDA events between the step's phases (benchmarks)
         self._events: list = []
@@ -189,6 +276,8 @@ class Exl3ExpertParallel(torch.nn.Module):
             w = w.float()
         topk = ids.shape[1]
         self._events = []
+        if self.transport == "nvlink":
+            return self._forward_nvlink(x, ids, w, limit, n_valid, out)
         if self.capacity is not None:
             return self._forward_fixed(x, ids, w, limit, n_valid, out)
         self._mark()
@@ -251,5 +340,61 @@ class Exl3ExpertParallel(torch.nn.Module):
         y = self.ops.combine(back, pair_idx, T, G, x.dtype, n_valid, out=out)
         self._mark()
         return y
+
+    def window(self, x_dtype: torch.dtype, topk: int, hidden: int) -> NvlinkEpWindow:
+        """The NVLink window, created on first use (every rank must call it
+        at the same point: the IPC handles are exchanged collectively)."""
+        if self._win is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+            self._win = NvlinkEpWindow(self.world, self.rank, self.capacity, hidden, topk, x_dtype,
+                                       self.combine_dtype, dev, group=self.group)
+            self._pair_idx = torch.empty(self.capacity, self.world, dtype=torch.int32, device=dev)
+            self._partial = torch.empty(self.world * self.capacity, hidden, dtype=self.combine_dtype, device=dev)
+        return self._win
+
+    def _forward_nvlink(self, x, ids, w, limit, n_valid, out):
+        T, H = x.shape
+        G, C = self.world, self.capacity
+        if T > C:
+            raise ValueError(f"{T} tokens exceed the exchange capacity {C}")
+        topk = ids.shape[1]
+        win = self.window(x.dtype, topk, H)
+        lib = win.lib
+        stream = _n.stream_of(x)
+        if out is None:
+            out = torch.empty(T, H, dtype=x.dtype, device=x.device)
+        _n.require_cuda(x, ids, w, n_valid, out, who="expert-parallel NVLink step")
+        pc, xc = win.p_code, win.x_code
+        self._mark()
+        _n.check(lib.exl3_ep_p2p_dispatch(
+            x.data_ptr(), xc, T, H, ids.data_ptr(), _n.dtype_code(ids), w.data_ptr(), _n.dtype_code(w), topk,
+            self.n_global, G, self.rank, C, _n.ptr(n_valid), win.window, win.peers.data_ptr(), pc,
+            self._pair_idx.data_ptr(), stream), "exl3_ep_p2p_dispatch")
+        self._mark()
+        _n.check(lib.exl3_ep_p2p_wait(win.window, G, 0, stream), "exl3_ep_p2p_wait")
+        self._mark()
+        moe_forward_ptrs(self.layer, x.device, win.recv_x, xc, G * C, win.recv_ids, _n.DT_I32, win.recv_w,
+                         _n.DT_F32, topk, self._partial.data_ptr(), pc, limit)
+        self._mark()
+        _n.check(lib.exl3_ep_p2p_return(self._partial.data_ptr(), pc, G, self.rank, C, H, topk, xc, win.window,
+                                        win.peers.data_ptr(), stream), "exl3_ep_p2p_return")
+        _n.check(lib.exl3_ep_p2p_wait(win.window, G, 1, stream), "exl3_ep_p2p_wait")
+        self._mark()
+        _n.check(lib.exl3_ep_p2p_combine(win.window, G, self.rank, C, H, topk, xc, pc, self._pair_idx.data_ptr(),
+                                         T, _n.ptr(n_valid), out.data_ptr(), _n.dtype_code(out), stream),
+                 "exl3_ep_p2p_combine")
+        self._mark()
+        return out
+
+    def close(self) -> None:
+        """Unmap the peers' windows and free this rank's (call on every rank,
+        after the last step; ranks synchronise first so no peer is still
+        writing)."""
+        if self._win is not None:
+            torch.cuda.synchronize()
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            self._win.close()
+            self._win = None
 
     apply = forward

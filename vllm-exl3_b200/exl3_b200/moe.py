@@ -169,6 +169,37 @@ def apply_exl3_experts(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: to
     return out.view(*x.shape[:-1], hidden)
 
 
+def moe_forward_ptrs(layer, device: torch.device, x_ptr: int, x_dtype: int, tokens: int, ids_ptr: int,
+                     ids_dtype: int, w_ptr: int, w_dtype: int, topk: int, out_ptr: int, out_dtype: int,
+                     limit: float | None = None) -> None:
+    """The layer's fused forward on raw device buffers (dtype codes of the C
+    ABI): rows that live outside torch, e.g. an expert-parallel window."""
+    lib = _n.load()
+    inners = getattr(layer, "_exl3_inners", None)
+    if not inners:
+        raise RuntimeError("EXL3 experts were not built after weight load")
+    if getattr(layer, "_exl3_ptrs", None) is None:
+        build_exl3_fused_state(layer, inners)
+    lim = 0.0 if limit is None or not (limit > 0) else float(limit)
+    hidden = int(layer._exl3_hidden_size)
+    inter = int(layer._exl3_intermediate_local)
+    kmax = int(layer._exl3_k_max_launch)
+    with torch.cuda.device(device):
+        need = lib.exl3_moe_workspace_size(tokens, topk, hidden, inter, len(inners), kmax)
+        if need == 0:
+            raise RuntimeError("fused MoE: unsupported geometry")
+        ws = _n.workspace(device, need)
+        p = layer._exl3_ptrs
+        kg, ku, kd = layer._exl3_k_tables
+        tables = [p[k] for k in ("gate_trellis", "gate_suh", "gate_svh", "up_trellis", "up_suh", "up_svh",
+                                 "down_trellis", "down_suh", "down_svh")]
+        _n.check(lib.exl3_moe_forward(
+            x_ptr, x_dtype, tokens, hidden, inter, *[t.data_ptr() for t in tables], ids_ptr, ids_dtype, w_ptr,
+            w_dtype, topk, None, 0, _n.ptr(kg), _n.ptr(ku), _n.ptr(kd), 0, kmax, len(inners),
+            int(layer._exl3_codebook), int(getattr(layer, "_exl3_moe_act", 0)), lim, None, out_ptr, out_dtype,
+            ws.data_ptr(), ws.numel(), torch.cuda.current_stream(device).cuda_stream), "fused MoE")
+
+
 class Exl3RoutedExperts(torch.nn.Module):
     """Minimal routed-expert layer: EXL3 experts + fused state + apply."""
 
