@@ -427,8 +427,9 @@ PREFILL = {
                     name="configs[2] mixed-K prefill: 160 experts top-8, H5120 I1536, K2/3 mul1"),
 }
 
-# expert-parallel workloads: experts sharded evenly over the ranks, NCCL
-# all-to-all dispatch/combine (exl3_b200.ep, fixed-capacity exchange)
+# expert-parallel workloads: experts sharded evenly over the ranks, rows
+# exchanged over NVLink peer memory or NCCL (exl3_b200.ep, fixed-capacity
+# exchange)
 EP_WORKLOADS = {
     # configs[1] decode layer at N > 1: T tokens per rank (weak scaling)
     "decode": dict(E=128, topk=8, H=2048, I=768, cb=1, k=(4,), kp=None, router="softmax", sigma=1.0,
@@ -440,9 +441,9 @@ EP_WORKLOADS = {
 
 
 def run_ep(args, rank, local_rank, world, which):
-    """One expert-parallel layer step per rank: dispatch, all-to-all, local
-    fused forward, all-to-all back, combine (fixed-capacity exchange, no host
-    synchronisation inside a step)."""
+    """One expert-parallel layer step per rank: dispatch and exchange, local
+    fused forward, partial rows back, combine (fixed-capacity exchange, no
+    host synchronisation inside a step)."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -496,7 +497,7 @@ def run_ep(args, rank, local_rank, world, which):
         return float(t.item())
 
     # decode-sized steps are launch-bound: capture the whole EP step (dispatch,
-    # NCCL transfers, local forward, combine) in one CUDA graph; the fixed-
+    # exchange, local forward, combine) in one CUDA graph; the fixed-
     # capacity exchange has no host synchronisation, so it is capturable.
     # Every rank must agree, so capture success is reduced over the ranks.
     graph = None
@@ -569,7 +570,7 @@ def run_ep(args, rank, local_rank, world, which):
         torch.cuda.synchronize(dev)
         loc.append(_native.profile_read())
     _native.profile_enable(False)
-    eph = {n: statistics.median(p[n] for p in ep_ph[1:]) * 1e3 for n in ep.PHASES}
+    eph = {n: statistics.median(p[n] for p in ep_ph[1:]) * 1e3 for n in ep.phases}
     nloc = len(loc[0])
     names = ["prep", "rotate", "gate_up", "act", "down", "combine"] if nloc == 6 else \
         ["prep", "rotate", "gate_up", "down", "combine"]

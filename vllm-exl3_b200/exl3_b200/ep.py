@@ -216,6 +216,14 @@ class Exl3ExpertParallel(torch.nn.Module):
         self._events: list = []
 
     PHASES = ("dispatch", "counts", "exchange", "local", "return", "combine")
+    # NVLink transport: dispatch stores rows into the owners' windows,
+    # "arrive" waits for every peer's rows, "return" stores the partial rows
+    # back and waits for the peers' partial rows
+    NVLINK_PHASES = ("dispatch", "arrive", "local", "return", "combine")
+
+    @property
+    def phases(self) -> tuple:
+        return self.NVLINK_PHASES if self.transport == "nvlink" else self.PHASES
 
     def _mark(self) -> None:
         if self.profile:
@@ -226,10 +234,11 @@ class Exl3ExpertParallel(torch.nn.Module):
     def phase_ms(self) -> dict:
         """Milliseconds of each phase of the last profiled step (synchronises)."""
         ev = self._events
-        if len(ev) != len(self.PHASES) + 1:
+        names = self.phases
+        if len(ev) != len(names) + 1:
             return {}
         ev[-1].synchronize()
-        return {n: ev[i].elapsed_time(ev[i + 1]) for i, n in enumerate(self.PHASES)}
+        return {n: ev[i].elapsed_time(ev[i + 1]) for i, n in enumerate(names)}
 
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_split: list[int], in_split: list[int]) -> None:
         if self.world == 1:
