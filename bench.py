@@ -555,13 +555,30 @@ def run_ep(args, rank, local_rank, world, which):
     total_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs))
     step_s = total_ms / args.steps / 1e3
 
-    # per-phase times: the EP step (CUDA events between phases) and, inside
-    # the local forward, the library's kernel phases
+    # per-phase times: the EP step (CUDA events between phases; with a graph,
+    # event nodes captured into a second graph of the same step, so the
+    # phases are timed as the graph runs them) and, inside the local
+    # forward, the library's kernel phases (eager)
     ep.profile = True
     ep_ph = []
-    for i in range(4):
-        step(i)
-        ep_ph.append(ep.phase_ms())
+    if graph is not None:
+        pgraph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(pgraph):
+            ep(sx, sw, sid, out=out)
+        for i in range(4):
+            flush.zero_()
+            x, ids, w = batches[i % NB]
+            sx.copy_(x)
+            sid.copy_(ids)
+            sw.copy_(w)
+            pgraph.replay()
+            ep_ph.append(ep.phase_ms())
+        del pgraph
+    else:
+        for i in range(4):
+            flush.zero_()
+            step(i)
+            ep_ph.append(ep.phase_ms())
     ep.profile = False
     _native.profile_enable(True, 2_000_000)
     loc = []

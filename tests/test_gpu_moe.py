@@ -119,6 +119,21 @@ def test_large_batch_split_prep(native, cuda, n_valid):
     _close(got, want)
 
 
+@pytest.mark.parametrize("n_experts", [6, 3])
+def test_prefill_gemm_split_k(native, cuda, n_experts):
+    """Few (tile, column block) items: each is split over K across up to four
+    CTAs whose fp32 partials the last one sums in split order before the
+    epilogue (gate rows, the fused up + SwiGLU epilogue and the weighted down
+    rows all run split).  Repeats must be bit-identical."""
+    import torch
+    pack, layer, x, ids, w = _setup(cuda, "cfg2", seed=55 + n_experts, tokens=16 * n_experts, n_experts=n_experts,
+                                    topk=2, hidden=2048, inter=1024, k_choices=(2, 3, 4), k_probs=None)
+    want = oracle.moe_eager(x, ids, w, _dense(pack))
+    got = _run(layer, cuda, x, ids, w, dtype=torch.float32)
+    _close(got, want)
+    assert np.array_equal(got, _run(layer, cuda, x, ids, w, dtype=torch.float32))
+
+
 def test_prefill_gemm_path_mixed_k_mul1_limit(native, cuda):
     import torch
     pack, layer, x, ids, w = _setup(cuda, "cfg3", seed=77, tokens=256, n_experts=10, hidden=384,

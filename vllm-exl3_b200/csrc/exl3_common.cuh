@@ -37,6 +37,7 @@ enum DevStatus : int {
     DEV_NULL_PTR = 3,       // null pointer in a pointer table
     DEV_WAIT_TIMEOUT = 4,   // an mbarrier wait exceeded its bound
     DEV_BAD_ROUTE = 5,      // routing table inconsistent (internal)
+    DEV_BAD_LAUNCH = 6,     // launch shape inconsistent with the kernel's needs (internal)
 };
 
 __device__ __forceinline__ void set_status(int* status, int code) {
@@ -376,8 +377,17 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
         : "memory");
 }
 
+// hint: bring [gmem_src, +bytes) into L2 (16-byte aligned, multiple of 16 bytes)
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(gmem_src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ void named_bar_arrive(int id, int threads) {
+    asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
 }
 
 // dtype codes of the C ABI

@@ -51,6 +51,10 @@ struct MoePlan {
     int64_t t128max = 0;   // max work tiles
     int tc_stages = 0;
     size_t tc_smem = 0;
+    // split-K ceiling per GEMM projection (gate/up, down): the kernel picks
+    // 1..ceiling on the device from the real tile count
+    int tc_split1 = 1, tc_split2 = 1;
+    size_t off_tcpart = 0, off_tccnt = 0;
     // offsets
     size_t off_status = 0, off_nslots = 0, off_slots = 0, off_route_pos = 0, off_sorted_tok = 0,
            off_sorted_route = 0, off_ntiles128 = 0, off_tiles128 = 0, off_g = 0, off_u = 0, off_x2 = 0,

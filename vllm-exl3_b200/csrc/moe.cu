@@ -76,6 +76,7 @@ struct WsPtrs {
     int* cnt1;
     int* cnt2;
     int* ntiles128;
+    float* tcpart;  // GEMM split-K partials
     int4* tiles128;  // {expert, first sorted row, rows <= tile_rows, 0}: the GEMM path's work tiles
     float* g;
     float* u;
@@ -102,6 +103,7 @@ static WsPtrs ws_ptrs(const MoePlan& p, void* ws) {
     w.cnt1 = reinterpret_cast<int*>(b + p.off_cnt1);
     w.cnt2 = reinterpret_cast<int*>(b + p.off_cnt2);
     w.ntiles128 = reinterpret_cast<int*>(b + p.off_ntiles128);
+    w.tcpart = reinterpret_cast<float*>(b + p.off_tcpart);
     w.tiles128 = reinterpret_cast<int4*>(b + p.off_tiles128);
     w.g = reinterpret_cast<float*>(b + p.off_g);
     w.u = reinterpret_cast<float*>(b + p.off_u);
@@ -220,17 +222,21 @@ __device__ void prep_layout(const PrepArgs& a, const int* cnt, int* poff, int* s
     __syncthreads();
 }
 
-// Stable placement of routes [r0, r1): route order within each expert.
-// run[e] holds each expert's next sorted row and is advanced; chunk[] is
-// scratch (per-expert totals of one 1024-route step, fast path).
-__device__ void prep_place(const PrepArgs& a, int64_t r0, int64_t r1, int64_t Rmax, int* run, int* chunk,
-                           unsigned short (*wcnt)[kFastRankExperts]) {
+__device__ __forceinline__ float route_weight(const PrepArgs& a, int64_t r) {
+    return (a.linear || a.batched) ? 1.f : load_as_float(a.weights, r, a.w_dtype);
+}
+
+// One 1024-route step of the stable placement: thread tid places route r
+// (local expert e, -1 = not local or past r1; weight wgt).  run[e] holds each
+// expert's next sorted row and is advanced; chunk[] is scratch (per-expert
+// totals of the step, fast path).  Whole CTA.
+__device__ __forceinline__ void prep_place_step(const PrepArgs& a, int64_t r, int64_t r1, int64_t Rmax, int e,
+                                                float wgt, int* run, int* chunk,
+                                                unsigned short (*wcnt)[kFastRankExperts]) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int E = a.n_local;
     const bool fast = E <= kFastRankExperts;
-    for (int64_t base = r0; base < r1; base += kPrepThreads) {
-        const int64_t r = base + tid;
-        const int e = r < r1 ? local_expert(a, r) : -1;
+    {
         const unsigned mask = __match_any_sync(0xffffffffu, e);
         const int rank = __popc(mask & ((1u << lane) - 1u));
         const int leader = __ffs(mask) - 1;
@@ -271,7 +277,7 @@ __device__ void prep_place(const PrepArgs& a, int64_t r0, int64_t r1, int64_t Rm
             a.w.sorted_tok[p] = int(r / a.topk);
             a.w.sorted_route[p] = int(r);
             a.w.sorted_exp[p] = e;
-            a.w.sorted_w[p] = (a.linear || a.batched) ? 1.f : load_as_float(a.weights, r, a.w_dtype);
+            a.w.sorted_w[p] = wgt;
         } else if (r < r1 && r < Rmax) {
             a.w.route_pos[r] = -1;
         }
@@ -280,6 +286,16 @@ __device__ void prep_place(const PrepArgs& a, int64_t r0, int64_t r1, int64_t Rm
             for (int x = tid; x < E; x += kPrepThreads) run[x] += chunk[x];
             __syncthreads();
         }
+    }
+}
+
+// Stable placement of routes [r0, r1): route order within each expert.
+__device__ void prep_place(const PrepArgs& a, int64_t r0, int64_t r1, int64_t Rmax, int* run, int* chunk,
+                           unsigned short (*wcnt)[kFastRankExperts]) {
+    for (int64_t base = r0; base < r1; base += kPrepThreads) {
+        const int64_t r = base + threadIdx.x;
+        const int e = r < r1 ? local_expert(a, r) : -1;
+        prep_place_step(a, r, r1, Rmax, e, e >= 0 ? route_weight(a, r) : 0.f, run, chunk, wcnt);
     }
 }
 
@@ -299,16 +315,35 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
     const int E = a.n_local;
     const int64_t R = prep_routes(a), Rmax = a.t_max * a.topk;
 
+    // every route's local expert and weight loaded once, up front (one
+    // memory round trip instead of one per 1024-route step and pass)
+    constexpr int kPer = int(kPrepSplitRoutes / kPrepThreads);
+    int ev[kPer];
+    float wv[kPer];
+    #pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int64_t r = int64_t(j) * kPrepThreads + tid;
+        ev[j] = r < R ? local_expert(a, r) : -1;
+    }
+    #pragma unroll
+    for (int j = 0; j < kPer; ++j) wv[j] = ev[j] >= 0 ? route_weight(a, int64_t(j) * kPrepThreads + tid) : 0.f;
+
     for (int i = tid; i < a.cnt1_n; i += kPrepThreads) a.w.cnt1[i] = 0;
     for (int i = tid; i < a.cnt2_n; i += kPrepThreads) a.w.cnt2[i] = 0;
     for (int e = tid; e < E; e += kPrepThreads) cnt[e] = 0;
     __syncthreads();
-    prep_histogram(a, 0, R, cnt);
+    #pragma unroll
+    for (int j = 0; j < kPer; ++j)
+        if (ev[j] >= 0) atomicAdd(&cnt[ev[j]], 1);
     __syncthreads();
     prep_layout(a, cnt, poff, sh32);
     for (int e = tid; e < E; e += kPrepThreads) cnt[e] = poff[e];  // running positions
     __syncthreads();
-    prep_place(a, 0, R, Rmax, cnt, poff, wcnt);
+    #pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        if (int64_t(j) * kPrepThreads >= R) break;  // CTA-uniform
+        prep_place_step(a, int64_t(j) * kPrepThreads + tid, R, Rmax, ev[j], wv[j], cnt, poff, wcnt);
+    }
     for (int64_t r = R + tid; r < Rmax; r += kPrepThreads) a.w.route_pos[r] = -1;
 }
 
@@ -445,7 +480,9 @@ __global__ void __launch_bounds__(256) rotate_rows_mma_kernel(const RotArgs a, c
             hs[j][q] = __floats2half2_rn((__popc(k & n) & 1) ? -1.f : 1.f, (__popc((k + 1) & n) & 1) ? -1.f : 1.f);
         }
     }
-    for (int64_t it = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; it < ngroups * nkb;
+    // warp w of CTA b takes items w * gridDim + b, ...: a small batch
+    // spreads over every SM instead of filling the first CTAs' warps
+    for (int64_t it = int64_t(threadIdx.x >> 5) * gridDim.x + blockIdx.x; it < ngroups * nkb;
          it += (int64_t(gridDim.x) * blockDim.x) >> 5) {
         const int64_t p0 = (it / nkb) * 16;
         const int kb = int(it % nkb);
@@ -1172,8 +1209,19 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
         p.off_x2 = take(linear ? 0 : size_t(p.rpad) * inter * 2);
         p.off_yd = take(linear ? 0 : size_t(p.rpad) * hidden * 4);
         p.off_a2 = p.off_part1 = p.off_part2 = take(0);
-        p.off_cnt1 = p.off_cnt2 = take(0);
         p.nsplit1 = p.nsplit2 = 1;
+        // split-K for the fused layer when few (tile, column block) items
+        // can exist: fp32 partials per split and one counter per item
+        if (!linear) {
+            p.tc_split1 = tc_split_ceiling(p.t128max * p.ncb1, hidden, grid);
+            p.tc_split2 = tc_split_ceiling(p.t128max * p.ncb2, inter, grid);
+        }
+        const int64_t items = p.t128max * std::max(p.ncb1, p.ncb2);
+        const bool split = p.tc_split1 > 1 || p.tc_split2 > 1;
+        const int64_t part_items = std::max(p.t128max * p.ncb1 * p.tc_split1, p.t128max * p.ncb2 * p.tc_split2);
+        p.off_tcpart = take(split ? size_t(part_items) * p.tile_m * 128 * 4 : 0);
+        p.off_tccnt = p.off_cnt1 = take(split ? size_t(items) * 4 : 0);
+        p.off_cnt2 = take(0);
     } else {
         p.off_xr = take(size_t(nproj1) * (hidden / 128) * p.rpad * x_pitch(p.dup) * 2);
         p.off_a2 = take(linear ? 0 : size_t(inter / 128) * p.rpad * x_pitch(p.dup) * 2);
@@ -1258,13 +1306,16 @@ static cudaError_t run_moe_gemm(const MoePlan& p, const MoeCall& c, const WsPtrs
     TcArgs t{};
     t.status = w.status;
     t.kmax = p.kmax;
-    t.stages = p.tc_stages;
+    t.stage_mem = int(p.tc_smem - 1024 - 256);
     t.ntiles = w.ntiles128;
     t.tiles = w.tiles128;
     t.sorted_w = w.sorted_w;
     t.sorted_tok = w.sorted_tok;
     t.scatter_idx = c.scatter_idx;
     t.scatter_w = static_cast<const __half*>(c.scatter_w);
+    t.ctas = nsm * kCtasPerSm;
+    t.part = w.tcpart;
+    t.cnt = w.cnt1;
     cudaError_t e;
     if (p.linear) {
         if (c.batched) return cudaErrorNotSupported;  // callers route batched linears to the GEMV path
@@ -1286,8 +1337,11 @@ static cudaError_t run_moe_gemm(const MoePlan& p, const MoeCall& c, const WsPtrs
     t.epi = TC_EPI_ROWS;
     t.proj = c.gate;
     t.yrows = w.g;
+    t.max_split = p.tc_split1;
     const int mt = p.tile_m / 128;
-    if ((e = run_tc_gemm(c.cb, mt, t, w.xr, p.rpad, p.t128max * t.ncb, p.tc_smem, s)) != cudaSuccess) return e;
+    if ((e = run_tc_gemm(c.cb, mt, t, w.xr, p.rpad, tc_grid(p.t128max * t.ncb, t.max_split, t.ctas), p.tc_smem, s)) !=
+        cudaSuccess)
+        return e;
     // up, fused with SwiGLU and the down input rotation (reads the gate rows)
     t.proj = c.up;
     t.epi = TC_EPI_UPACT;
@@ -1296,8 +1350,8 @@ static cudaError_t run_moe_gemm(const MoePlan& p, const MoeCall& c, const WsPtrs
     t.down = c.down;
     t.limit = c.limit;
     t.act = c.act;
-    if ((e = run_tc_gemm(c.cb, mt, t, w.xr + size_t(p.rpad) * p.hidden, p.rpad, p.t128max * t.ncb, p.tc_smem,
-                         s)) != cudaSuccess)
+    if ((e = run_tc_gemm(c.cb, mt, t, w.xr + size_t(p.rpad) * p.hidden, p.rpad,
+                         tc_grid(p.t128max * t.ncb, t.max_split, t.ctas), p.tc_smem, s)) != cudaSuccess)
         return e;
     prof_mark(s);
     prof_mark(s);  // the activation phase is part of the up launch
@@ -1307,7 +1361,10 @@ static cudaError_t run_moe_gemm(const MoePlan& p, const MoeCall& c, const WsPtrs
     t.ncb = p.hidden / 128;
     t.epi = TC_EPI_DOWN;
     t.yrows = w.yd;
-    if ((e = run_tc_gemm(c.cb, mt, t, w.x2, p.rpad, p.t128max * t.ncb, p.tc_smem, s)) != cudaSuccess) return e;
+    t.max_split = p.tc_split2;
+    if ((e = run_tc_gemm(c.cb, mt, t, w.x2, p.rpad, tc_grid(p.t128max * t.ncb, t.max_split, t.ctas), p.tc_smem, s)) !=
+        cudaSuccess)
+        return e;
     prof_mark(s);
     const int64_t total = p.t_max * (p.hidden / 4);
     const int64_t blocks = std::min<int64_t>((total + 255) / 256, int64_t(nsm) * 16);
@@ -1341,7 +1398,8 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     pa.n_local = p.n_local;
     pa.linear = (p.linear && !c.batched) ? 1 : 0;
     pa.batched = c.batched ? 1 : 0;
-    pa.cnt1_n = p.gemm ? 0 : int(p.smax * p.ncb1);
+    pa.cnt1_n = p.gemm ? ((p.tc_split1 > 1 || p.tc_split2 > 1) ? int(p.t128max * std::max(p.ncb1, p.ncb2)) : 0)
+                       : int(p.smax * p.ncb1);
     pa.cnt2_n = (p.linear || p.gemm) ? 0 : int(p.smax * p.ncb2);
     pa.tile_rows = p.tile_m;
     pa.w = w;
@@ -1373,16 +1431,11 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     ra.prerotated = c.prerotated ? 1 : 0;
     ra.rowmajor = p.gemm ? 1 : 0;
     ra.dup = p.dup ? 1 : 0;
-    if (p.gemm) {
-        if (c.x_dtype == DT_F32) launch_rotate_rows<DT_F32>(ra, w.sorted_exp, nsm * 8, s);
-        else if (c.x_dtype == DT_F16) launch_rotate_rows<DT_F16>(ra, w.sorted_exp, nsm * 8, s);
-        else launch_rotate_rows<DT_BF16>(ra, w.sorted_exp, nsm * 8, s);
-    }
-    else {
-        if (c.x_dtype == DT_F32) launch_rotate_rows<DT_F32>(ra, w.sorted_exp, nsm * 8, s);
-        else if (c.x_dtype == DT_F16) launch_rotate_rows<DT_F16>(ra, w.sorted_exp, nsm * 8, s);
-        else launch_rotate_rows<DT_BF16>(ra, w.sorted_exp, nsm * 8, s);
-    }
+    // one resident wave (two 256-thread CTAs per SM at <= 128 registers);
+    // the warps loop over the (16-row group, 128-column block) items
+    if (c.x_dtype == DT_F32) launch_rotate_rows<DT_F32>(ra, w.sorted_exp, nsm * 2, s);
+    else if (c.x_dtype == DT_F16) launch_rotate_rows<DT_F16>(ra, w.sorted_exp, nsm * 2, s);
+    else launch_rotate_rows<DT_BF16>(ra, w.sorted_exp, nsm * 2, s);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     prof_mark(s);
     if (p.gemm) return run_moe_gemm(p, c, w, nsm, s);

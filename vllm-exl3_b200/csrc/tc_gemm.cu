@@ -51,6 +51,11 @@ constexpr int kTcKt = kTcK / 16;            // k-tiles per stage
 constexpr int kTcSwB = kTcK * 2;            // swizzle span = row bytes
 constexpr int kTcABytes = kTcM * kTcK * 2;  // 16 KB per 128-row half
 constexpr int kTcBBytes = kTcN * kTcK * 2;  // 16 KB
+constexpr int kTcMaxStages = 8;
+// K stages of trellis words prefetched into L2 ahead of the stage being
+// loaded: the ring is only 2-3 stages deep, so without it every stage pays a
+// DRAM round trip for its weights
+constexpr int kTcPrefetch = 8;
 
 __device__ __forceinline__ uint32_t tc_b_offset(int row, int k) {
     if constexpr (kTcSwB == 128) return sw128_offset(row, k);
@@ -151,29 +156,60 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ TcArgs a) {
     extern __shared__ __align__(1024) char tc_smem_raw[];
     char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
-    const int S = a.stages;
-    const size_t stage_bytes = tc_stage_bytes(a.kmax, MT);
-    constexpr int kBOff = MT * kTcABytes;             // decoded weight tile
-    constexpr int kRawOff = MT * kTcABytes + kTcBBytes;  // raw trellis words
+
+    const int64_t n_base = int64_t(*a.ntiles) * a.ncb;
+    const int nst_all = a.in_f / kTcK;
+    // split-K count (CTA-uniform): the smallest s <= max_split minimising the
+    // waves per unit of work, ceil(n_base * s / ctas) / s
+    int nsplit = 1;
+    if (a.max_split > 1 && n_base > 0) {
+        int64_t best_w = (n_base + a.ctas - 1) / a.ctas;  // waves x s, compared as fractions
+        for (int sp = 2; sp <= a.max_split && n_base * sp <= int64_t(gridDim.x); ++sp) {
+            const int64_t w = (n_base * sp + a.ctas - 1) / a.ctas;
+            if (w * nsplit < best_w * sp) {
+                best_w = w;
+                nsplit = sp;
+            }
+        }
+    }
+    const int64_t n_items = n_base * nsplit;
+    // the grid is sized for the most tiles the routing could produce; CTAs
+    // without work take the LOW block indices, which the hardware dispatches
+    // first, so they exit while every SM slot is still free instead of
+    // trickling through the few slots the working CTAs leave
+    const int64_t item = int64_t(gridDim.x) - 1 - blockIdx.x;
+    if (item >= n_items) return;  // whole CTA, before any barrier
+    const int64_t base = item / nsplit;  // (tile, column block)
+    const int split = int(item % nsplit);
+    const int4 T = a.tiles[base / a.ncb];
+    const int cb = int(base % a.ncb);
+    const int e = T.x, p0 = T.y, rows = T.z;
+    const int nh = (MT == 2 && rows > 128) ? 2 : 1;  // halves holding rows (CTA-uniform)
+
+    // stage ring sized for this tile: a tile with one 128-row half needs no
+    // room for a second activation box, which buys a deeper ring
+    const size_t stage_bytes = tc_stage_bytes(a.kmax, nh);
+    const int S = int(min(size_t(kTcMaxStages), size_t(a.stage_mem) / stage_bytes));
+    if (S < 2 || size_t(S) * stage_bytes < size_t(128) * kTcEpiPitch * 4) {  // host sizing error: refuse
+        if (threadIdx.x == 0) set_status(a.status, DEV_BAD_LAUNCH);
+        return;
+    }
+    const int kBOff = nh * kTcABytes;             // decoded weight tile
+    const int kRawOff = nh * kTcABytes + kTcBBytes;  // raw trellis words
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(S) * stage_bytes);
     uint64_t* dec = full + S;
     uint64_t* empty = dec + S;
     uint64_t* accf = empty + S;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
-    const int64_t n_items = int64_t(*a.ntiles) * a.ncb;
-    const int64_t item = blockIdx.x;
-    if (item >= n_items) return;  // whole CTA, before any barrier
-    const int4 T = a.tiles[item / a.ncb];
-    const int cb = int(item % a.ncb);
-    const int e = T.x, p0 = T.y, rows = T.z;
     const int K = proj_k(a.proj, e);
     const uint16_t* trellis = proj_trellis(a.proj, e);
     const bool ok = K >= 2 && K <= a.kmax && trellis != nullptr && (reinterpret_cast<uintptr_t>(trellis) & 15) == 0;
-    const int nst = a.in_f / kTcK;
+    const int ks0 = int(int64_t(split) * nst_all / nsplit);  // this split's K stages [ks0, ks0 + nst)
+    const int nst = int(int64_t(split + 1) * nst_all / nsplit) - ks0;
     const int ntiles_out = a.out_f / 16;
-    const int nh = (MT == 2 && rows > 128) ? 2 : 1;  // halves holding rows (CTA-uniform)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -195,19 +231,30 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
 
     if (warp == 0) {
         if (lane == 0) {
+            const int tw = 16 * K;
+            // L2 prefetch of K stage ksr's trellis words (four 256·K-byte runs)
+            auto prefetch = [&](int ksr) {
+                if (!ok || ksr >= nst) return;
+                const int kg = ks0 + ksr;
+                for (int kk = 0; kk < kTcKt; ++kk)
+                    bulk_prefetch_l2(trellis + (int64_t(kg * kTcKt + kk) * ntiles_out + int64_t(cb) * 8) * tw,
+                                     uint32_t(256 * K));
+            };
+            for (int i = 0; i < kTcPrefetch; ++i) prefetch(i);
             int s = 0;
             uint32_t ph = 0u;
             for (int ks = 0; ks < nst; ++ks, ring_next(s, ph, S)) {
+                prefetch(ks + kTcPrefetch);
                 if (!tc_wait(&empty[s], ph ^ 1u, a.status, abort_flag)) break;
                 char* st = smem + size_t(s) * stage_bytes;
                 const uint32_t rawb = ok ? uint32_t(kTcKt * 256 * K) : 0u;
                 mbar_arrive_expect_tx(&full[s], uint32_t(nh * kTcABytes) + rawb);
-                for (int h = 0; h < nh; ++h) tma_load_2d(st + h * kTcABytes, &amap, ks * kTcK, p0 + 128 * h, &full[s]);
+                const int kg = ks0 + ks;  // K stage within the projection
+                for (int h = 0; h < nh; ++h) tma_load_2d(st + h * kTcABytes, &amap, kg * kTcK, p0 + 128 * h, &full[s]);
                 if (ok) {
-                    const int tw = 16 * K;
                     for (int kk = 0; kk < kTcKt; ++kk) {
                         const uint16_t* src =
-                            trellis + (int64_t(ks * kTcKt + kk) * ntiles_out + int64_t(cb) * 8) * tw;
+                            trellis + (int64_t(kg * kTcKt + kk) * ntiles_out + int64_t(cb) * 8) * tw;
                         bulk_g2s(st + kRawOff + size_t(kk) * 256 * K, src, uint32_t(256 * K), &full[s]);
                     }
                 }
@@ -235,6 +282,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
             }
             umma_commit(accf);  // also covers the no-MMA case: arrives at once
         }
+        // free TMEM as soon as the epilogue warps have read the accumulators
+        // (barrier 2: warp 1 + warps 2-5); the deallocation takes
+        // microseconds and would otherwise sit on every CTA's exit path
+        __syncwarp();
+        named_bar_sync(2, 5 * 32);
+        tc_fence_after();
+        tmem_dealloc(taddr, kTcN * MT);
     } else {
         const int d = warp - 2;  // 16-column tile of the 128-column block
         const int kd = ok ? K : 0;
@@ -260,7 +314,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
         float sv[4];
         #pragma unroll
         for (int i = 0; i < 4; ++i) sv[i] = __half2float(svh[lane + 32 * i]) * kHadNorm;
-        for (int h = 0; h < nh; ++h) {
+        const int et = threadIdx.x - 64;  // epilogue thread 0..255
+        // accumulator half h: TMEM -> epilogue tile (warps 2-5, one TMEM lane quarter each)
+        auto tile_from_tmem = [&](int h) {
             if (warp < 6) {
                 if (h == 0) {
                     // on an abort still wait (bounded) for issued MMAs before TMEM is read or freed
@@ -277,9 +333,83 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                     for (int i = 0; i < 32; ++i) ep[row * kTcEpiPitch + 32 * c4 + i] = part[i];
                 }
                 tc_fence_before();
+                if (h == nh - 1) named_bar_arrive(2, 5 * 32);  // last accumulator read: warp 1 may free TMEM
             }
             named_bar_sync(1, 8 * 32);
+        };
+        bool run_epi = true;
+        float* parts = nullptr;
+        if (nsplit > 1) {
+            // every split stores its fp32 partial; the last split of the
+            // (tile, column block) to arrive sums them in split order
+            parts = a.part + size_t(base) * a.max_split * (128 * MT * 128);
+            for (int h = 0; h < nh; ++h) {
+                tile_from_tmem(h);
+                const int rows_h = min(128, rows - 128 * h);
+                float4* dst = reinterpret_cast<float4*>(parts + (size_t(split) * MT + h) * (128 * 128));
+                for (int i = et; i < rows_h * 32; i += 256) {
+                    const float* src = ep + (i >> 5) * kTcEpiPitch + 4 * (i & 31);
+                    dst[i] = make_float4(src[0], src[1], src[2], src[3]);
+                }
+                named_bar_sync(1, 8 * 32);  // the tile is refilled next
+            }
+            __threadfence();
+            named_bar_sync(1, 8 * 32);
+            if (et == 0) {
+                const int prev = atomicAdd(&a.cnt[base], 1);
+                const bool last = prev == nsplit - 1;
+                if (last) a.cnt[base] = 0;  // ready for the next launch
+                *last_flag = last ? 1 : 0;
+            }
+            named_bar_sync(1, 8 * 32);
+            run_epi = *last_flag != 0;
+            if (run_epi) __threadfence();
+        }
+        for (int h = 0; run_epi && h < nh; ++h) {
             const int rows_h = min(128, rows - 128 * h);
+            if (nsplit > 1) {
+                // sum in split order; four 16-byte loads per split in flight
+                // per thread (one L2 round trip per 1024 vectors, not per element)
+                const float4* src = reinterpret_cast<const float4*>(parts + size_t(h) * (128 * 128));
+                const size_t sstride = size_t(MT) * (128 * 128) / 4;  // float4s between splits
+                for (int i0 = et; i0 < rows_h * 32; i0 += 4 * 256) {
+                    float4 v[4];
+                    #pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int i = i0 + 256 * u;
+                        v[u] = i < rows_h * 32 ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                    for (int sp = 1; sp < nsplit; ++sp) {
+                        float4 w[4];
+                        #pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int i = i0 + 256 * u;
+                            w[u] = i < rows_h * 32 ? __ldcg(src + sp * sstride + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+                        #pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            v[u].x += w[u].x;
+                            v[u].y += w[u].y;
+                            v[u].z += w[u].z;
+                            v[u].w += w[u].w;
+                        }
+                    }
+                    #pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int i = i0 + 256 * u;
+                        if (i < rows_h * 32) {
+                            float* d = ep + (i >> 5) * kTcEpiPitch + 4 * (i & 31);
+                            d[0] = v[u].x;
+                            d[1] = v[u].y;
+                            d[2] = v[u].z;
+                            d[3] = v[u].w;
+                        }
+                    }
+                }
+                named_bar_sync(1, 8 * 32);
+            } else {
+                tile_from_tmem(h);
+            }
             // UPACT: the gate rows are read from global memory; keep two rows
             // in flight ahead of the one being processed (latency hiding)
             float gq[2][4];
@@ -359,11 +489,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
             if (h + 1 < nh) named_bar_sync(1, 8 * 32);  // the tile is refilled with the next half
         }
     }
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(taddr, kTcN * MT);
-    }
 }
 
 // ---------------------------------------------------------------------------
@@ -406,12 +531,19 @@ bool tc_pick_stages(int kmax, int mt, int& stages, size_t& smem) {
     const size_t budget = (228 * 1024) / 2 - 1024 /* per-CTA reserve */ - 1024 /* alignment */ - 256;
     const size_t sb = tc_stage_bytes(kmax, mt);
     const size_t epi = size_t(128) * kTcEpiPitch * 4;
-    int s = int(std::min<size_t>(6, budget / sb));
+    int s = int(std::min<size_t>(kTcMaxStages, budget / sb));
     if (size_t(s) * sb < epi) s = int((epi + sb - 1) / sb);
     if (s < 2 || size_t(s) * sb > budget) return false;
     stages = s;
-    smem = size_t(s) * sb + 1024 + 256;
+    // the whole budget: a tile with fewer rows than the launch's widest
+    // sizes a deeper ring from the same memory
+    smem = budget + 1024 + 256;
     return true;
+}
+
+int tc_split_ceiling(int64_t max_items, int in_f, int ctas) {
+    if (max_items >= 2 * int64_t(ctas)) return 1;
+    return std::max(1, std::min(kTcMaxSplit, in_f / kTcK / 8));
 }
 
 cudaError_t run_tc_gemm(int cb, int mt, const TcArgs& a, const void* act, int64_t act_rows, int64_t grid,

@@ -227,7 +227,9 @@ class Exl3ExpertParallel(torch.nn.Module):
 
     def _mark(self) -> None:
         if self.profile:
-            ev = torch.cuda.Event(enable_timing=True)
+            # inside a CUDA-graph capture the marks become event-record nodes,
+            # so a replay of the captured step times its own phases
+            ev = torch.cuda.Event(enable_timing=True, external=torch.cuda.is_current_stream_capturing())
             ev.record()
             self._events.append(ev)
 
