@@ -39,3 +39,18 @@ def native(cuda):
     from exl3_b200 import _native
     _native.load()
     return vllm_exl3_c
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean(request):
+    """GPU tests: the shared workspace's device status word must stay 0 (a
+    kernel that skipped work or gave up a bounded wait records a code there
+    and would otherwise pass unnoticed).  Tests that provoke a code clear it."""
+    if request.node.get_closest_marker("gpu") is None or not cuda_ok():
+        yield
+        return
+    import vllm_exl3_c
+    vllm_exl3_c.device_status(clear=True)
+    yield
+    st = vllm_exl3_c.device_status(clear=True)
+    assert st == 0, f"device status word {st} after the test"

@@ -56,7 +56,7 @@ struct MoePlan {
     int tc_split1 = 1, tc_split2 = 1;
     size_t off_tcpart = 0, off_tccnt = 0;
     // offsets
-    size_t off_status = 0, off_nslots = 0, off_slots = 0, off_route_pos = 0, off_sorted_tok = 0,
+    size_t off_status = 0, off_nslots = 0, off_sched = 0, off_slots = 0, off_route_pos = 0, off_sorted_tok = 0,
            off_sorted_route = 0, off_ntiles128 = 0, off_tiles128 = 0, off_g = 0, off_u = 0, off_x2 = 0,
            off_sorted_exp = 0, off_sorted_w = 0, off_xr = 0, off_a2 = 0, off_yd = 0,
            off_part1 = 0, off_part2 = 0, off_cnt1 = 0, off_cnt2 = 0, off_hist = 0;

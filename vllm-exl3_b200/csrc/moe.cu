@@ -77,6 +77,7 @@ struct WsPtrs {
     int* cnt2;
     int* ntiles128;
     float* tcpart;  // GEMM split-K partials
+    int* sched;     // GEMV dynamic item counters [gate/up or linear, down]
     int4* tiles128;  // {expert, first sorted row, rows <= tile_rows, 0}: the GEMM path's work tiles
     float* g;
     float* u;
@@ -104,6 +105,7 @@ static WsPtrs ws_ptrs(const MoePlan& p, void* ws) {
     w.cnt2 = reinterpret_cast<int*>(b + p.off_cnt2);
     w.ntiles128 = reinterpret_cast<int*>(b + p.off_ntiles128);
     w.tcpart = reinterpret_cast<float*>(b + p.off_tcpart);
+    w.sched = reinterpret_cast<int*>(b + p.off_sched);
     w.tiles128 = reinterpret_cast<int4*>(b + p.off_tiles128);
     w.g = reinterpret_cast<float*>(b + p.off_g);
     w.u = reinterpret_cast<float*>(b + p.off_u);
@@ -330,6 +332,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
 
     for (int i = tid; i < a.cnt1_n; i += kPrepThreads) a.w.cnt1[i] = 0;
     for (int i = tid; i < a.cnt2_n; i += kPrepThreads) a.w.cnt2[i] = 0;
+    if (tid < 2) a.w.sched[tid] = 0;
     for (int e = tid; e < E; e += kPrepThreads) cnt[e] = 0;
     __syncthreads();
     #pragma unroll
@@ -371,6 +374,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_plan_kernel(const PrepArgs 
     const int64_t R = prep_routes(a), Rmax = a.t_max * a.topk;
     for (int i = tid; i < a.cnt1_n; i += kPrepThreads) a.w.cnt1[i] = 0;
     for (int i = tid; i < a.cnt2_n; i += kPrepThreads) a.w.cnt2[i] = 0;
+    if (tid < 2) a.w.sched[tid] = 0;
     for (int e = tid; e < E; e += kPrepThreads) {
         int n = 0;
         for (int c = 0; c < nchunks; ++c) n += a.w.hist[int64_t(c) * E + e];
@@ -619,12 +623,16 @@ struct GemvArgs {
     // split-K
     float* part;
     int* cnt;
+    int* sched;  // dynamic item counter (zeroed by the routing prep)
 };
+
+constexpr int kGemvItemQueue = 16;  // > the most stages the producer runs ahead
 
 struct GemvSmem {
     uint64_t* full;
     uint64_t* empty;
     int* flags;  // [0] abort, [1] last-of-group
+    int* items;  // [kGemvItemQueue] item ids the producer claimed, in order (-1: no more)
     float* ys;   // [NPROJ][16][kYsPitch]
     char* stages;
 };
@@ -638,7 +646,7 @@ __host__ __device__ inline size_t gemv_stage_bytes(int nproj, int kmax, bool dup
     return (gemv_trellis_bytes(nproj, kmax) + size_t(nproj) * x_slice(dup) + 127) & ~size_t(127);
 }
 __host__ __device__ inline size_t gemv_fixed_bytes(int nproj, int stages) {
-    const size_t bars = (size_t(stages) * 2 * 8 + 8 * 4 + 127) & ~size_t(127);
+    const size_t bars = (size_t(stages) * 2 * 8 + 8 * 4 + kGemvItemQueue * 4 + 127) & ~size_t(127);
     const size_t ys = (size_t(nproj) * 16 * kYsPitch * 4 + 127) & ~size_t(127);
     return bars + ys;
 }
@@ -648,7 +656,8 @@ __device__ __forceinline__ GemvSmem gemv_smem(char* base, int nproj, int stages)
     s.full = reinterpret_cast<uint64_t*>(base);
     s.empty = s.full + stages;
     s.flags = reinterpret_cast<int*>(s.empty + stages);
-    const size_t bars = (size_t(stages) * 2 * 8 + 8 * 4 + 127) & ~size_t(127);
+    s.items = s.flags + 8;
+    const size_t bars = (size_t(stages) * 2 * 8 + 8 * 4 + kGemvItemQueue * 4 + 127) & ~size_t(127);
     s.ys = reinterpret_cast<float*>(base + bars);
     s.stages = base + gemv_fixed_bytes(nproj, stages);
     return s;
@@ -822,8 +831,14 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
         uint32_t q = 0;   // stages issued
         int ps = 0;       // ring slot and parity of stage q
         uint32_t pph = 0u;
-        for (int64_t it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
+        // items: the CTA's own first, then claimed from the shared counter
+        // (dynamic: SMs that finish early take more), each published in the
+        // item queue before its first stage is issued
+        uint32_t jq = 0;
+        for (int64_t it = blockIdx.x; it < n_items && !*abort_flag;
+             it = int64_t(gridDim.x) + atomicAdd(a.sched, 1), ++jq) {
             const ItemInfo I = gemv_item(a, it);
+            sm.items[jq % kGemvItemQueue] = int(it);
             bool ok[NPROJ];
             int Kp[NPROJ];
             const uint16_t* tp[NPROJ];
@@ -863,11 +878,20 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 }
             }
         }
-        // drain: every issued stage must land before the CTA exits
+        // drain: every issued stage must land before the CTA exits.  This
+        // comes before the end marker below, which advances the full barrier
+        // of slot q % S, the slot of stage q - S: a parity wait for that
+        // stage after the marker would see the barrier two phases on.
         const uint32_t first = q > uint32_t(S) ? q - uint32_t(S) : 0u;
         for (uint32_t r = first; r < q; ++r) {
             const int s = int(r % uint32_t(S));
             mbar_wait(&sm.full[s], (r / uint32_t(S)) & 1u, a.status);
+        }
+        // no more items: publish the end marker through the next ring slot
+        // (an arrival without data, once the slot's previous use is consumed)
+        if (guarded_wait(&sm.empty[ps], pph ^ 1u, a.status, abort_flag)) {
+            sm.items[jq % kGemvItemQueue] = -1;
+            mbar_arrive(&sm.full[ps]);
         }
         return;
     }
@@ -879,7 +903,11 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
     const uint32_t xs_lane = uint32_t(brow * XP * 2 + ((lane >> 3) & 1) * 16);
     int cs = 0;  // ring slot and parity of the next stage
     uint32_t cph = 0u;
-    for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+    for (uint32_t jc = 0;; ++jc) {
+        // the next stage's arrival publishes its item (or the end marker)
+        if (!guarded_wait(&sm.full[cs], cph, a.status, abort_flag)) break;
+        const int it = sm.items[jc % kGemvItemQueue];
+        if (it < 0) break;
         const ItemInfo I = gemv_item(a, it);
         bool ok[NPROJ];
         int Kp[NPROJ];
@@ -1191,6 +1219,7 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     };
     p.off_status = take(64);
     p.off_nslots = take(64);
+    p.off_sched = take(64);
     p.off_slots = take(size_t(p.smax) * 16);
     p.off_route_pos = take(size_t(p.routes) * 4);
     p.off_sorted_tok = take(size_t(p.rpad) * 4);
@@ -1466,6 +1495,7 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
         g.y_dtype = c.out_dtype;
         g.part = w.part1;
         g.cnt = w.cnt1;
+        g.sched = w.sched;
         e = c.batched ? launch_gemv<1, EPI_ROUTE>(c.cb, g, p.grid1, p.smem1, s)
                       : launch_gemv<1, EPI_LINEAR>(c.cb, g, p.grid1, p.smem1, s);
         prof_mark(s);
@@ -1487,6 +1517,7 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     g.act = c.act;
     g.part = w.part1;
     g.cnt = w.cnt1;
+    g.sched = w.sched;
     if ((e = launch_gemv<2, EPI_GATEUP>(c.cb, g, p.grid1, p.smem1, s)) != cudaSuccess) return e;
     prof_mark(s);
 
@@ -1503,6 +1534,7 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     d.yd = w.yd;
     d.part = w.part2;
     d.cnt = w.cnt2;
+    d.sched = w.sched + 1;
     if ((e = launch_gemv<1, EPI_DOWN>(c.cb, d, p.grid2, p.smem2, s)) != cudaSuccess) return e;
     prof_mark(s);
 

@@ -156,5 +156,6 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     buf = _ws_cache.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        buf[:256].zero_()  # the device status word starts clean
         _ws_cache[key] = buf
     return buf
