@@ -377,11 +377,6 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
         : "memory");
 }
 
-// hint: bring [gmem_src, +bytes) into L2 (16-byte aligned, multiple of 16 bytes)
-__device__ __forceinline__ void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(gmem_src), "r"(bytes) : "memory");
-}
-
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
 }

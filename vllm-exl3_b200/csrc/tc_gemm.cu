@@ -52,10 +52,6 @@ constexpr int kTcSwB = kTcK * 2;            // swizzle span = row bytes
 constexpr int kTcABytes = kTcM * kTcK * 2;  // 16 KB per 128-row half
 constexpr int kTcBBytes = kTcN * kTcK * 2;  // 16 KB
 constexpr int kTcMaxStages = 8;
-// K stages of trellis words prefetched into L2 ahead of the stage being
-// loaded: the ring is only 2-3 stages deep, so without it every stage pays a
-// DRAM round trip for its weights
-constexpr int kTcPrefetch = 8;
 
 __device__ __forceinline__ uint32_t tc_b_offset(int row, int k) {
     if constexpr (kTcSwB == 128) return sw128_offset(row, k);
@@ -232,19 +228,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
     if (warp == 0) {
         if (lane == 0) {
             const int tw = 16 * K;
-            // L2 prefetch of K stage ksr's trellis words (four 256·K-byte runs)
-            auto prefetch = [&](int ksr) {
-                if (!ok || ksr >= nst) return;
-                const int kg = ks0 + ksr;
-                for (int kk = 0; kk < kTcKt; ++kk)
-                    bulk_prefetch_l2(trellis + (int64_t(kg * kTcKt + kk) * ntiles_out + int64_t(cb) * 8) * tw,
-                                     uint32_t(256 * K));
-            };
-            for (int i = 0; i < kTcPrefetch; ++i) prefetch(i);
             int s = 0;
             uint32_t ph = 0u;
             for (int ks = 0; ks < nst; ++ks, ring_next(s, ph, S)) {
-                prefetch(ks + kTcPrefetch);
                 if (!tc_wait(&empty[s], ph ^ 1u, a.status, abort_flag)) break;
                 char* st = smem + size_t(s) * stage_bytes;
                 const uint32_t rawb = ok ? uint32_t(kTcKt * 256 * K) : 0u;
