@@ -639,7 +639,7 @@ def run_ep(args, rank, local_rank, world, which):
     evs = e2e(args.steps)
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs))
-    launches = (2 + nloc + 1) if args.ep_transport == "nccl" else (3 + 1 + nloc + 2 + 1 + 2)
+    launches = (2 + nloc + 1) if args.ep_transport == "nccl" else (2 + 1 + nloc + 1 + 1 + 1)
     graph_used = graph is not None
     del graph
     torch.cuda.synchronize(dev)

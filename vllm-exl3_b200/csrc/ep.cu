@@ -50,12 +50,37 @@ struct EpPlanArgs {
     int64_t capacity;  // > 0: rank g's pairs start at row g * capacity
 };
 
+// A token's routes, loaded together (one memory round trip, not one per
+// route): up to kEpRegTopk in registers; wider top-k reads the rest in place.
+constexpr int kEpRegTopk = 16;
+
+struct TokenRoutes {
+    int32_t id[kEpRegTopk];  // global expert id, -1 if invalid or past topk
+};
+
+__device__ __forceinline__ int64_t route_id(const EpPlanArgs& a, const TokenRoutes& r, int64_t t, int k) {
+    if (k < kEpRegTopk) return r.id[k];
+    const int64_t id = load_id(a.ids, t * a.topk + k, a.ids_dtype);
+    return (id >= 0 && id < a.n_global) ? id : -1;
+}
+
+__device__ __forceinline__ void load_routes(const EpPlanArgs& a, int64_t t, bool live, TokenRoutes& r) {
+    #pragma unroll
+    for (int k = 0; k < kEpRegTopk; ++k) {
+        const int64_t id = (live && k < a.topk) ? load_id(a.ids, t * a.topk + k, a.ids_dtype) : -1;
+        r.id[k] = (id >= 0 && id < a.n_global) ? int32_t(id) : -1;
+    }
+}
+
 // bit g set <=> a route of token t is owned by rank g (invalid ids own nothing)
-__device__ __forceinline__ uint64_t token_ranks(const EpPlanArgs& a, int64_t t, int64_t epr) {
+__device__ __forceinline__ uint64_t token_ranks(const EpPlanArgs& a, const TokenRoutes& r, int64_t t, int64_t epr) {
     uint64_t m = 0;
-    for (int k = 0; k < a.topk; ++k) {
-        const int64_t id = load_id(a.ids, t * a.topk + k, a.ids_dtype);
-        if (id >= 0 && id < a.n_global) m |= uint64_t(1) << int(id / epr);
+    #pragma unroll
+    for (int k = 0; k < kEpRegTopk; ++k)
+        if (r.id[k] >= 0) m |= uint64_t(1) << int(r.id[k] / epr);
+    for (int k = kEpRegTopk; k < a.topk; ++k) {
+        const int64_t id = route_id(a, r, t, k);
+        if (id >= 0) m |= uint64_t(1) << int(id / epr);
     }
     return m;
 }
@@ -74,9 +99,11 @@ __global__ void __launch_bounds__(kEpPlanThreads) ep_plan_kernel(const EpPlanArg
 
     if (tid < G) run[tid] = 0;
     __syncthreads();
+    TokenRoutes rt;
     for (int64_t c = 0; c < T; c += kEpPlanThreads) {
         const int64_t t = c + tid;
-        const uint64_t m = t < T ? token_ranks(a, t, epr) : 0;
+        load_routes(a, t, t < T, rt);
+        const uint64_t m = t < T ? token_ranks(a, rt, t, epr) : 0;
         for (int g = 0; g < G; ++g) {
             const unsigned b = __ballot_sync(0xffffffffu, (m >> g) & 1);
             if (lane == 0 && b) atomicAdd(&run[g], __popc(b));
@@ -110,7 +137,13 @@ __global__ void __launch_bounds__(kEpPlanThreads) ep_plan_kernel(const EpPlanArg
 
     for (int64_t c = 0; c < T; c += kEpPlanThreads) {
         const int64_t t = c + tid;
-        const uint64_t m = t < T ? token_ranks(a, t, epr) : 0;
+        // a single chunk keeps pass 1's routes; later chunks reload theirs
+        if (c > 0 || T > kEpPlanThreads) load_routes(a, t, t < T, rt);
+        const uint64_t m = t < T ? token_ranks(a, rt, t, epr) : 0;
+        float wr[kEpRegTopk];
+        #pragma unroll
+        for (int k = 0; k < kEpRegTopk; ++k)
+            wr[k] = (m != 0 && k < a.topk) ? load_as_float(a.weights, t * a.topk + k, a.w_dtype) : 0.f;
         for (int g = 0; g < G; ++g) {
             const unsigned b = __ballot_sync(0xffffffffu, (m >> g) & 1);
             if (lane == 0) wpos[warp][g] = __popc(b);
@@ -133,9 +166,17 @@ __global__ void __launch_bounds__(kEpPlanThreads) ep_plan_kernel(const EpPlanArg
                 const int pos = wpos[warp][g] + __popc(b & lt);
                 a.pair_idx[t * G + g] = pos;
                 a.send_tok[pos] = int32_t(t);
-                for (int k = 0; k < a.topk; ++k) {
-                    const int64_t id = load_id(a.ids, t * a.topk + k, a.ids_dtype);
-                    const bool own = id >= 0 && id < a.n_global && id / epr == g;
+                #pragma unroll
+                for (int k = 0; k < kEpRegTopk; ++k) {
+                    if (k >= a.topk) break;
+                    const int64_t id = rt.id[k];
+                    const bool own = id >= 0 && id / epr == g;
+                    a.send_ids[int64_t(pos) * a.topk + k] = own ? int32_t(id - g * epr) : -1;
+                    a.send_w[int64_t(pos) * a.topk + k] = own ? wr[k] : 0.f;
+                }
+                for (int k = kEpRegTopk; k < a.topk; ++k) {
+                    const int64_t id = route_id(a, rt, t, k);
+                    const bool own = id >= 0 && id / epr == g;
                     a.send_ids[int64_t(pos) * a.topk + k] = own ? int32_t(id - g * epr) : -1;
                     a.send_w[int64_t(pos) * a.topk + k] = own ? load_as_float(a.weights, t * a.topk + k, a.w_dtype) : 0.f;
                 }
@@ -147,6 +188,22 @@ __global__ void __launch_bounds__(kEpPlanThreads) ep_plan_kernel(const EpPlanArg
     }
     // rows past n_valid own no pairs
     for (int64_t i = T * G + tid; i < a.tokens * G; i += kEpPlanThreads) a.pair_idx[i] = -1;
+}
+
+// One warp copies a row of nvec 16-byte vectors, eight vectors per lane
+// loaded before any is stored (the source and destination may alias as far
+// as the compiler knows, which would otherwise serialise load -> store).
+__device__ __forceinline__ void copy_row_warp(uint4* dst, const uint4* src, int64_t nvec, int lane) {
+    constexpr int B = 8;
+    for (int64_t v0 = lane; v0 < nvec; v0 += 32 * B) {
+        uint4 r[B];
+        #pragma unroll
+        for (int b = 0; b < B; ++b)
+            if (v0 + 32 * b < nvec) r[b] = src[v0 + 32 * b];
+        #pragma unroll
+        for (int b = 0; b < B; ++b)
+            if (v0 + 32 * b < nvec) dst[v0 + 32 * b] = r[b];
+    }
 }
 
 // Copy each pair's token row into the send buffer: warp per pair, 16-byte
@@ -169,9 +226,7 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(const uint4* __restrict_
     for (int64_t p = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; p < total; p += nw) {
         const int tok = send_tok[p];
         if (tok < 0) continue;
-        const uint4* src = x + int64_t(tok) * row_vecs;
-        uint4* dst = send_x + p * row_vecs;
-        for (int64_t v = lane; v < row_vecs; v += 32) dst[v] = src[v];
+        copy_row_warp(send_x + p * row_vecs, x + int64_t(tok) * row_vecs, row_vecs, lane);
     }
 }
 
@@ -211,35 +266,52 @@ __device__ __forceinline__ void store4(void* p, int64_t i, int dt, const float (
     }
 }
 
-// out[t] = sum over ranks g (ascending) of partial[pair_idx[t][g]]; warp per
-// token, lanes holding 4 consecutive features.  Rows past n_valid are zero.
+// out[t] = sum over ranks g (ascending) of partial[pair_idx[t][g]].  Warp
+// per (token, 128-feature chunk), lanes holding 4 consecutive features; the
+// ranks' rows are loaded eight at a time before they are added in rank order
+// (deterministic, and one memory round trip per eight ranks).  Rows past
+// n_valid are zero.
 __global__ void __launch_bounds__(256) ep_combine_kernel(const void* __restrict__ partial, int pdt,
                                                          const int32_t* __restrict__ pair_idx, int64_t tokens,
                                                          int world, int hidden, const int32_t* n_valid,
-                                                         void* __restrict__ out, int odt) {
+                                                         void* __restrict__ out, int odt, uint32_t* epoch) {
+    constexpr int B = 8;
     const int lane = threadIdx.x & 31;
+    // NVLink transport: this step is over once the combine runs (every wait
+    // that reads the epoch came before it on the stream): advance the epoch
+    if (epoch && blockIdx.x == 0 && threadIdx.x == 0) *epoch += 1u;
     int64_t T = tokens;
     if (n_valid) T = min(T, int64_t(max(0, *n_valid)));
+    const int nch = hidden / 128;
+    const int64_t tasks = tokens * nch;
     const int64_t nw = (int64_t(gridDim.x) * blockDim.x) >> 5;
-    for (int64_t t = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; t < tokens; t += nw) {
-        const bool live = t < T;
-        const int p0 = live && lane < world ? pair_idx[t * world + lane] : -1;
-        const int p1 = live && lane + 32 < world ? pair_idx[t * world + lane + 32] : -1;
-        for (int c0 = 4 * lane; c0 < hidden; c0 += 128) {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            if (live) {
-                for (int g = 0; g < world; ++g) {
-                    const int p = g < 32 ? __shfl_sync(0xffffffffu, p0, g) : __shfl_sync(0xffffffffu, p1, g - 32);
-                    if (p < 0) continue;
-                    float v[4];
-                    load4(partial, int64_t(p) * hidden + c0, pdt, v);
-                    #pragma unroll
-                    for (int i = 0; i < 4; ++i) acc[i] += v[i];
-                }
+    for (int64_t task = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; task < tasks; task += nw) {
+        const int64_t t = task / nch;
+        const int c0 = int(task % nch) * 128 + 4 * lane;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        if (t < T) {
+            for (int g0 = 0; g0 < world; g0 += B) {
+                int pj[B];
+                #pragma unroll
+                for (int j = 0; j < B; ++j) pj[j] = g0 + j < world ? pair_idx[t * world + g0 + j] : -1;
+                float v[B][4];
+                #pragma unroll
+                for (int j = 0; j < B; ++j)
+                    if (pj[j] >= 0) load4(partial, int64_t(pj[j]) * hidden + c0, pdt, v[j]);
+                #pragma unroll
+                for (int j = 0; j < B; ++j)
+                    if (pj[j] >= 0)
+                        #pragma unroll
+                        for (int i = 0; i < 4; ++i) acc[i] += v[j][i];
             }
-            store4(out, t * hidden + c0, odt, acc);
         }
+        store4(out, t * hidden + c0, odt, acc);
     }
+}
+
+static int combine_grid(int64_t tokens, int hidden) {
+    const int64_t tasks = tokens * (hidden / 128);
+    return int(std::max<int64_t>(1, std::min<int64_t>((tasks + 7) / 8, int64_t(num_sms_current()) * 8)));
 }
 
 // ---------------------------------------------------------------------------
@@ -272,8 +344,42 @@ struct EpP2pArgs {
     const int64_t* peers;
 };
 
+// True in the last CTA of the grid to get here.  Every thread's earlier
+// stores (peer memory included) are made visible system-wide before its CTA
+// counts itself done; the last CTA fences again before it signals, so a peer
+// that acquires the signal sees every CTA's stores.  The counter (zero on
+// entry) is reset by the last CTA.
+__device__ __forceinline__ bool ep_last_cta(int* ctr) {
+    __shared__ int s_last;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int prev = atomicAdd(ctr, 1);
+        s_last = prev == int(gridDim.x) - 1;
+        if (s_last) *ctr = 0;
+    }
+    __syncthreads();
+    const bool last = s_last != 0;
+    if (last) __threadfence_system();
+    return last;
+}
+
+// raise this step's flag (arrival or return) in every peer's window; with
+// counts, first tell each owner how many pairs it gets from this rank
+__device__ __forceinline__ void ep_raise_flags(const EpP2pArgs& a, size_t flag_off, size_t counts_off,
+                                               const int32_t* send_counts) {
+    const int g = threadIdx.x;
+    if (g >= a.world) return;
+    const uint32_t epoch = *reinterpret_cast<const uint32_t*>(a.window + kEpCtlEpoch);
+    char* dst = reinterpret_cast<char*>(a.peers[g]);
+    if (send_counts) reinterpret_cast<volatile int32_t*>(dst + counts_off)[a.rank] = send_counts[g];
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<uint32_t*>(dst + flag_off) + a.rank, epoch + 1u);
+}
+
 // source: pair slots (g, idx) of the capacity layout -> owner g's window at
-// [rank * cap + idx]; empty slots carry ids -1 / weight 0 (rows untouched)
+// [rank * cap + idx]; empty slots carry ids -1 / weight 0 (rows untouched).
+// The last CTA to finish raises the arrival flags.
 __global__ void __launch_bounds__(256) ep_p2p_scatter_kernel(const EpP2pArgs a) {
     const int lane = threadIdx.x & 31;
     const int32_t* counts = reinterpret_cast<const int32_t*>(a.window + a.L.send_counts);
@@ -290,9 +396,8 @@ __global__ void __launch_bounds__(256) ep_p2p_scatter_kernel(const EpP2pArgs a) 
         int32_t* did = reinterpret_cast<int32_t*>(dst + a.L.recv_ids) + slot * a.topk;
         float* dw = reinterpret_cast<float*>(dst + a.L.recv_w) + slot * a.topk;
         if (idx < counts[g]) {
-            const uint4* src = a.x + int64_t(tok[it]) * a.row_vecs;
-            uint4* dx = reinterpret_cast<uint4*>(dst + a.L.recv_x) + slot * a.row_vecs;
-            for (int64_t v = lane; v < a.row_vecs; v += 32) dx[v] = src[v];
+            copy_row_warp(reinterpret_cast<uint4*>(dst + a.L.recv_x) + slot * a.row_vecs,
+                          a.x + int64_t(tok[it]) * a.row_vecs, a.row_vecs, lane);
             for (int k = lane; k < a.topk; k += 32) {
                 did[k] = sid[it * a.topk + k];
                 dw[k] = sw[it * a.topk + k];
@@ -304,10 +409,12 @@ __global__ void __launch_bounds__(256) ep_p2p_scatter_kernel(const EpP2pArgs a) 
             }
         }
     }
-    __threadfence_system();  // this thread's peer stores are visible system-wide before the flag kernel runs
+    if (ep_last_cta(reinterpret_cast<int*>(a.window + kEpCtlScatterDone)))
+        ep_raise_flags(a, a.L.arrive, a.L.counts, counts);
 }
 
-// owner: its partial rows of source g's pairs -> source g's window at [rank * cap + idx]
+// owner: its partial rows of source g's pairs -> source g's window at
+// [rank * cap + idx]; the last CTA to finish raises the return flags
 __global__ void __launch_bounds__(256) ep_p2p_return_kernel(const uint4* __restrict__ partial, int64_t row_vecs,
                                                             const EpP2pArgs a) {
     const int lane = threadIdx.x & 31;
@@ -319,23 +426,10 @@ __global__ void __launch_bounds__(256) ep_p2p_return_kernel(const uint4* __restr
         const int64_t idx = it % a.cap;
         if (idx >= counts[g]) continue;
         char* dst = reinterpret_cast<char*>(a.peers[g]);
-        uint4* db = reinterpret_cast<uint4*>(dst + a.L.back) + (int64_t(a.rank) * a.cap + idx) * row_vecs;
-        const uint4* src = partial + it * row_vecs;
-        for (int64_t v = lane; v < row_vecs; v += 32) db[v] = src[v];
+        copy_row_warp(reinterpret_cast<uint4*>(dst + a.L.back) + (int64_t(a.rank) * a.cap + idx) * row_vecs,
+                      partial + it * row_vecs, row_vecs, lane);
     }
-    __threadfence_system();
-}
-
-// raise this step's flag (arrival or return) on every peer; with counts,
-// first tell each owner how many pairs it gets from this rank
-__global__ void ep_p2p_signal_kernel(const int64_t* peers, int world, int rank, size_t flag_off, size_t counts_off,
-                                     const int32_t* send_counts, const uint32_t* epoch) {
-    const int g = threadIdx.x;
-    if (g >= world) return;
-    char* dst = reinterpret_cast<char*>(peers[g]);
-    if (send_counts) reinterpret_cast<volatile int32_t*>(dst + counts_off)[rank] = send_counts[g];
-    __threadfence_system();
-    st_release_sys(reinterpret_cast<uint32_t*>(dst + flag_off) + rank, *epoch + 1u);
+    if (ep_last_cta(reinterpret_cast<int*>(a.window + kEpCtlReturnDone))) ep_raise_flags(a, a.L.ret, 0, nullptr);
 }
 
 // wait (bounded) until every peer raised this step's flag in our window;
@@ -398,25 +492,18 @@ cudaError_t run_ep_p2p(const EpP2pCall& c, cudaStream_t s) {
         a.x = static_cast<const uint4*>(c.x);
         a.row_vecs = c.hidden * int64_t(c.x_esize) / 16;
         ep_p2p_scatter_kernel<<<grid, 256, 0, s>>>(a);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-        ep_p2p_signal_kernel<<<1, 64, 0, s>>>(c.peers, c.world, c.rank, L.arrive, L.counts, p.send_counts,
-                                               reinterpret_cast<const uint32_t*>(win + kEpCtlEpoch));
     } else if (c.phase == EP_P2P_WAIT_ARRIVE || c.phase == EP_P2P_WAIT_RETURN) {
         ep_p2p_wait_kernel<<<1, 64, 0, s>>>(win, c.world, c.phase == EP_P2P_WAIT_ARRIVE ? L.arrive : L.ret);
     } else if (c.phase == EP_P2P_RETURN) {
         ep_p2p_return_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(c.partial),
                                                   c.hidden * int64_t(c.p_esize) / 16, a);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-        ep_p2p_signal_kernel<<<1, 64, 0, s>>>(c.peers, c.world, c.rank, L.ret, 0, nullptr,
-                                               reinterpret_cast<const uint32_t*>(win + kEpCtlEpoch));
     } else if (c.phase == EP_P2P_COMBINE) {
-        if (c.tokens > 0) {
-            const int cgrid = int(std::max<int64_t>(1, std::min<int64_t>((c.tokens + 7) / 8, int64_t(num_sms_current()) * 8)));
-            ep_combine_kernel<<<cgrid, 256, 0, s>>>(win + L.back, c.p_dtype, c.pair_idx, c.tokens, c.world, c.hidden,
-                                                    c.n_valid, c.out, c.out_dtype);
-            if ((e = cudaGetLastError()) != cudaSuccess) return e;
-        }
-        ep_p2p_epoch_kernel<<<1, 1, 0, s>>>(win);
+        if (c.tokens > 0)
+            ep_combine_kernel<<<combine_grid(c.tokens, int(c.hidden)), 256, 0, s>>>(
+                win + L.back, c.p_dtype, c.pair_idx, c.tokens, c.world, c.hidden, c.n_valid, c.out, c.out_dtype,
+                reinterpret_cast<uint32_t*>(win + kEpCtlEpoch));
+        else
+            ep_p2p_epoch_kernel<<<1, 1, 0, s>>>(win);
     } else {
         return cudaErrorInvalidValue;
     }
@@ -455,8 +542,8 @@ cudaError_t run_ep_dispatch(const EpDispatchCall& c, cudaStream_t s) {
 cudaError_t run_ep_combine(const void* partial, int pdt, const int32_t* pair_idx, int64_t tokens, int world,
                            int hidden, const int32_t* n_valid, void* out, int odt, cudaStream_t s) {
     if (tokens == 0) return cudaSuccess;
-    const int grid = int(std::max<int64_t>(1, std::min<int64_t>((tokens + 7) / 8, int64_t(num_sms_current()) * 8)));
-    ep_combine_kernel<<<grid, 256, 0, s>>>(partial, pdt, pair_idx, tokens, world, hidden, n_valid, out, odt);
+    ep_combine_kernel<<<combine_grid(tokens, hidden), 256, 0, s>>>(partial, pdt, pair_idx, tokens, world, hidden, n_valid, out, odt,
+                                                                  nullptr);
     return cudaGetLastError();
 }
 

@@ -132,6 +132,9 @@ cudaError_t run_ep_dispatch(const EpDispatchCall& c, cudaStream_t s);
 // rank).  Control word 0: step epoch; word 1: status.  Peers write arrive[],
 // counts[], ret[], recv_*[] and back[]; the send_* scratch is local.
 constexpr size_t kEpCtlEpoch = 0, kEpCtlStatus = 4;
+// completion counters of the scatter / return grids (the last CTA raises the
+// step's flags and resets its counter)
+constexpr size_t kEpCtlScatterDone = 8, kEpCtlReturnDone = 12;
 struct EpWindow {
     size_t arrive, counts, ret, send_counts, recv_x, recv_ids, recv_w, back, send_tok, send_ids, send_w, total;
 };
