@@ -102,7 +102,7 @@ def test_prefill_gemm_256_row_tiles(native, cuda, tokens):
 @pytest.mark.parametrize("n_valid", [None, 1030])
 def test_large_batch_split_prep(native, cuda, n_valid):
     """>= 8192 routes: the routing prep runs as chunk histograms, a one-CTA
-    layout pass and a chunked stable placement; the result must equal the
+    layout pass and a chunked placement; the result must equal the
     eager loop, including the padded n_valid rows."""
     import torch
     pack, layer, x, ids, w = _setup(cuda, "cfg2", seed=123, tokens=1100, n_experts=16, hidden=256,

@@ -13,10 +13,12 @@
 // computed in the rotated domain x W = ((x o suh) H / sqrt128) W~ (H / sqrt128) o svh.
 //
 // Kernels, in stream order (no host synchronisation, graph-capturable):
-//  1. prep     one CTA: map ids to local experts (expert_map, n_local
-//              sentinel; exl3.py:2332-2354), stable counting sort of routes
-//              by expert, each expert's rows padded to 16, work slots of <= 16
-//              rows, split-K counters cleared.
+//  1. prep     one CTA (chunked over CTAs for large batches): map ids to
+//              local experts (expert_map, n_local sentinel;
+//              exl3.py:2332-2354), counting sort of routes by expert (rows
+//              claimed with warp-aggregated atomics, so their order within an
+//              expert is free: no kernel mixes rows), each expert's rows
+//              padded to 16, work slots of <= 16 rows, counters cleared.
 //  2. rotate   fp16 H128(x o suh)/sqrt128 per (route, projection, 128-block),
 //              stored [proj][kblock][row][136] (rows padded to 272 bytes so a
 //              1-D bulk copy lands ldmatrix-conflict-free).
@@ -44,7 +46,6 @@ enum Act : int { ACT_SILU = 0, ACT_SWIGLU_OAI = 3 };
 
 constexpr int kPrepThreads = 1024;
 constexpr int kMaxLocal = 2048;
-constexpr int kFastRankExperts = 256;  // per-warp histogram ranking up to this many experts
 constexpr int kPrepChunk = 2048;       // routes per CTA when the prep is split over CTAs
 constexpr int64_t kPrepSplitRoutes = 4 * kPrepChunk;  // split the prep from this many routes on
 constexpr int kYsPitch = 132;          // fp32 pitch of the epilogue tile (conflict-free fragment stores)
@@ -228,76 +229,40 @@ __device__ __forceinline__ float route_weight(const PrepArgs& a, int64_t r) {
     return (a.linear || a.batched) ? 1.f : load_as_float(a.weights, r, a.w_dtype);
 }
 
-// One 1024-route step of the stable placement: thread tid places route r
-// (local expert e, -1 = not local or past r1; weight wgt).  run[e] holds each
-// expert's next sorted row and is advanced; chunk[] is scratch (per-expert
-// totals of the step, fast path).  Whole CTA.
+// Placement of one route per thread: thread tid places route r (local expert
+// e, -1 = not local or past r1; weight wgt) at the next free sorted row of
+// its expert.  run[e] (shared memory) holds each expert's next row; the lanes
+// of a warp that share an expert take one block of rows with a single atomic
+// add by their leader.  The order of rows within an expert is not fixed, and
+// need not be: every output row is computed from its own input row only (no
+// kernel mixes rows), and the combine finds a route's row through route_pos.
+// No barrier: rows are claimed atomically.
 __device__ __forceinline__ void prep_place_step(const PrepArgs& a, int64_t r, int64_t r1, int64_t Rmax, int e,
-                                                float wgt, int* run, int* chunk,
-                                                unsigned short (*wcnt)[kFastRankExperts]) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int E = a.n_local;
-    const bool fast = E <= kFastRankExperts;
-    {
-        const unsigned mask = __match_any_sync(0xffffffffu, e);
-        const int rank = __popc(mask & ((1u << lane) - 1u));
-        const int leader = __ffs(mask) - 1;
-        int p = -1;
-        if (fast) {
-            // per-warp counts -> exclusive prefix over warps per expert (in
-            // wcnt), step totals in chunk; three barriers per 1024 routes
-            for (int i = tid; i < (kPrepThreads / 32) * kFastRankExperts; i += kPrepThreads)
-                (&wcnt[0][0])[i] = 0;
-            __syncthreads();
-            if (e >= 0 && lane == leader) wcnt[warp][e] = (unsigned short)__popc(mask);
-            __syncthreads();
-            for (int x = tid; x < E; x += kPrepThreads) {
-                int acc = 0;
-                for (int w = 0; w < kPrepThreads / 32; ++w) {
-                    const int c = wcnt[w][x];
-                    wcnt[w][x] = (unsigned short)acc;
-                    acc += c;
-                }
-                chunk[x] = acc;
-            }
-            __syncthreads();
-            if (e >= 0) p = run[e] + int(wcnt[warp][e]) + rank;
-        } else {
-            int my_base = 0;
-            for (int w = 0; w < kPrepThreads / 32; ++w) {
-                if (warp == w && e >= 0 && lane == leader) {
-                    my_base = run[e];
-                    run[e] += __popc(mask);
-                }
-                __syncthreads();
-            }
-            my_base = __shfl_sync(0xffffffffu, my_base, leader);
-            if (e >= 0) p = my_base + rank;
-        }
-        if (e >= 0) {
-            a.w.route_pos[r] = p;
-            a.w.sorted_tok[p] = int(r / a.topk);
-            a.w.sorted_route[p] = int(r);
-            a.w.sorted_exp[p] = e;
-            a.w.sorted_w[p] = wgt;
-        } else if (r < r1 && r < Rmax) {
-            a.w.route_pos[r] = -1;
-        }
-        if (fast) {
-            __syncthreads();
-            for (int x = tid; x < E; x += kPrepThreads) run[x] += chunk[x];
-            __syncthreads();
-        }
+                                                float wgt, int* run) {
+    const int lane = threadIdx.x & 31;
+    const unsigned mask = __match_any_sync(0xffffffffu, e);
+    const int leader = __ffs(mask) - 1;
+    int base = 0;
+    if (e >= 0 && lane == leader) base = atomicAdd(&run[e], __popc(mask));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (e >= 0) {
+        const int p = base + __popc(mask & ((1u << lane) - 1u));
+        a.w.route_pos[r] = p;
+        a.w.sorted_tok[p] = int(r / a.topk);
+        a.w.sorted_route[p] = int(r);
+        a.w.sorted_exp[p] = e;
+        a.w.sorted_w[p] = wgt;
+    } else if (r < r1 && r < Rmax) {
+        a.w.route_pos[r] = -1;
     }
 }
 
-// Stable placement of routes [r0, r1): route order within each expert.
-__device__ void prep_place(const PrepArgs& a, int64_t r0, int64_t r1, int64_t Rmax, int* run, int* chunk,
-                           unsigned short (*wcnt)[kFastRankExperts]) {
+// Placement of routes [r0, r1) within each expert's rows (run[] = first rows).
+__device__ void prep_place(const PrepArgs& a, int64_t r0, int64_t r1, int64_t Rmax, int* run) {
     for (int64_t base = r0; base < r1; base += kPrepThreads) {
         const int64_t r = base + threadIdx.x;
         const int e = r < r1 ? local_expert(a, r) : -1;
-        prep_place_step(a, r, r1, Rmax, e, e >= 0 ? route_weight(a, r) : 0.f, run, chunk, wcnt);
+        prep_place_step(a, r, r1, Rmax, e, e >= 0 ? route_weight(a, r) : 0.f, run);
     }
 }
 
@@ -311,7 +276,6 @@ __device__ __forceinline__ int64_t prep_routes(const PrepArgs& a) {
 __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
     __shared__ int cnt[kMaxLocal];
     __shared__ int poff[kMaxLocal];
-    __shared__ unsigned short wcnt[kPrepThreads / 32][kFastRankExperts];
     __shared__ int sh32[32];
     const int tid = threadIdx.x;
     const int E = a.n_local;
@@ -336,8 +300,10 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
     for (int e = tid; e < E; e += kPrepThreads) cnt[e] = 0;
     __syncthreads();
     #pragma unroll
-    for (int j = 0; j < kPer; ++j)
-        if (ev[j] >= 0) atomicAdd(&cnt[ev[j]], 1);
+    for (int j = 0; j < kPer; ++j) {  // warp-aggregated: one add per expert per warp
+        const unsigned m = __match_any_sync(0xffffffffu, ev[j]);
+        if (ev[j] >= 0 && (threadIdx.x & 31) == __ffs(m) - 1) atomicAdd(&cnt[ev[j]], __popc(m));
+    }
     __syncthreads();
     prep_layout(a, cnt, poff, sh32);
     for (int e = tid; e < E; e += kPrepThreads) cnt[e] = poff[e];  // running positions
@@ -345,7 +311,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
     #pragma unroll
     for (int j = 0; j < kPer; ++j) {
         if (int64_t(j) * kPrepThreads >= R) break;  // CTA-uniform
-        prep_place_step(a, int64_t(j) * kPrepThreads + tid, R, Rmax, ev[j], wv[j], cnt, poff, wcnt);
+        prep_place_step(a, int64_t(j) * kPrepThreads + tid, R, Rmax, ev[j], wv[j], cnt);
     }
     for (int64_t r = R + tid; r < Rmax; r += kPrepThreads) a.w.route_pos[r] = -1;
 }
@@ -393,17 +359,15 @@ __global__ void __launch_bounds__(kPrepThreads) prep_plan_kernel(const PrepArgs 
     for (int64_t r = R + tid; r < Rmax; r += kPrepThreads) a.w.route_pos[r] = -1;
 }
 
-// 3. per chunk: stable placement from the chunk's first rows
+// 3. per chunk: placement from the chunk's first rows
 __global__ void __launch_bounds__(kPrepThreads) prep_place_kernel(const PrepArgs a) {
     __shared__ int run[kMaxLocal];
-    __shared__ int chunk[kMaxLocal];
-    __shared__ unsigned short wcnt[kPrepThreads / 32][kFastRankExperts];
     const int E = a.n_local;
     const int64_t R = prep_routes(a), Rmax = a.t_max * a.topk;
     const int64_t r0 = int64_t(blockIdx.x) * kPrepChunk, r1 = min(R, r0 + kPrepChunk);
     for (int e = threadIdx.x; e < E; e += kPrepThreads) run[e] = a.w.hist[int64_t(blockIdx.x) * E + e];
     __syncthreads();
-    prep_place(a, r0, r1, Rmax, run, chunk, wcnt);
+    prep_place(a, r0, r1, Rmax, run);
 }
 
 // ---------------------------------------------------------------------------
