@@ -50,11 +50,15 @@ sys.path.insert(0, os.path.join(ROOT, "oracle"))
 H, I, E, TOPK, KBITS = 2048, 768, 128, 8, 4
 
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
-# capture of this workload (dram__bytes_read.sum + dram__bytes_write.sum);
+# capture of this workload (dram__bytes_read.sum + dram__bytes_write.sum).
 # ncu cannot run inside the timed bench, so the capture's figure is reported
+# with its source; it belongs to the kernel build named there, not
+# necessarily to the build being timed.
 DRAM_TRAFFIC = {
-    "decode": {"bytes": 241.6e6, "kernel": "gemv_kernel<2,GATEUP,MCG>, T=64"},
-    "prefill": {"bytes": 695.5e6, "kernel": "tc_gemm_kernel gate/up launches (mean), T=2048"},
+    "decode": {"bytes": 241.6e6, "kernel": "gemv_kernel<2,GATEUP,MCG>, T=64",
+               "source": "profiles/gemv_gateup_cfg2_T64.md"},
+    "prefill": {"bytes": 695.5e6, "kernel": "tc_gemm_kernel gate/up launches (mean), T=2048",
+                "source": "profiles/tc_gemm_cfg3_T2048.md"},
 }
 METRIC = "MoE layer decode tokens/s (128 experts top-8, H2048 I768, K4 MCG)"
 
@@ -351,6 +355,7 @@ def run_b200(args, rank, local_rank, world):
         "frac": gu_bytes / gu_s / 1e9 / peak,
         "bytes_per_launch": gu_bytes, "us_per_launch": ph["gate_up"],
         "traffic": DRAM_TRAFFIC["decode"]["bytes"] if T == 64 else None,
+        "traffic_source": DRAM_TRAFFIC["decode"]["source"] if T == 64 else None,
         "layer": {"bytes": layer_bytes, "us": total_ms / args.steps * 1e3,
                   "achieved": layer_bytes / (total_ms / args.steps / 1e3) / 1e9,
                   "frac": layer_bytes / (total_ms / args.steps / 1e3) / 1e9 / peak},
@@ -758,6 +763,7 @@ def run_prefill(args, rank, local_rank, world):
                 "unit": "TFLOP/s", "achieved": flops_gu / gu_s / 1e12, "peak": tpk, "peak_kind": tkind,
                 "frac": flops_gu / gu_s / 1e12 / tpk, "flops_per_launch": flops_gu, "us_per_launch": ph["gate_up"],
                 "traffic": DRAM_TRAFFIC["prefill"]["bytes"] if T == 2048 else None,
+                "traffic_source": DRAM_TRAFFIC["prefill"]["source"] if T == 2048 else None,
                 "layer": {"flops": flops_layer, "us": step_s * 1e6, "achieved": flops_layer / step_s / 1e12,
                           "frac": flops_layer / step_s / 1e12 / tpk}}
     del graph

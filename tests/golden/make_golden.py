@@ -3,7 +3,7 @@
 Run in the build container, where the reference tree exists and its CPU
 dequant is compiled (``make -C oracle ref``):
 
-    python tests/golden/make_golden.py [--ref-src /root/reference/src]
+    python tests/golden/make_golden.py [--ref-src <reference checkout>/src]
 
 Every expected value comes from reference code, never from this repository:
 
@@ -37,7 +37,9 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-src", default="/root/reference/src")
+    # the reference checkout: EXL3_REFERENCE_ROOT, else a sibling of this repository
+    ref_root = os.environ.get("EXL3_REFERENCE_ROOT", os.path.join(os.path.dirname(ROOT), "reference"))
+    ap.add_argument("--ref-src", default=os.path.join(ref_root, "src"))
     args = ap.parse_args()
     sys.path.insert(0, args.ref_src)
     sys.path.insert(0, os.path.join(ROOT, "oracle", "_ref"))

@@ -2,7 +2,8 @@
 device memory when they run a projection (an engine that has handed all free
 HBM to its KV cache, a C/FFI host without a caching allocator).  It must give
 the same result as exl3_linear -- the workspace entry -- on consecutive calls
-that reuse its built-in scratch, and reject a call that would not fit.
+that reuse its built-in scratch (through both the decode GEMV and the
+tensor-core GEMM path), and reject a call that would not fit.
 
 This file is collected last on purpose, so a run that stops at the first
 failure has already run every other test.
@@ -39,7 +40,9 @@ def test_noalloc_matches_workspace_linear_on_consecutive_calls(native, cuda):
     v = ((rng.integers(0, 2, out_f) * 2 - 1) * np.float16(1 / 32)).astype(np.float16)
     dt, du, dv = (torch.from_numpy(a).to(cuda) for a in (t, u, v))
     stream = torch.cuda.current_stream(cuda).cuda_stream
-    for call, m in enumerate((5, 19)):  # two calls in a row, different shapes, one scratch
+    # calls in a row on one scratch: m = 5 and 19 take the decode GEMV, m = 64
+    # the tcgen05 GEMM path (>= 32 rows), each reusing what the last one left
+    for call, m in enumerate((5, 19, 64)):
         x = torch.from_numpy(rng.normal(0, 1, (m, in_f)).astype(np.float32)).to(cuda)
         want = native.exl3_linear(x, dt, du, dv, K, cb, out_dtype=torch.float32)
         y = torch.full((m, out_f), float("nan"), dtype=torch.float32, device=cuda)

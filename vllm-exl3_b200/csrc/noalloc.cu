@@ -16,9 +16,9 @@
 //    device current, by the first call made on it (cudaGetSymbolAddress);
 //    make that first call before any stream capture, e.g. during warm-up;
 //  * every call reuses the array and it keeps the previous call's contents;
-//    the words that must start at zero (status word, slot count) are cleared
-//    on the call's stream before the kernels run, and the split-K counters
-//    are cleared by the first kernel;
+//    the status word, the one word that must start at zero, is cleared on
+//    the call's stream before the kernels run; the routing prep kernel then
+//    rewrites the slot count and clears the split-K and scheduling counters;
 //  * calls whose GPU work overlaps (two streams, or two host threads on one
 //    device without ordering) race on the array and corrupt each other;
 //  * a call whose work buffers would exceed the array is rejected before
@@ -87,6 +87,8 @@ extern "C" int exl3_linear_noalloc(const void* x, int x_dtype, int64_t m, const 
                             who);
     if (reinterpret_cast<uintptr_t>(trellis) & 15)
         return noalloc_fail(EXL3_ERR_ARG, "%s: trellis must be 16-byte aligned", who);
+    if ((reinterpret_cast<uintptr_t>(suh) & 1) || (reinterpret_cast<uintptr_t>(svh) & 1))
+        return noalloc_fail(EXL3_ERR_ARG, "%s: suh/svh must be 2-byte aligned fp16 arrays", who);
     if (m < 0) return noalloc_fail(EXL3_ERR_ARG, "%s: m must be >= 0", who);
     if (m == 0) return EXL3_OK;
     exl3::MoePlan p;
@@ -103,7 +105,8 @@ extern "C" int exl3_linear_noalloc(const void* x, int x_dtype, int64_t m, const 
         return noalloc_fail(EXL3_ERR_CUDA, "%s: scratch lookup failed: CUDA error %d (%s)", who, int(e),
                             cudaGetErrorString(e));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // status word and slot count of the previous call
+    // the previous call's status word (the prep kernel rewrites the slot
+    // count and clears the counters itself)
     e = cudaMemsetAsync(ws, 0, 256, s);
     if (e != cudaSuccess)
         return noalloc_fail(EXL3_ERR_CUDA, "%s: CUDA error %d (%s)", who, int(e), cudaGetErrorString(e));

@@ -62,24 +62,5 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB_PATH
 
 
-MICROBENCH_PATH = os.path.join(PKG_DIR, "decode_microbench")
-
-
-def build_microbench(force: bool = False) -> str:
-    """Compile ``csrc/decode_microbench.cu`` (a standalone executable that
-    times the GEMM path's trellis decode per bit width and codebook)."""
-    src = os.path.join(CSRC, "decode_microbench.cu")
-    deps = [src] + [os.path.join(CSRC, h) for h in ("exl3_common.cuh", "tc_common.cuh", "exl3_internal.h")]
-    if (not force and os.path.exists(MICROBENCH_PATH)
-            and all(os.path.getmtime(p) <= os.path.getmtime(MICROBENCH_PATH) for p in deps)):
-        return MICROBENCH_PATH
-    cmd = [_nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
-           "-o", MICROBENCH_PATH, src]
-    res = subprocess.run(cmd, capture_output=True, text=True)
-    if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stderr[-4000:]}")
-    return MICROBENCH_PATH
-
-
 if __name__ == "__main__":
     print(build(force=True, verbose=True))
