@@ -1,35 +1,49 @@
 """Benchmark of the EXL3 routed-expert MoE layer on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--tokens T]
+                    [--workload decode|prefill|ep] [--no-prefill] [--no-ep-cfg4] [--no-cpu-baseline]
 
-Workload (the decode config): one routed-MoE layer,
+Headline (the decode config): one routed-MoE layer,
 128 experts, top-8 softmax routing, hidden 2048, expert intermediate 768,
-uniform K=4 MCG, T=64 tokens per step (the largest decode batch of the
-config; T = 1, 8, 32 are reported in `decode_sweep`).  Weights and inputs are
-seeded synthetic (exl3_b200.synthetic).  A step is one layer forward over
+uniform K=4 MCG, T=64 tokens per step (the config's largest decode batch;
+T = 1, 8, 32 are reported in `decode_sweep_us_per_layer`).  Weights and inputs
+are seeded synthetic (exl3_b200.synthetic).  A step is one layer forward over
 one batch; 8 different routings/batches rotate across steps.
+
+The same line carries, as sub-objects measured in the same run:
+* `prefill`: configs[2] (160 experts, H5120 I1536, K2/3 mul1, T=2048), the
+  tcgen05 grouped-GEMM path, one GPU;
+* `ep_cfg4`: configs[4] (256 experts top-8 sigmoid+Zipf, H7168 I2048,
+  K2/3/4 MCG, 8192 tokens split over the N ranks: strong scaling), the
+  expert-parallel step with per-phase in-graph times and the per-rank
+  local-route skew.
 
 Timing: W untimed warm-up steps, then exactly K steps bracketed by a barrier
 and torch.cuda.synchronize(); every step is timed with CUDA events on the
-launching stream around the layer only, after an untimed 256 MB L2 flush.
-`value` = tokens of all ranks / max-over-ranks device time (CUDA graph of the
-layer, inputs resident in HBM).  `e2e` = the same metric through the public
-API (exl3_b200.moe.Exl3RoutedExperts.apply, eager) with pinned-host inputs
-copied in and the output copied back inside the timed region.
+launching stream around the layer only, after an untimed 256 MB L2 flush
+(larger than the 126 MB L2).  `value` = tokens of all ranks / max-over-ranks
+device time (CUDA graph of the layer, inputs resident in HBM).  `e2e` = the
+same metric through the public API (exl3_b200.moe.Exl3RoutedExperts.apply,
+eager) with pinned-host inputs copied in and the output copied back inside
+the timed region.  Every line's outputs are checked against the CPU eager
+loop (oracle/parity.py) outside the timed region: `parity`.
 
 N > 1: expert parallelism (exl3_b200.ep): rank g holds experts
-[g*128/N, (g+1)*128/N) and T tokens of its own (weak scaling); a step is
-dispatch (the library's kernels store each pair row straight into its
-owner's IPC-mapped window over NVLink; --ep-transport nccl uses NCCL
-instead), the local fused forward, the partial rows stored back, and the
-per-token combine, one CUDA graph per step, timed per step and taken as the
-max over ranks.
---workload ep: configs[4] (256 experts, H7168 I2048, 8192 tokens split over
-the ranks: strong scaling), same EP step at any N.  --workload prefill:
-configs[2] on one GPU (tcgen05 grouped GEMM path).  --impl reference: rank 0 times the
-reference's CPU path (dequant_trellis compiled from the reference's own
-csrc/bindings.cpp, oracle/_ref; else the oracle port) on a bounded sample of
-each step's experts, scaled to the step.
+[g*E/N, (g+1)*E/N); the headline runs the decode layer with T tokens per rank
+(weak scaling); a step is dispatch (the library's kernels store each pair row
+straight into its owner's IPC-mapped window over NVLink; --ep-transport nccl
+uses NCCL instead), the local fused forward, the partial rows stored back,
+and the per-token combine, one CUDA graph per step, timed per step and taken
+as the max over ranks.
+
+--impl reference: rank 0 times the reference's CPU path (oracle/ref_loop.py:
+the reference's eager loop apply_exl3_python_loop with dequant_trellis from
+the reference's own csrc/bindings.cpp compiled into oracle/_ref) on this
+box's host cores: each step runs the loop body of a sample of the batch's
+distinct experts, one process per core; `ms_per_step` is that step's
+measured time and `value` the equivalent tokens/s (tokens x the sampled
+fraction of the step's experts / step time).  configs[0] is also timed as one
+whole layer, serially as the reference runs it (median of 3).
 """
 
 from __future__ import annotations
@@ -38,7 +52,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -71,12 +84,15 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the configs[2] prefill sub-object")
+    ap.add_argument("--no-ep-cfg4", action="store_true", help="skip the configs[4] expert-parallel sub-object")
+    ap.add_argument("--no-parity", action="store_true", help="skip the output checks against the oracle")
     ap.add_argument("--no-graph", action="store_true", help="time the expert-parallel step eagerly")
     ap.add_argument("--ep-transport", default="nvlink", choices=["nvlink", "nccl"],
                     help="expert-parallel exchange: the library's NVLink peer-store kernels or NCCL")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep"],
-                    help="decode = configs[1] (the default, reported line); prefill = configs[2]; "
-                         "ep = configs[4]")
+                    help="decode = configs[1] (the default, reported line, with the prefill and ep_cfg4 "
+                         "sub-objects); prefill = configs[2] alone; ep = configs[4] alone")
     return ap.parse_args()
 
 
@@ -86,116 +102,72 @@ def env_rank():
 
 
 def peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, kind) from MEASURED_PEAKS.json, else the
+    pool's earlier measurement."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return 6650.0, 1590.0, "fallback"
+
+
+def log(msg: str) -> None:
+    print(f"[bench] {msg}", file=sys.stderr, flush=True)
 
 
 # ---------------------------------------------------------------------------
-# CPU reference sample (reference arm and the cpu_baseline key)
+# the reference's CPU path (the reference arm and the cpu_baseline key)
 # ---------------------------------------------------------------------------
-_REF = None
-
-
-def _ref_dequant():
-    """dequant_trellis of the reference's own compiled CPU code, else the port."""
-    global _REF
-    if _REF is None:
-        import torch  # noqa: F401
-        sys.path.insert(0, os.path.join(ROOT, "oracle", "_ref"))
-        try:
-            import vllm_exl3_ref_c
-            _REF = ("reference", vllm_exl3_ref_c)
-        except Exception:
-            import cpu_oracle
-            _REF = ("port", cpu_oracle)
-    return _REF
-
-
-def _slice_task(args):
-    """One sampled slice of the eager loop (exl3.py:2377-2413): dequant_trellis
-    of `rows` input rows of one expert projection per call (the CPU branch of
-    exl3_gemv, bindings.cpp:144-146) and its routes' matmul.  Returns
-    (seconds, weights decoded)."""
-    import numpy as np
-    import torch
-    torch.set_num_threads(1)
-    seed, which, rows, route_rows = args
-    from exl3_b200 import synthetic
-    rng = np.random.default_rng(seed)
-    in_f, out_f = (H, I) if which < 2 else (I, H)
-    rows = min(rows, in_f)
-    p = synthetic.make_projection(rng, rows, out_f, KBITS, 1)
-    h = torch.from_numpy(rng.normal(0, 1, (route_rows, rows)).astype(np.float32)).half()
-    kind, mod = _ref_dequant()
-    t0 = time.perf_counter()
-    if kind == "reference":
-        w = mod.dequant_trellis(torch.from_numpy(p.trellis), torch.from_numpy(p.suh),
-                                torch.from_numpy(p.svh), KBITS, True)
-    else:
-        w = torch.from_numpy(mod.dequant(p.trellis, p.suh, p.svh, KBITS, True))
-    y = h.float() @ w.float()
-    _ = float(y.sum())
-    return time.perf_counter() - t0, rows * out_f
-
-
-def cpu_reference(tokens: int, steps: int, warmup: int, budget_s: float):
-    """Time the reference CPU path on bounded samples; returns a dict.
-
-    A full step decodes gate, up and down of every distinct routed expert
-    (3 * H * I weights each) and runs their routes' matmuls.  Each sample runs
-    `cores` slices in parallel (one process each) sized so a sample takes about
-    `budget_s`; step time = full-step weights / sampled decode throughput."""
-    import multiprocessing as mp
+def _decode_batches_np(T: int, NB: int = 8, seed0: int = 100):
     import numpy as np
     from exl3_b200 import synthetic
-    cores = max(1, min(os.cpu_count() or 1, 32))
-    ctx = mp.get_context("spawn")
-    kind = _ref_dequant()[0]
-    rng = np.random.default_rng(5)
-    ids, _ = synthetic.softmax_topk(rng, tokens, E, TOPK)
-    uniq, counts = np.unique(ids, return_counts=True)
-    n_distinct = len(uniq)
-    step_weights = n_distinct * 3 * H * I
-    per_step = []
-    with ctx.Pool(cores) as pool:
-        cal = pool.map(_slice_task, [(9000 + c, c % 3, 128, 1) for c in range(cores)])
-        sec_per_w = statistics.median(t / n for t, n in cal)
-        rows = int(max(128, min(2048, budget_s / sec_per_w / I)) // 128 * 128)
-        for s in range(warmup + steps):
-            tasks = [(s * 131 + c, c % 3, rows, int(counts[c % n_distinct])) for c in range(cores)]
-            t0 = time.perf_counter()
-            res = pool.map(_slice_task, tasks)
-            wall = time.perf_counter() - t0
-            if s >= warmup:
-                per_step.append(wall * step_weights / sum(n for _, n in res))
-    step_s = statistics.median(per_step)
-    return {
-        "value": tokens / step_s,
-        "unit": "tokens/s",
-        "cores": cores,
-        "kind": kind,
-        "step_seconds": step_s,
-        "sample": (f"per sample {cores} parallel slices ({rows} input rows of one gate/up/down "
-                   f"projection each: dequant_trellis + the routes' matmul), scaled to the "
-                   f"{n_distinct} distinct experts x 3 projections of a T={tokens} step; median of "
-                   f"{len(per_step)} samples"),
-        "cpu": _cpu_model(),
-    }
+    out = []
+    for b in range(NB):
+        rng = np.random.default_rng(seed0 + b)
+        x = synthetic.activations(rng, T, H)
+        ids, w = synthetic.softmax_topk(rng, T, E, TOPK)
+        out.append((x, ids, w))
+    return out
 
 
-def _cpu_model():
+def cpu_reference(tokens: int, steps: int, warmup: int, per_step: int | None = None, cfg0: bool = False):
+    """Measured steps of the reference's eager loop on the host cores
+    (oracle/ref_loop.py); see the module docstring for what a step is."""
+    import numpy as np
+    import ref_loop
+    from exl3_b200 import synthetic
+    pack = synthetic.make_moe_pack(0, E, H, I, synthetic.CB_MCG, (KBITS,))
+    batches = _decode_batches_np(tokens)
+    pool = ref_loop.ExpertPool(pack)
     try:
-        with open("/proc/cpuinfo") as f:
-            for line in f:
-                if line.startswith("model name"):
-                    return line.split(":", 1)[1].strip()
-    except Exception:
-        pass
-    return "unknown"
+        n = pool.cores if per_step is None else per_step
+        r = ref_loop.sampled_steps(pool, batches, steps, warmup, n)
+    finally:
+        pool.close()
+    secs, fr = r["seconds"], r["fractions"]
+    eq_tokens = [tokens * f for f in fr]
+    value = sum(eq_tokens) / sum(secs)
+    distinct = float(np.mean([np.unique(b[1]).size for b in batches]))
+    res = {
+        "value": value, "unit": "tokens/s", "cores": pool.cores, "kind": ref_loop.ref_module()[0],
+        "ms_per_step": 1e3 * sum(secs) / len(secs),
+        "sample": (f"each step: the reference eager loop (apply_exl3_python_loop, dequant_trellis of the "
+                   f"reference's compiled csrc/bindings.cpp) over {n} of the batch's ~{distinct:.0f} distinct "
+                   f"experts, one process per host core; value = T={tokens} x sampled fraction / measured "
+                   f"step time, over {len(secs)} timed steps"),
+        "equivalent_tokens_per_step": float(np.mean(eq_tokens)),
+        "full_step_seconds_estimate": sum(secs) / sum(fr),
+        "cpu": ref_loop.cpu_model(), "nproc": os.cpu_count(),
+    }
+    if cfg0:
+        p0, x0, i0, w0 = synthetic.make_config("cfg1", seed=0)
+        med, reps = ref_loop.time_layer_serial(p0, x0, i0, w0, reps=3, threads=os.cpu_count() or 1)
+        res["cfg0_full_layer"] = {
+            "workload": "configs[0]: 8 experts top-2, H1024 I512, K4 MCG, T=16, whole layer, serial loop",
+            "seconds_median": med, "seconds": reps, "tokens_per_s": 16 / med,
+            "torch_threads": os.cpu_count()}
+    return res
 
 
 # ---------------------------------------------------------------------------
@@ -248,10 +220,41 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
+def _capture(fn, dev, warm: int = 2):
+    """fn captured in a CUDA graph after `warm` eager runs on a side stream."""
+    import torch
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(warm):
+            fn()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g
+
+
+def _timed_replays(graph, n, flush, load):
+    """CUDA events around each replay, after an untimed L2 flush and input load."""
+    import torch
+    evs = []
+    for i in range(n):
+        flush.zero_()
+        load(i)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        evs.append((a, b))
+    return evs
+
+
 # ---------------------------------------------------------------------------
-# the B200 arm
+# the headline: configs[1] decode on one GPU
 # ---------------------------------------------------------------------------
-def run_b200(args, rank, local_rank, world):
+def run_decode(args, rank, local_rank, world):
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -263,17 +266,11 @@ def run_b200(args, rank, local_rank, world):
     pack = synthetic.make_moe_pack(0, E, H, I, synthetic.CB_MCG, (KBITS,))
     layer = moe.layer_from_pack(pack, dev)
     NB = 8
-    batches = []
-    for b in range(NB):
-        rng = np.random.default_rng(100 + b)
-        x = synthetic.activations(rng, T, H)
-        ids, w = synthetic.softmax_topk(rng, T, E, TOPK)
-        batches.append((torch.from_numpy(x).to(dev).to(torch.bfloat16), torch.from_numpy(ids).to(dev),
-                        torch.from_numpy(w).to(dev)))
+    np_batches = _decode_batches_np(T, NB)
+    batches = [(torch.from_numpy(x).to(dev).to(torch.bfloat16), torch.from_numpy(ids).to(dev),
+                torch.from_numpy(w).to(dev)) for x, ids, w in np_batches]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    sx = batches[0][0].clone()
-    sid = batches[0][1].clone()
-    sw = batches[0][2].clone()
+    sx, sid, sw = (t.clone() for t in batches[0])
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
 
     def fwd():
@@ -285,36 +282,13 @@ def run_b200(args, rank, local_rank, world):
         sid.copy_(ids)
         sw.copy_(w)
 
-    # capture the layer once (5 kernels) in a CUDA graph
-    s = torch.cuda.Stream(dev)
-    s.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(s):
-        for _ in range(3):
-            fwd()
-    torch.cuda.current_stream(dev).wait_stream(s)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        fwd()
-
-    def timed_loop(n, record=True):
-        evs = []
-        for i in range(n):
-            flush.zero_()
-            load(i)
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            a.record()
-            graph.replay()
-            b.record()
-            evs.append((a, b))
-        return evs
-
-    timed_loop(args.warmup)
+    graph = _capture(fwd, dev, warm=3)
+    _timed_replays(graph, args.warmup, flush, load)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
     with ClockSampler(local_rank) as clk:
-        evs = timed_loop(args.steps)
+        evs = _timed_replays(graph, args.steps, flush, load)
         torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
@@ -326,7 +300,21 @@ def run_b200(args, rank, local_rank, world):
         total_ms = float(t.item())
     value = world * T * args.steps / (total_ms / 1e3)
 
-    # ---- per-kernel phase times (eager, library events, queued behind a spin)
+    # parity: batch 0 through the captured graph, every token, against the eager loop
+    par = None
+    if not args.no_parity:
+        import parity
+        f32 = torch.empty(T, H, dtype=torch.float32, device=dev)
+        load(0)
+        graph.replay()
+        f32.copy_(out.float())
+        torch.cuda.synchronize(dev)
+        _x0, ids0, w0 = np_batches[0]
+        xb = batches[0][0].float().cpu().numpy()
+        par = parity.check_moe(f32.cpu().numpy(), xb, ids0, w0, lambda e: pack.experts[e], E)
+        par["note"] = "bf16 output of the captured graph vs the eager loop, every token of one batch"
+
+    # per-kernel phase times (eager, library events, queued behind a spin)
     _native.profile_enable(True, 2_000_000)
     phases = []
     for i in range(12):
@@ -336,32 +324,35 @@ def run_b200(args, rank, local_rank, world):
         phases.append(_native.profile_read())
     _native.profile_enable(False)
     names = ["prep", "rotate", "gate_up", "down", "combine"]
+    n_ph = len(phases[0])
+    if n_ph != len(names):
+        names = [f"phase{j}" for j in range(n_ph)]
     ph = {n: statistics.median(p[j] for p in phases[2:]) * 1e3 for j, n in enumerate(names)}
 
     # algorithmic bytes (per step average over the rotating batches)
     tile_b = KBITS * 32
     gu_bytes_e = 2 * (H // 16) * (I // 16) * tile_b + 2 * (H + I) * 2
     dn_bytes_e = (I // 16) * (H // 16) * tile_b + (I + H) * 2
-    distinct = [len(np.unique(batches[b][1].cpu().numpy())) for b in range(NB)]
+    distinct = [len(np.unique(b[1])) for b in np_batches]
     routes = T * TOPK
     gu_bytes = np.mean([d * gu_bytes_e for d in distinct]) + routes * 2 * H * 2 + routes * I * 2
     layer_bytes = np.mean([d * (gu_bytes_e + dn_bytes_e) for d in distinct]) + T * H * 2 * 2
-    peak, peak_kind = peaks()
-    gu_s = ph["gate_up"] / 1e6
+    peak, _tpk, peak_kind = peaks()
+    gu_us = ph.get("gate_up")
     roofline = {
-        "kernel": "gemv_kernel<2,GATEUP> (gate+up decode GEMV)",
-        "bound": "hbm", "unit": "GB/s",
-        "achieved": gu_bytes / gu_s / 1e9, "peak": peak, "peak_kind": peak_kind,
-        "frac": gu_bytes / gu_s / 1e9 / peak,
-        "bytes_per_launch": gu_bytes, "us_per_launch": ph["gate_up"],
+        "kernel": "gemv_kernel<2,GATEUP> (gate+up decode GEMV)", "bound": "hbm", "unit": "GB/s",
+        "peak": peak, "peak_kind": peak_kind, "bytes_per_launch": gu_bytes, "us_per_launch": gu_us,
         "traffic": DRAM_TRAFFIC["decode"]["bytes"] if T == 64 else None,
         "traffic_source": DRAM_TRAFFIC["decode"]["source"] if T == 64 else None,
         "layer": {"bytes": layer_bytes, "us": total_ms / args.steps * 1e3,
                   "achieved": layer_bytes / (total_ms / args.steps / 1e3) / 1e9,
                   "frac": layer_bytes / (total_ms / args.steps / 1e3) / 1e9 / peak},
     }
+    if gu_us:
+        roofline["achieved"] = gu_bytes / (gu_us / 1e6) / 1e9
+        roofline["frac"] = roofline["achieved"] / peak
 
-    # ---- e2e through the public API with host buffers
+    # e2e through the public API with host buffers
     hx = [batches[b][0].cpu().pin_memory() for b in range(NB)]
     hid = [batches[b][1].cpu().pin_memory() for b in range(NB)]
     hw = [batches[b][2].cpu().pin_memory() for b in range(NB)]
@@ -396,11 +387,8 @@ def run_b200(args, rank, local_rank, world):
     h2d = T * H * 2 + T * TOPK * 8 + T * TOPK * 4
     d2h = T * H * 2
 
-    # ---- decode sweep (graph per batch size), single rank
-    sweep = {}
-    for tt in (1, 8, 32, 64):
-        sweep[str(tt)] = _sweep_point(layer, dev, tt, flush)
-
+    sweep = {str(tt): _sweep_point(layer, dev, tt, flush) for tt in (1, 8, 32, 64)}
+    del graph
     result = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
@@ -418,23 +406,147 @@ def run_b200(args, rank, local_rank, world):
         "e2e": {"value": world * T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "us_per_step": e2e_ms / args.steps * 1e3},
-        "gpu_launches": 5 * args.steps,
+        "gpu_launches": n_ph * args.steps,
         "clocks": clk.summary(),
         "decode_sweep_us_per_layer": sweep,
     }
-    del graph
+    if par is not None:
+        result["parity"] = par
+    del layer
+    torch.cuda.empty_cache()
     return result
 
 
-PREFILL = {
-    # GLM-class mixed-K prefill, mul1, K in {2,3}
-    "prefill": dict(cfg="cfg3", E=160, topk=8, H=5120, I=1536, tokens=2048,
-                    name="configs[2] mixed-K prefill: 160 experts top-8, H5120 I1536, K2/3 mul1"),
-}
+def _sweep_point(layer, dev, T, flush):
+    import numpy as np
+    import torch
+    from exl3_b200 import synthetic
+    rng = np.random.default_rng(7000 + T)
+    bs = []
+    for b in range(8):
+        x = synthetic.activations(rng, T, H)
+        ids, w = synthetic.softmax_topk(rng, T, E, TOPK)
+        bs.append((torch.from_numpy(x).to(dev).to(torch.bfloat16), torch.from_numpy(ids).to(dev),
+                   torch.from_numpy(w).to(dev)))
+    sx, sid, sw = (t.clone() for t in bs[0])
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
 
-# expert-parallel workloads: experts sharded evenly over the ranks, rows
-# exchanged over NVLink peer memory or NCCL (exl3_b200.ep, fixed-capacity
-# exchange)
+    def load(i):
+        sx.copy_(bs[i % 8][0])
+        sid.copy_(bs[i % 8][1])
+        sw.copy_(bs[i % 8][2])
+
+    g = _capture(lambda: layer.apply(sx, sw, sid, out=out), dev, warm=3)
+    ts = _timed_replays(g, 40, flush, load)
+    torch.cuda.synchronize(dev)
+    del g
+    return statistics.median(a.elapsed_time(b) * 1e3 for a, b in ts[8:])
+
+
+# ---------------------------------------------------------------------------
+# mixed-K prefill (tcgen05 grouped GEMM), one GPU
+# ---------------------------------------------------------------------------
+PREFILL = dict(cfg="cfg3", E=160, topk=8, H=5120, I=1536, tokens=2048,
+               name="configs[2] mixed-K prefill: 160 experts top-8, H5120 I1536, K2/3 mul1")
+
+
+def run_prefill(args, local_rank, steps, warmup, tokens=None):
+    import numpy as np
+    import torch
+    from exl3_b200 import _native, moe, synthetic
+
+    w = PREFILL
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    T = tokens or w["tokens"]
+    pack, x, ids, wt = synthetic.make_config(w["cfg"], seed=0, tokens=T)
+    layer = moe.layer_from_pack(pack, dev)
+    NB = 2
+    batches = [(torch.from_numpy(x).to(dev).to(torch.bfloat16), torch.from_numpy(ids).to(dev),
+                torch.from_numpy(wt).to(dev))]
+    rng = np.random.default_rng(1234)
+    x2 = synthetic.activations(rng, T, w["H"])
+    ids2, w2 = synthetic.softmax_topk(rng, T, w["E"], w["topk"], 1.5)
+    batches.append((torch.from_numpy(x2).to(dev).to(torch.bfloat16), torch.from_numpy(ids2).to(dev),
+                    torch.from_numpy(w2).to(dev)))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    sx, sid, sw = (t.clone() for t in batches[0])
+    out = torch.empty(T, w["H"], dtype=torch.bfloat16, device=dev)
+
+    def fwd():
+        layer.apply(sx, sw, sid, out=out)
+
+    def load(b):
+        sx.copy_(batches[b % NB][0])
+        sid.copy_(batches[b % NB][1])
+        sw.copy_(batches[b % NB][2])
+
+    graph = _capture(fwd, dev)
+    _timed_replays(graph, warmup, flush, load)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local_rank) as clk:
+        evs = _timed_replays(graph, steps, flush, load)
+        torch.cuda.synchronize(dev)
+    total_ms = sum(a.elapsed_time(b) for a, b in evs)
+
+    par = None
+    if not args.no_parity:
+        import parity
+        f32 = torch.empty(T, w["H"], dtype=torch.float32, device=dev)
+        load(0)
+        graph.replay()
+        f32.copy_(out.float())
+        torch.cuda.synchronize(dev)
+        sel = parity.sample_tokens(T, 8, seed=1)
+        xb = batches[0][0].float().cpu().numpy()[sel]
+        par = parity.check_moe(f32[torch.from_numpy(sel).to(dev)].cpu().numpy(), xb, ids[sel], wt[sel],
+                               lambda e: pack.experts[e], w["E"])
+        par["note"] = "bf16 output of the captured graph vs the eager loop, 8 sampled tokens x every column"
+    del graph
+
+    _native.profile_enable(True, 2_000_000)
+    phases = []
+    for i in range(4):
+        load(i)
+        fwd()
+        phases.append(_native.profile_read())
+    _native.profile_enable(False)
+    names = ["prep", "rotate", "gate_up", "act", "down", "combine"]
+    n_ph = len(phases[0])
+    ph = {n: statistics.median(p[j] for p in phases[1:]) * 1e3 for j, n in enumerate(names) if j < n_ph}
+
+    H_, I_, k = w["H"], w["I"], w["topk"]
+    flops_layer = T * k * 6.0 * H_ * I_
+    flops_gu = T * k * 4.0 * H_ * I_
+    _hbm, tpk, tkind = peaks()
+    gu_s = ph["gate_up"] / 1e6
+    step_s = total_ms / steps / 1e3
+    roofline = {"kernel": "tc_gemm_kernel (gate and up: tcgen05 grouped GEMM)", "bound": "tensor",
+                "unit": "TFLOP/s", "achieved": flops_gu / gu_s / 1e12, "peak": tpk, "peak_kind": tkind,
+                "frac": flops_gu / gu_s / 1e12 / tpk, "flops_per_launch": flops_gu, "us_per_launch": ph["gate_up"],
+                "traffic": DRAM_TRAFFIC["prefill"]["bytes"] if T == 2048 else None,
+                "traffic_source": DRAM_TRAFFIC["prefill"]["source"] if T == 2048 else None,
+                "layer": {"flops": flops_layer, "us": step_s * 1e6, "achieved": flops_layer / step_s / 1e12,
+                          "frac": flops_layer / step_s / 1e12 / tpk}}
+    res = {"metric": f"MoE layer prefill tokens/s ({w['name']})", "value": T * steps / (total_ms / 1e3),
+           "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": warmup,
+           "ms_per_step": total_ms / steps, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "fp16 MMA (tcgen05), fp32 accumulate", "data": "synthetic",
+           "config": {"workload": w["name"] + f", T={T}", "tokens_per_step": T,
+                      "l2": "256 MB L2 flush before every step (untimed)",
+                      "timing": "CUDA events per step around one CUDA-graph replay of the layer"},
+           "us_per_layer": step_s * 1e6, "phases_us": ph, "roofline": roofline,
+           "gpu_launches": n_ph * steps, "clocks": clk.summary()}
+    if par is not None:
+        res["parity"] = par
+    del layer
+    torch.cuda.empty_cache()
+    return res
+
+
+# ---------------------------------------------------------------------------
+# expert-parallel workloads
+# ---------------------------------------------------------------------------
 EP_WORKLOADS = {
     # configs[1] decode layer at N > 1: T tokens per rank (weak scaling)
     "decode": dict(E=128, topk=8, H=2048, I=768, cb=1, k=(4,), kp=None, router="softmax", sigma=1.0,
@@ -445,7 +557,7 @@ EP_WORKLOADS = {
 }
 
 
-def run_ep(args, rank, local_rank, world, which):
+def run_ep(args, rank, local_rank, world, which, steps, warmup):
     """One expert-parallel layer step per rank: dispatch and exchange, local
     fused forward, partial rows back, combine (fixed-capacity exchange, no
     host synchronisation inside a step)."""
@@ -463,28 +575,36 @@ def run_ep(args, rank, local_rank, world, which):
         Tr, scaling = args.tokens, "weak"
         Tt = Tr * world
     else:
-        Tt = c["tokens"] if args.tokens == 64 else args.tokens
+        Tt = c["tokens"]
         Tr, scaling = Tt // world, "strong"
     epr = E_ // world
-    lo, hi = rank * epr, (rank + 1) * epr
-    pack = synthetic.make_moe_pack_slice(0, E_, H_, I_, c["cb"], c["k"], c["kp"], lo, hi)
-    kbits = [e["gate"].K for e in pack.experts]
-    layer = moe.layer_from_pack(pack, dev)
-    del pack
+    lo = rank * epr
+
+    def make(a, b):
+        return synthetic.make_moe_pack_slice(0, E_, H_, I_, c["cb"], c["k"], c["kp"], a, b)
+
+    def expert_of(e):
+        return make(e, e + 1).experts[0]
+
+    layer = moe.layer_from_slices(lambda a, b: make(lo + a, lo + b), epr, H_, I_, dev)
+    kbits = [int(inn["gate"].K) for inn in layer._exl3_inners]
     ep = Exl3ExpertParallel(layer, E_, capacity=Tr, transport=args.ep_transport)
     NB = 4 if which == "decode" else 2
-    batches, local_routes, local_experts = [], [], []
+    batches, np_batches, local_routes, local_experts, rank_routes = [], [], [], [], []
     for b in range(NB):
         rng = np.random.default_rng([900 + b])  # routing of all tokens: identical on every rank
         if c["router"] == "softmax":
             ids, w = synthetic.softmax_topk(rng, Tt, E_, k, c["sigma"])
         else:
             ids, w = synthetic.sigmoid_zipf_topk(rng, Tt, E_, k)
-        mine = (ids >= lo) & (ids < hi)
+        owner = ids // epr
+        rank_routes.append([int((owner == g).sum()) for g in range(world)])
+        mine = owner == rank
         local_routes.append(int(mine.sum()))
         local_experts.append(len(np.unique(ids[mine])))
         x = synthetic.activations(np.random.default_rng([900 + b, rank]), Tr, H_)
         sl = slice(rank * Tr, (rank + 1) * Tr)
+        np_batches.append((x, ids[sl], w[sl]))
         batches.append((torch.from_numpy(x).to(torch.bfloat16).to(dev), torch.from_numpy(ids[sl]).to(dev),
                         torch.from_numpy(w[sl]).to(dev)))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -507,7 +627,7 @@ def run_ep(args, rank, local_rank, world, which):
     # Every rank must agree, so capture success is reduced over the ranks.
     graph = None
     sx, sid, sw = (t.clone() for t in batches[0])
-    if which == "decode" and not args.no_graph:
+    if not args.no_graph:
         ok, why = 1.0, ""
         try:
             side = torch.cuda.Stream(dev)
@@ -525,17 +645,20 @@ def run_ep(args, rank, local_rank, world, which):
         if max_over_ranks(ok, dist.ReduceOp.MIN if world > 1 else None) < 1.0:
             graph = None
             if why:
-                print(f"[bench] EP graph capture failed: {why}", file=sys.stderr)
+                log(f"EP graph capture failed: {why}")
+
+    def load(i):
+        x, ids, w = batches[i % NB]
+        sx.copy_(x)
+        sid.copy_(ids)
+        sw.copy_(w)
 
     def timed(n):
         evs = []
         for i in range(n):
             flush.zero_()
             if graph is not None:
-                x, ids, w = batches[i % NB]
-                sx.copy_(x)
-                sid.copy_(ids)
-                sw.copy_(w)
+                load(i)
             a0 = torch.cuda.Event(enable_timing=True)
             a1 = torch.cuda.Event(enable_timing=True)
             a0.record()
@@ -547,18 +670,45 @@ def run_ep(args, rank, local_rank, world, which):
             evs.append((a0, a1))
         return evs
 
-    timed(args.warmup)
+    timed(warmup)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
     with ClockSampler(local_rank) as clk:
-        evs = timed(args.steps)
+        evs = timed(steps)
         torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     total_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs))
-    step_s = total_ms / args.steps / 1e3
+    step_s = total_ms / steps / 1e3
+    ep.check_status()
+
+    # parity (rank 0's tokens of batch 0, a sample, against the eager loop);
+    # every rank runs the step, rank 0 checks
+    par = None
+    if not args.no_parity:
+        f32 = torch.empty(Tr, H_, dtype=torch.float32, device=dev)
+        if graph is not None:
+            load(0)
+            graph.replay()
+            f32.copy_(out.float())
+        else:
+            ep(batches[0][0], batches[0][2], batches[0][1], out=f32)
+        torch.cuda.synchronize(dev)
+        if rank == 0:
+            import parity
+            _xb, idb, wb = np_batches[0]
+            xb = batches[0][0].float().cpu().numpy()
+            sel = parity.sample_tokens(Tr, 8 if which == "decode" else 4, seed=3)
+            blocks = None if which == "decode" else parity.col_blocks(H_, 4, seed=3)
+            par = parity.check_moe(f32[torch.from_numpy(sel).to(dev)].cpu().numpy(), xb[sel], idb[sel],
+                                   wb[sel], expert_of, E_, blocks)
+            par["note"] = (f"rank 0's output ({'graph replay' if graph is not None else 'eager'}) vs the "
+                           f"eager loop over all {E_} experts, {len(sel)} sampled tokens"
+                           + ("" if blocks is None else f" x {len(blocks)} 128-column blocks"))
+        if world > 1:
+            dist.barrier()
 
     # per-phase times: the EP step (CUDA events between phases; with a graph,
     # event nodes captured into a second graph of the same step, so the
@@ -572,10 +722,7 @@ def run_ep(args, rank, local_rank, world, which):
             ep(sx, sw, sid, out=out)
         for i in range(4):
             flush.zero_()
-            x, ids, w = batches[i % NB]
-            sx.copy_(x)
-            sid.copy_(ids)
-            sw.copy_(w)
+            load(i)
             pgraph.replay()
             ep_ph.append(ep.phase_ms())
         del pgraph
@@ -596,29 +743,30 @@ def run_ep(args, rank, local_rank, world, which):
     nloc = len(loc[0])
     names = ["prep", "rotate", "gate_up", "act", "down", "combine"] if nloc == 6 else \
         ["prep", "rotate", "gate_up", "down", "combine"]
+    if nloc not in (5, 6):
+        names = [f"phase{j}" for j in range(nloc)]
     lph = {n: statistics.median(p[j] for p in loc[1:]) * 1e3 for j, n in enumerate(names)}
+    # the slowest rank's phases and local forward (the step waits for it)
+    eph_max = {n: max_over_ranks(v) for n, v in eph.items()}
+    lph_max = {n: max_over_ranks(v) for n, v in lph.items()}
 
-    peak_b, kind_b = peaks()
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            tpk, kind_t = float(json.load(f)["bf16_tflops"]), "measured"
-    except Exception:
-        tpk, kind_t = 1590.0, "fallback"
-    gu_s = lph["gate_up"] / 1e6
+    peak_b, tpk, kind = peaks()
+    gu_us = lph.get("gate_up", 0.0) or 1e-9
+    gu_s = gu_us / 1e6
     routes = float(np.mean(local_routes))
     if which == "ep":
         flops = routes * 4.0 * H_ * I_
-        roof = {"kernel": "tc_gemm_kernel x2 (gate, up) of the local forward, rank %d" % rank,
+        roof = {"kernel": "tc_gemm_kernel (gate and up) of the local forward, rank %d" % rank,
                 "bound": "tensor", "unit": "TFLOP/s", "achieved": flops / gu_s / 1e12, "peak": tpk,
-                "peak_kind": kind_t, "frac": flops / gu_s / 1e12 / tpk, "flops_per_launch": flops,
-                "us_per_launch": lph["gate_up"], "traffic": None}
+                "peak_kind": kind, "frac": flops / gu_s / 1e12 / tpk, "flops_per_launch": flops,
+                "us_per_launch": gu_us, "traffic": None}
     else:
         kb = float(np.mean(kbits))
         per_e = 2 * (H_ // 16) * (I_ // 16) * kb * 32 + 2 * (H_ + I_) * 2
         byts = float(np.mean(local_experts)) * per_e + routes * 2 * H_ * 2
         roof = {"kernel": "gate+up phase of the local forward, rank %d" % rank, "bound": "hbm", "unit": "GB/s",
-                "achieved": byts / gu_s / 1e9, "peak": peak_b, "peak_kind": kind_b,
-                "frac": byts / gu_s / 1e9 / peak_b, "bytes_per_launch": byts, "us_per_launch": lph["gate_up"],
+                "achieved": byts / gu_s / 1e9, "peak": peak_b, "peak_kind": kind,
+                "frac": byts / gu_s / 1e9 / peak_b, "bytes_per_launch": byts, "us_per_launch": gu_us,
                 "traffic": None}
 
     # e2e through the public API with pinned host buffers
@@ -639,22 +787,25 @@ def run_ep(args, rank, local_rank, world, which):
             evs.append((a0, a1))
         return evs
 
-    e2e(max(1, args.warmup))
+    e2e(max(1, warmup))
     torch.cuda.synchronize(dev)
-    evs = e2e(args.steps)
+    evs = e2e(steps)
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs))
+    ep.check_status()
     launches = (2 + nloc + 1) if args.ep_transport == "nccl" else (2 + 1 + nloc + 1 + 1 + 1)
     graph_used = graph is not None
     del graph
     torch.cuda.synchronize(dev)
     ep.close()
-    return {
+    rr = np.asarray(rank_routes, dtype=np.float64).mean(axis=0)
+    res = {
         "metric": METRIC if which == "decode" else f"MoE layer prefill tokens/s ({c['name']})",
-        "value": Tt * args.steps / (total_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "value": Tt * steps / (total_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": total_ms / steps, "higher_is_better": True,
         "scaling": scaling, "vs_baseline": None,
-        "dtype": "fp16 MMA, fp32 accumulate (int trellis decode); bf16 rows out, fp32 partials back", "data": "synthetic",
+        "dtype": "fp16 MMA, fp32 accumulate (int trellis decode); bf16 rows out, fp32 partials back",
+        "data": "synthetic",
         "config": {"workload": f"{c['name']}, T={Tt} tokens/step ({Tr} per rank)", "experts": E_,
                    "experts_per_rank": epr, "topk": k, "hidden": H_, "intermediate": I_,
                    "parallelism": f"ep{world}",
@@ -664,199 +815,77 @@ def run_ep(args, rank, local_rank, world, which):
                    "l2": "256 MB L2 flush before every step (untimed)",
                    "timing": ("CUDA events per step around one CUDA-graph replay of the EP step" if graph_used
                               else "CUDA events per step around the eager EP step") + ", max over ranks"},
-        "us_per_layer": step_s * 1e6, "phases_us": {"ep": eph, "local": lph}, "roofline": roof,
-        "local_routes_per_rank": routes,
-        "e2e": {"value": Tt * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+        "us_per_layer": step_s * 1e6,
+        "phases_us": {"ep_rank0": eph, "ep_max_over_ranks": eph_max, "local_rank0": lph,
+                      "local_max_over_ranks": lph_max},
+        "roofline": roof,
+        "local_routes_per_rank": {"rank0": routes, "max": float(rr.max()), "min": float(rr.min()),
+                                  "max_over_mean": float(rr.max() / rr.mean())},
+        "e2e": {"value": Tt * steps / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": Tr * H_ * 2 + Tr * k * 8 + Tr * k * 4, "d2h_bytes_per_step": Tr * H_ * 2,
-                "us_per_step": e2e_ms / args.steps * 1e3},
-        "gpu_launches": launches * args.steps, "clocks": clk.summary(),
+                "us_per_step": e2e_ms / steps * 1e3},
+        "gpu_launches": launches * steps, "clocks": clk.summary(),
     }
+    if par is not None:
+        res["parity"] = par
+    del layer, ep
+    torch.cuda.empty_cache()
+    return res
 
 
-def run_prefill(args, rank, local_rank, world):
-    """Tensor-bound workloads (tcgen05 grouped GEMM path); single GPU."""
-    import numpy as np
-    import torch
-    from exl3_b200 import _native, moe, synthetic
-
-    w = PREFILL[args.workload]
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    T = args.tokens if args.tokens != 64 else w["tokens"]
-    pack, x, ids, wt = synthetic.make_config(w["cfg"], seed=0, tokens=T)
-    layer = moe.layer_from_pack(pack, dev)
-    NB = 2
-    batches = [(torch.from_numpy(x).to(dev).to(torch.bfloat16), torch.from_numpy(ids).to(dev),
-                torch.from_numpy(wt).to(dev))]
-    rng = np.random.default_rng(1234)
-    x2 = synthetic.activations(rng, T, w["H"])
-    if w["cfg"] == "cfg5":
-        ids2, w2 = synthetic.sigmoid_zipf_topk(rng, T, w["E"], w["topk"])
-    else:
-        ids2, w2 = synthetic.softmax_topk(rng, T, w["E"], w["topk"], 1.5)
-    batches.append((torch.from_numpy(x2).to(dev).to(torch.bfloat16), torch.from_numpy(ids2).to(dev),
-                    torch.from_numpy(w2).to(dev)))
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    sx, sid, sw = (t.clone() for t in batches[0])
-    out = torch.empty(T, w["H"], dtype=torch.bfloat16, device=dev)
-
-    def fwd():
-        layer.apply(sx, sw, sid, out=out)
-
-    def load(b):
-        sx.copy_(batches[b % NB][0])
-        sid.copy_(batches[b % NB][1])
-        sw.copy_(batches[b % NB][2])
-
-    st = torch.cuda.Stream(dev)
-    st.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(st):
-        for _ in range(2):
-            fwd()
-    torch.cuda.current_stream(dev).wait_stream(st)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        fwd()
-
-    def timed(n):
-        evs = []
-        for i in range(n):
-            flush.zero_()
-            load(i)
-            a0 = torch.cuda.Event(enable_timing=True)
-            a1 = torch.cuda.Event(enable_timing=True)
-            a0.record()
-            graph.replay()
-            a1.record()
-            evs.append((a0, a1))
-        return evs
-
-    timed(args.warmup)
-    torch.cuda.synchronize(dev)
-    with ClockSampler(local_rank) as clk:
-        evs = timed(args.steps)
-        torch.cuda.synchronize(dev)
-    total_ms = sum(a.elapsed_time(b) for a, b in evs)
-
-    _native.profile_enable(True, 2_000_000)
-    phases = []
-    for i in range(4):
-        load(i)
-        fwd()
-        phases.append(_native.profile_read())
-    _native.profile_enable(False)
-    names = ["prep", "rotate", "gate_up", "act", "down", "combine"]
-    ph = {n: statistics.median(p[j] for p in phases[1:]) * 1e3 for j, n in enumerate(names) if j < len(phases[0])}
-
-    H_, I_, k = w["H"], w["I"], w["topk"]
-    flops_layer = T * k * 6.0 * H_ * I_
-    flops_gu = T * k * 4.0 * H_ * I_
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            tpk = float(json.load(f)["bf16_tflops"])
-        tkind = "measured"
-    except Exception:
-        tpk, tkind = 1590.0, "fallback"
-    gu_s = ph["gate_up"] / 1e6
-    step_s = total_ms / args.steps / 1e3
-    roofline = {"kernel": "tc_gemm_kernel x2 (gate, up: tcgen05 grouped GEMM)", "bound": "tensor",
-                "unit": "TFLOP/s", "achieved": flops_gu / gu_s / 1e12, "peak": tpk, "peak_kind": tkind,
-                "frac": flops_gu / gu_s / 1e12 / tpk, "flops_per_launch": flops_gu, "us_per_launch": ph["gate_up"],
-                "traffic": DRAM_TRAFFIC["prefill"]["bytes"] if T == 2048 else None,
-                "traffic_source": DRAM_TRAFFIC["prefill"]["source"] if T == 2048 else None,
-                "layer": {"flops": flops_layer, "us": step_s * 1e6, "achieved": flops_layer / step_s / 1e12,
-                          "frac": flops_layer / step_s / 1e12 / tpk}}
-    del graph
-    return {"metric": f"MoE layer prefill tokens/s ({w['name']})", "value": T * args.steps / (total_ms / 1e3),
-            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp16 MMA (tcgen05), fp32 accumulate", "data": "synthetic",
-            "config": {"workload": w["name"] + f", T={T}", "tokens_per_step": T,
-                       "l2": "256 MB L2 flush before every step (untimed)"},
-            "us_per_layer": step_s * 1e6, "phases_us": ph, "roofline": roofline,
-            "gpu_launches": 7 * args.steps, "clocks": clk.summary()}
-
-
-def _sweep_point(layer, dev, T, flush):
-    import numpy as np
-    import torch
-    from exl3_b200 import synthetic
-    rng = np.random.default_rng(7000 + T)
-    bs = []
-    for b in range(8):
-        x = synthetic.activations(rng, T, H)
-        ids, w = synthetic.softmax_topk(rng, T, E, TOPK)
-        bs.append((torch.from_numpy(x).to(dev).to(torch.bfloat16), torch.from_numpy(ids).to(dev),
-                   torch.from_numpy(w).to(dev)))
-    sx, sid, sw = (t.clone() for t in bs[0])
-    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
-    s = torch.cuda.Stream(dev)
-    s.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(s):
-        for _ in range(3):
-            layer.apply(sx, sw, sid, out=out)
-    torch.cuda.current_stream(dev).wait_stream(s)
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        layer.apply(sx, sw, sid, out=out)
-    ts = []
-    for i in range(40):
-        flush.zero_()
-        sx.copy_(bs[i % 8][0])
-        sid.copy_(bs[i % 8][1])
-        sw.copy_(bs[i % 8][2])
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record()
-        g.replay()
-        b.record()
-        ts.append((a, b))
-    torch.cuda.synchronize(dev)
-    del g
-    vals = [a.elapsed_time(b) * 1e3 for a, b in ts[8:]]
-    return statistics.median(vals)
+def _ref_line(args, world):
+    r = cpu_reference(args.tokens, args.steps, args.warmup, cfg0=True)
+    return {"metric": METRIC, "value": r["value"], "unit": "tokens/s", "impl": "reference",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (CPU; fp16 weights and activations)",
+            "data": "synthetic",
+            "config": {"workload": f"configs[1] decode GEMV, T={args.tokens} tokens/step",
+                       "experts": E, "topk": TOPK, "hidden": H, "intermediate": I, "K": KBITS,
+                       "codebook": "MCG"},
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu", "nproc")},
+            "equivalent_tokens_per_step": r["equivalent_tokens_per_step"],
+            "full_step_seconds_estimate": r["full_step_seconds_estimate"],
+            "cfg0_full_layer": r["cfg0_full_layer"],
+            "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():
     args = parse()
     rank, local_rank, world = env_rank()
     if args.impl == "reference":
-        if rank != 0:
-            return
-        budget = max(0.05, min(2.0, 150.0 / max(1, args.steps + args.warmup)))
-        r = cpu_reference(args.tokens, args.steps, args.warmup, budget)
-        line = {"metric": METRIC, "value": r["value"], "unit": "tokens/s", "impl": "reference",
-                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": r["step_seconds"] * 1e3, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (CPU)", "data": "synthetic",
-                "config": {"workload": f"configs[1] decode GEMV, T={args.tokens} tokens/step",
-                           "experts": E, "topk": TOPK, "hidden": H, "intermediate": I, "K": KBITS},
-                "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
-                "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
+        if rank == 0:
+            print(json.dumps(_ref_line(args, world)), flush=True)
         return
 
     import torch
     import torch.distributed as dist
     from datetime import timedelta
+    # the CPU sample runs first, before CUDA is touched (spawned workers)
+    cpu = None
+    if rank == 0 and world == 1 and args.workload == "decode" and not args.no_cpu_baseline:
+        cpu = cpu_reference(args.tokens, 2, 1)
     if args.workload == "prefill":
-        print(json.dumps(run_prefill(args, rank, local_rank, world)), flush=True)
+        print(json.dumps(run_prefill(args, local_rank, args.steps, args.warmup,
+                                     args.tokens if args.tokens != 64 else None)), flush=True)
         return
     if world > 1:
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    # the CPU sample runs first, before CUDA is touched (spawned workers)
-    cpu = None
-    if rank == 0 and world == 1 and args.workload == "decode" and not args.no_cpu_baseline:
-        cpu = cpu_reference(args.tokens, 5, 1, 2.0)
-    if args.workload == "ep" or world > 1:
-        res = run_ep(args, rank, local_rank, world, "ep" if args.workload == "ep" else "decode")
+    if args.workload == "ep":
+        res = run_ep(args, rank, local_rank, world, "ep", args.steps, args.warmup)
     else:
-        res = run_b200(args, rank, local_rank, world)
+        res = (run_ep(args, rank, local_rank, world, "decode", args.steps, args.warmup) if world > 1
+               else run_decode(args, rank, local_rank, world))
+        sub_steps, sub_warm = max(3, min(args.steps, 20)), max(3, min(args.warmup, 5))
+        if world == 1 and not args.no_prefill:
+            res["prefill"] = run_prefill(args, local_rank, sub_steps, sub_warm)
+        if not args.no_ep_cfg4:
+            res["ep_cfg4"] = run_ep(args, rank, local_rank, world, "ep", sub_steps, sub_warm)
     if cpu is not None:
-        res["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        res["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu", "nproc")}
+        res["cpu_baseline"]["ms_per_step"] = cpu["ms_per_step"]
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

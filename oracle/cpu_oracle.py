@@ -44,6 +44,9 @@ def _load():
         P = ctypes.c_void_p
         lib.oracle_dequant.argtypes = [P, P, P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int, P]
         lib.oracle_dequant.restype = ctypes.c_int
+        lib.oracle_dequant_cols.argtypes = [P, P, P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int64, ctypes.c_int64, P]
+        lib.oracle_dequant_cols.restype = ctypes.c_int
         lib.oracle_decode_raw.argtypes = [P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int, P]
         lib.oracle_decode_raw.restype = None
         lib.oracle_decode_codebook_many.argtypes = [P, ctypes.c_int64, ctypes.c_int, P]
@@ -123,6 +126,24 @@ def dequant(trellis: np.ndarray, suh: np.ndarray, svh: np.ndarray, K: int, mcg: 
     return out.view(np.float16)
 
 
+def dequant_cols(trellis: np.ndarray, suh: np.ndarray, svh: np.ndarray, K: int, cb: int, c0: int,
+                 c1: int) -> np.ndarray:
+    """Columns [c0, c1) (multiples of 128) of ``dequant``'s result as float16
+    [in, c1 - c0].  Each 128x128 block of the reconstruction depends only on
+    its own tiles and scales, so this equals ``dequant(...)[:, c0:c1]`` bit
+    for bit without decoding the other columns."""
+    t = _check_trellis(trellis, K)
+    rows, cols = t.shape[0] * 16, t.shape[1] * 16
+    su = np.ascontiguousarray(np.asarray(suh, dtype=np.float16).reshape(-1)[:rows]).view(np.uint16)
+    sv = np.ascontiguousarray(np.asarray(svh, dtype=np.float16).reshape(-1)[:cols]).view(np.uint16)
+    out = np.empty((rows, c1 - c0), dtype=np.uint16)
+    rc = _load().oracle_dequant_cols(_ptr(t), _ptr(su), _ptr(sv), rows, cols, int(K), int(cb), int(c0), int(c1),
+                                     _ptr(out))
+    if rc != 0:
+        raise ValueError("column range and dimensions must be whole 128-element Hadamard blocks")
+    return out.view(np.float16)
+
+
 def map_topk_to_local(ids: np.ndarray, n_local: int, expert_map: np.ndarray | None) -> np.ndarray:
     """Global expert ids -> local ids; invalid or non-local routes -> the
     ``n_local`` sentinel (``exl3.py:2332-2354``)."""
@@ -142,34 +163,48 @@ def silu(x: np.ndarray) -> np.ndarray:
     return x / (1.0 + np.exp(-x.astype(np.float64))).astype(np.float32)
 
 
-def moe_eager(x: np.ndarray, ids: np.ndarray, weights: np.ndarray, dense: list,
+def moe_eager(x: np.ndarray, ids: np.ndarray, weights: np.ndarray, dense,
               expert_map: np.ndarray | None = None, limit: float | None = None,
-              act: str = "silu") -> np.ndarray:
+              act: str = "silu", n_local: int | None = None) -> np.ndarray:
     """``apply_exl3_python_loop`` (``exl3.py:2357-2413``).
 
     ``dense[e]`` maps ``"gate"``, ``"up"``, ``"down"`` to the float16 weights
     ``dequant`` produced for local expert e (``"gate"`` may be None for a
-    gateless layer).  Per unique local expert, ascending: gather its routes,
-    ``h.half()``, gate/up in fp32, clamp (gate from above, up both sides) when
+    gateless layer).  ``dense`` may also be a callable ``dense(e)`` returning
+    that dict (then ``n_local`` is required): experts are then decoded one at
+    a time, only those the routes touch, and dropped after use, so
+    full-size layers fit in host memory.  ``"down"`` may hold a subset of the
+    output columns; the result then has those columns only.
+
+    Per unique local expert, ascending: gather its routes, ``h.half()``,
+    gate/up in fp32, clamp (gate from above, up both sides) when
     ``limit > 0``, ``act = silu(g) * u`` (or the OAI / relu^2 variants),
     ``down = act.half() @ W_down`` in fp32, and ``out.index_add_`` of
     ``down * w``.  Returns fp32 [T, H].
     """
     x = np.asarray(x)
     T, H = x.shape
-    out = np.zeros((T, H), dtype=np.float32)
-    local = map_topk_to_local(ids, len(dense), expert_map).reshape(np.shape(ids))
+    if callable(dense):
+        if n_local is None:
+            raise ValueError("n_local is required with a callable dense")
+        get = dense
+    else:
+        n_local = len(dense)
+        get = dense.__getitem__
+    out = None
+    local = map_topk_to_local(ids, n_local, expert_map).reshape(np.shape(ids))
     w = np.asarray(weights, dtype=np.float32).reshape(local.shape)
     xh = x.astype(np.float16).astype(np.float32)
-    gateless = bool(dense) and dense[0].get("gate") is None
     for e in np.unique(local).tolist():
-        if e >= len(dense):
+        if e >= n_local:
             continue
         tok, kpos = np.nonzero(local == e)
         h = xh[tok]
-        pack = dense[e]
+        pack = get(e)
+        if out is None:
+            out = np.zeros((T, pack["down"].shape[1]), dtype=np.float32)
         up = h @ pack["up"].astype(np.float32)
-        if gateless:
+        if pack.get("gate") is None:
             if limit is not None and limit > 0:
                 up = np.clip(up, -limit, limit)
             a = np.square(np.maximum(up, 0.0))
@@ -185,4 +220,6 @@ def moe_eager(x: np.ndarray, ids: np.ndarray, weights: np.ndarray, dense: list,
         a = a.astype(np.float32).astype(np.float16).astype(np.float32)
         d = a @ pack["down"].astype(np.float32)
         np.add.at(out, tok, d * w[tok, kpos][:, None])
+    if out is None:
+        out = np.zeros((T, H), dtype=np.float32)
     return out

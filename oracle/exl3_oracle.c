@@ -18,9 +18,11 @@
  * separate adds; contraction into FMA would change bits.
  */
 #include <math.h>
+#include <pthread.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
 
 #define MCG_MUL 0xCBAC1FEDu  /* exl3_dequant.cuh:9 */
 #define MUL1_MUL 0x83DCD12Du /* exl3_dequant.cuh:10 */
@@ -163,42 +165,122 @@ void oracle_hadamard(float* v, int n) {
             }
 }
 
-/* Full reconstruction W = diag(suh) H W~ H diag(svh) / 128 with the
- * reference's float rounding order (bindings.cpp:79-98): per 128x128 block,
- * rows transformed then scaled by norm, columns transformed then multiplied
- * left to right by norm, suh[r], svh[c], and rounded to fp16.
- * Returns 0, or -1 when rows/cols are not multiples of 128 (bindings.cpp:22). */
-int oracle_dequant(const int16_t* trellis, const uint16_t* suh, const uint16_t* svh,
-                   int64_t rows, int64_t cols, int K, int cb, uint16_t* out) {
-    if (rows % 128 || cols % 128 || rows <= 0 || cols <= 0) return -1;
-    float* m = (float*)malloc((size_t)rows * (size_t)cols * sizeof(float));
-    uint16_t* raw = (uint16_t*)malloc((size_t)rows * (size_t)cols * sizeof(uint16_t));
-    if (!m || !raw) { free(m); free(raw); return -2; }
-    oracle_decode_raw(trellis, rows, cols, K, cb, raw);
-    for (int64_t i = 0; i < rows * cols; ++i) m[i] = oracle_half_to_float(raw[i]);
-    free(raw);
-    const float norm = 0.08838834764831845f;
+/* Lookup tables built once from the restated functions above: the codebook
+ * of every 16-bit state for each codebook, and binary16 -> float.  They are
+ * the same functions tabulated, so results stay bit-identical; they only
+ * take the per-weight cost of the parity checker from ~160 ns to a few. */
+static uint16_t g_cb_lut[3][65536];
+static float g_h2f_lut[65536];
+static pthread_once_t g_lut_once = PTHREAD_ONCE_INIT;
+
+static void build_luts(void) {
+    for (uint32_t w = 0; w < 65536u; ++w) {
+        for (int cb = 0; cb < 3; ++cb) g_cb_lut[cb][w] = oracle_decode_codebook((uint16_t)w, cb);
+        g_h2f_lut[w] = oracle_half_to_float((uint16_t)w);
+    }
+}
+
+/* One 128x128 block (rows r0.., columns c0..) of the reconstruction, the
+ * reference's float rounding order (bindings.cpp:79-98): rows transformed
+ * then scaled by norm, columns transformed then multiplied left to right by
+ * norm, suh[r], svh[c], then rounded to fp16.  `out` has row pitch `pitch`. */
+static void dequant_block(const int16_t* trellis, const uint16_t* suh, const uint16_t* svh, int64_t cols,
+                          int K, int cb, int64_t r0, int64_t c0, uint16_t* out, int64_t pitch) {
+    const size_t words = (size_t)16 * (size_t)K;
+    const int64_t nt_n = cols / 16;
+    static const float norm = 0.08838834764831845f;
+    float m[128][128];
     float line[128];
-    for (int64_t r0 = 0; r0 < rows; r0 += 128)
-        for (int64_t c0 = 0; c0 < cols; c0 += 128) {
-            for (int r = 0; r < 128; ++r) {
-                float* row = m + (r0 + r) * cols + c0;
-                for (int c = 0; c < 128; ++c) line[c] = row[c];
-                oracle_hadamard(line, 128);
-                for (int c = 0; c < 128; ++c) row[c] = line[c] * norm;
-            }
-            for (int c = 0; c < 128; ++c) {
-                for (int r = 0; r < 128; ++r) line[r] = m[(r0 + r) * cols + c0 + c];
-                oracle_hadamard(line, 128);
-                const float sv = oracle_half_to_float(svh[c0 + c]);
-                for (int r = 0; r < 128; ++r) {
-                    const float v = line[r] * norm * oracle_half_to_float(suh[r0 + r]) * sv;
-                    out[(r0 + r) * cols + c0 + c] = oracle_float_to_half(v);
+    for (int kt = 0; kt < 8; ++kt)
+        for (int nt = 0; nt < 8; ++nt) {
+            const uint16_t* tile =
+                (const uint16_t*)trellis + (size_t)(((r0 / 16) + kt) * nt_n + (c0 / 16) + nt) * words;
+            for (int l = 0; l < 32; ++l) {
+                const int rr = (l % 4) * 2, cc = l / 4;
+                for (int j = 0; j < 8; ++j) {
+                    const size_t start = ((size_t)(8 * l + j) + 257u) * (size_t)K - 16u;
+                    const uint16_t v = g_cb_lut[cb][oracle_read_window(tile, words, start)];
+                    const int row = rr + (j & 1) + ((j & 2) ? 8 : 0);
+                    const int col = cc + ((j & 4) ? 8 : 0);
+                    m[kt * 16 + row][nt * 16 + col] = g_h2f_lut[v];
                 }
             }
         }
-    free(m);
+    for (int r = 0; r < 128; ++r) {
+        oracle_hadamard(m[r], 128);
+        for (int c = 0; c < 128; ++c) m[r][c] = m[r][c] * norm;
+    }
+    for (int c = 0; c < 128; ++c) {
+        for (int r = 0; r < 128; ++r) line[r] = m[r][c];
+        oracle_hadamard(line, 128);
+        const float sv = g_h2f_lut[svh[c0 + c]];
+        for (int r = 0; r < 128; ++r) {
+            const float v = line[r] * norm * g_h2f_lut[suh[r0 + r]] * sv;
+            out[(size_t)r * (size_t)pitch + (size_t)c] = oracle_float_to_half(v);
+        }
+    }
+}
+
+struct dq_job {
+    const int16_t* trellis;
+    const uint16_t* suh;
+    const uint16_t* svh;
+    int64_t rows, cols, c0, c1;
+    int K, cb;
+    uint16_t* out;
+    int64_t next;  /* next block index, claimed atomically */
+};
+
+static void* dq_worker(void* arg) {
+    struct dq_job* j = (struct dq_job*)arg;
+    const int64_t ncb = (j->c1 - j->c0) / 128, nblk = (j->rows / 128) * ncb;
+    const int64_t pitch = j->c1 - j->c0;
+    for (;;) {
+        const int64_t b = __atomic_fetch_add(&j->next, 1, __ATOMIC_RELAXED);
+        if (b >= nblk) break;
+        const int64_t r0 = (b / ncb) * 128, cb0 = (b % ncb) * 128;
+        dequant_block(j->trellis, j->suh, j->svh, j->cols, j->K, j->cb, r0, j->c0 + cb0,
+                      j->out + (size_t)r0 * (size_t)pitch + (size_t)cb0, pitch);
+    }
+    return NULL;
+}
+
+static int oracle_threads(void) {
+    const char* e = getenv("EXL3_ORACLE_THREADS");
+    long n = e ? strtol(e, NULL, 10) : sysconf(_SC_NPROCESSORS_ONLN);
+    if (n < 1) n = 1;
+    if (n > 64) n = 64;
+    return (int)n;
+}
+
+/* Columns [c0, c1) (multiples of 128) of W = diag(suh) H W~ H diag(svh) /
+ * 128 as fp16 bits, out [rows][c1 - c0].  The 128x128 blocks are
+ * independent, so any column range is exactly the corresponding columns of
+ * the full reconstruction.  Blocks are spread over host threads.
+ * Returns 0, -1 for dimensions that are not whole blocks (bindings.cpp:22). */
+int oracle_dequant_cols(const int16_t* trellis, const uint16_t* suh, const uint16_t* svh, int64_t rows,
+                        int64_t cols, int K, int cb, int64_t c0, int64_t c1, uint16_t* out) {
+    if (rows % 128 || cols % 128 || rows <= 0 || cols <= 0) return -1;
+    if (c0 < 0 || c1 > cols || c0 >= c1 || c0 % 128 || c1 % 128) return -1;
+    if (K < 1 || K > 8 || cb < 0 || cb > 2) return -1;
+    pthread_once(&g_lut_once, build_luts);
+    struct dq_job job = {trellis, suh, svh, rows, cols, c0, c1, K, cb, out, 0};
+    const int64_t nblk = (rows / 128) * ((c1 - c0) / 128);
+    int nt = oracle_threads();
+    if (nt > nblk) nt = (int)nblk;
+    pthread_t th[64];
+    int started = 0;
+    for (int t = 1; t < nt; ++t)
+        if (pthread_create(&th[started], NULL, dq_worker, &job) == 0) ++started;
+    dq_worker(&job);
+    for (int t = 0; t < started; ++t) pthread_join(th[t], NULL);
     return 0;
+}
+
+/* Full reconstruction (bindings.cpp:15-100): every column. */
+int oracle_dequant(const int16_t* trellis, const uint16_t* suh, const uint16_t* svh,
+                   int64_t rows, int64_t cols, int K, int cb, uint16_t* out) {
+    return oracle_dequant_cols(trellis, suh, svh, rows, cols, K, cb, 0, cols, out);
 }
 
 /* Batch helpers for the Python wrapper. */

@@ -203,3 +203,38 @@ def nccl_worker(rank: int, world: int, port: int, cfg: dict, result_q) -> None:
         dist.barrier()
     finally:
         dist.destroy_process_group()
+
+
+def nvlink_emulated_step(layers, wins, x, ids, w, E, G, C, out_dtype):
+    """G ranks' NVLink steps on one GPU, phase by phase across the ranks (all
+    dispatches, then every rank's wait + local forward + return, then every
+    rank's wait + combine): no wait ever depends on a later launch."""
+    from exl3_b200 import _native as _n
+    from exl3_b200.moe import moe_forward_ptrs
+    lib = _n.load()
+    T = x.shape[0] // G
+    H = x.shape[1]
+    topk = ids.shape[1]
+    dev = x.device
+    stream = _n.stream_of(x)
+    pidx = [torch.empty(C, G, dtype=torch.int32, device=dev) for _ in range(G)]
+    part = [torch.empty(G * C, H, dtype=torch.float32, device=dev) for _ in range(G)]
+    outs = [torch.empty(T, H, dtype=out_dtype, device=dev) for _ in range(G)]
+    for r in range(G):
+        xr, ir, wr = x[r * T:(r + 1) * T], ids[r * T:(r + 1) * T], w[r * T:(r + 1) * T]
+        _n.check(lib.exl3_ep_p2p_dispatch(xr.data_ptr(), _n.dtype_code(xr), T, H, ir.data_ptr(),
+                                          _n.dtype_code(ir), wr.data_ptr(), _n.dtype_code(wr), topk, E, G, r, C,
+                                          None, wins[r].window, wins[r].peers.data_ptr(), _n.DT_F32,
+                                          pidx[r].data_ptr(), stream))
+    for r in range(G):
+        _n.check(lib.exl3_ep_p2p_wait(wins[r].window, G, 0, stream))
+        moe_forward_ptrs(layers[r], dev, wins[r].recv_x, _n.dtype_code(x), G * C, wins[r].recv_ids, _n.DT_I32,
+                         wins[r].recv_w, _n.DT_F32, topk, part[r].data_ptr(), _n.DT_F32)
+        _n.check(lib.exl3_ep_p2p_return(part[r].data_ptr(), _n.DT_F32, G, r, C, H, topk, _n.dtype_code(x),
+                                        wins[r].window, wins[r].peers.data_ptr(), stream))
+    for r in range(G):
+        _n.check(lib.exl3_ep_p2p_wait(wins[r].window, G, 1, stream))
+        _n.check(lib.exl3_ep_p2p_combine(wins[r].window, G, r, C, H, topk, _n.dtype_code(x), _n.DT_F32,
+                                         pidx[r].data_ptr(), T, None, outs[r].data_ptr(), _n.dtype_code(outs[r]),
+                                         stream))
+    return torch.cat(outs)

@@ -232,42 +232,6 @@ def test_ep_world1_module_matches_layer(native, cuda, cap):
     _close(got[:17], want[:17], rel=1e-3)
 
 
-def _nvlink_emulated_step(layers, wins, x, ids, w, E, G, C, out_dtype):
-    """G ranks' NVLink steps on one GPU, phase by phase across the ranks (all
-    dispatches, then every rank's wait + local forward + return, then every
-    rank's wait + combine): no wait ever depends on a later launch."""
-    import torch
-    from exl3_b200 import _native as _n
-    from exl3_b200.moe import moe_forward_ptrs
-    lib = _n.load()
-    T = x.shape[0] // G
-    H = x.shape[1]
-    topk = ids.shape[1]
-    dev = x.device
-    stream = _n.stream_of(x)
-    pidx = [torch.empty(C, G, dtype=torch.int32, device=dev) for _ in range(G)]
-    part = [torch.empty(G * C, H, dtype=torch.float32, device=dev) for _ in range(G)]
-    outs = [torch.empty(T, H, dtype=out_dtype, device=dev) for _ in range(G)]
-    for r in range(G):
-        xr, ir, wr = x[r * T:(r + 1) * T], ids[r * T:(r + 1) * T], w[r * T:(r + 1) * T]
-        _n.check(lib.exl3_ep_p2p_dispatch(xr.data_ptr(), _n.dtype_code(xr), T, H, ir.data_ptr(),
-                                          _n.dtype_code(ir), wr.data_ptr(), _n.dtype_code(wr), topk, E, G, r, C,
-                                          None, wins[r].window, wins[r].peers.data_ptr(), _n.DT_F32,
-                                          pidx[r].data_ptr(), stream))
-    for r in range(G):
-        _n.check(lib.exl3_ep_p2p_wait(wins[r].window, G, 0, stream))
-        moe_forward_ptrs(layers[r], dev, wins[r].recv_x, _n.dtype_code(x), G * C, wins[r].recv_ids, _n.DT_I32,
-                         wins[r].recv_w, _n.DT_F32, topk, part[r].data_ptr(), _n.DT_F32)
-        _n.check(lib.exl3_ep_p2p_return(part[r].data_ptr(), _n.DT_F32, G, r, C, H, topk, _n.dtype_code(x),
-                                        wins[r].window, wins[r].peers.data_ptr(), stream))
-    for r in range(G):
-        _n.check(lib.exl3_ep_p2p_wait(wins[r].window, G, 1, stream))
-        _n.check(lib.exl3_ep_p2p_combine(wins[r].window, G, r, C, H, topk, _n.dtype_code(x), _n.DT_F32,
-                                         pidx[r].data_ptr(), T, None, outs[r].data_ptr(), _n.dtype_code(outs[r]),
-                                         stream))
-    return torch.cat(outs)
-
-
 @pytest.mark.gpu
 @pytest.mark.parametrize("G", [2, 4])
 def test_ep_nvlink_emulated_ranks(native, cuda, G):
@@ -297,7 +261,7 @@ def test_ep_nvlink_emulated_ranks(native, cuda, G):
             ids, w = synthetic.softmax_topk(rng, Tr * G, E, topk)
             x = torch.from_numpy(xs).to(torch.bfloat16).to(cuda)
             idt, wt = torch.from_numpy(ids).to(cuda), torch.from_numpy(w).to(cuda)
-            got = _nvlink_emulated_step(layers, wins, x, idt, wt, E, G, C, torch.float32).cpu().numpy()
+            got = ep_helpers.nvlink_emulated_step(layers, wins, x, idt, wt, E, G, C, torch.float32).cpu().numpy()
             single = torch.empty(x.shape[0], H, dtype=torch.float32, device=cuda)
             full.apply(x, wt, idt, out=single)
             _close(got, single.cpu().numpy())
@@ -377,3 +341,35 @@ def test_ep_nccl_two_gpus(native, capacity, transport):
     for r in range(world):
         sl = slice(r * cfg["T"], (r + 1) * cfg["T"])
         _close(got[r], oracle.moe_eager(xh[sl], ids[sl], w[sl], dense))
+
+
+@pytest.mark.gpu
+def test_ep_nvlink_forward_reports_failed_wait(native, cuda):
+    """A failure recorded in the window's status word (as a bounded peer wait
+    that gave up records it; here written by the host, so no kernel has to
+    time out) makes the next forward() raise, and check_status() raises at
+    once, instead of steps continuing on stale rows."""
+    import torch
+    from exl3_b200 import moe, synthetic
+    from exl3_b200.ep import Exl3ExpertParallel
+    pack = synthetic.make_moe_pack(8, 8, 256, 128, synthetic.CB_MCG, (4,))
+    layer = moe.layer_from_pack(pack, cuda)
+    ep = Exl3ExpertParallel(layer, 8, combine_dtype=torch.float32, capacity=16, transport="nvlink")
+    try:
+        rng = np.random.default_rng(3)
+        x = torch.from_numpy(synthetic.activations(rng, 16, 256)).to(torch.bfloat16).to(cuda)
+        ids, w = synthetic.softmax_topk(rng, 16, 8, 2)
+        idt, wt = torch.from_numpy(ids).to(cuda), torch.from_numpy(w).to(cuda)
+        ep(x, wt, idt)
+        ep.check_status()  # clean
+        win = ep.window(x.dtype, 2, 256)
+        win.status_tensor().fill_(4)  # what ep_p2p_wait_kernel records on a timeout
+        ep(x, wt, idt)                # this step's status copy carries the failure to the host
+        torch.cuda.synchronize(cuda)
+        with pytest.raises(RuntimeError, match="status 4"):
+            ep(x, wt, idt)
+        with pytest.raises(RuntimeError, match="status 4"):
+            ep.check_status()
+        assert win.status(clear=True) == 4
+    finally:
+        ep.close()

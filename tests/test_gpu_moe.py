@@ -302,3 +302,43 @@ def test_graph_replay_consumes_new_inputs_and_is_deterministic(native, cuda):
         torch.cuda.synchronize()
         _close(out.cpu().numpy(), oracle.moe_eager(x2, ids2, w, dense))
     del g
+
+
+def test_graph_survives_workspace_growth(native, cuda):
+    """A graph captured with a cached workspace keeps its results after a
+    larger eager call on the same stream has grown the workspace, and its
+    replay writes into no memory the allocator has since given to other
+    tensors (the replaced workspace stays allocated)."""
+    import torch
+    from exl3_b200 import synthetic
+    pack, layer, x, ids, w = _setup(cuda, "cfg1", seed=21, tokens=4)
+    dense = _dense(pack)
+    s = torch.cuda.Stream(cuda)
+    xt, wt, it = (torch.from_numpy(a).to(cuda) for a in (x, w, ids))
+    out = torch.empty_like(xt)
+    with torch.cuda.stream(s):
+        for _ in range(2):  # warm-up: sizes this stream's workspace for the captured shape
+            layer.apply(xt, wt, it, out=out)
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        layer.apply(xt, wt, it, out=out)
+    # 600 tokens (the tensor-core GEMM path) need a far larger workspace
+    rng = np.random.default_rng(22)
+    xb = synthetic.activations(rng, 600, 1024)
+    idb, wb = synthetic.softmax_topk(rng, 600, 8, 2)
+    with torch.cuda.stream(s):
+        big = layer.apply(torch.from_numpy(xb).to(cuda), torch.from_numpy(wb).to(cuda),
+                          torch.from_numpy(idb).to(cuda))
+    s.synchronize()
+    _close(big.cpu().numpy(), oracle.moe_eager(xb, idb, wb, dense))
+    # unrelated tensors take whatever the allocator has free now
+    fillers = [torch.full((1 << 18,), 7.0, device=cuda) for _ in range(64)]
+    x2 = np.random.default_rng(23).normal(0, 1, x.shape).astype(np.float32)
+    xt.copy_(torch.from_numpy(x2))
+    with torch.cuda.stream(s):
+        g.replay()
+    s.synchronize()
+    _close(out.cpu().numpy(), oracle.moe_eager(x2, ids, w, dense))
+    assert all(bool(torch.all(f == 7.0)) for f in fillers), "graph replay wrote into freed memory"
+    del g

@@ -145,17 +145,43 @@ def profile_read(max_phases: int = 8) -> list[float]:
 
 
 _ws_cache: dict[tuple, torch.Tensor] = {}
+# Every workspace ever handed out stays referenced for the life of the
+# process: a CUDA graph captured with one keeps its address, so freeing it
+# when a larger call replaces it would let the next replay write into memory
+# that other tensors own.  Growth is geometric, so what is retained is bounded
+# by about twice the largest workspace of each (device, stream).
+_ws_retired: list[torch.Tensor] = []
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """A cached, 256-byte aligned uint8 workspace of at least ``nbytes``.
+def workspace(device: torch.device, nbytes: int, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """A cached uint8 workspace of at least ``nbytes`` for ``stream`` (torch's
+    current stream of ``device`` when None).
 
-    Grown (never shrunk) per device; callers on one stream reuse it.
+    One workspace per (device, stream): calls on one stream run in order, so
+    they may share it; calls on different streams never do.  A workspace that
+    is too small is replaced by one at least twice as large, and the old one
+    is kept alive (see ``_ws_retired``), so graphs captured earlier stay
+    valid.  Sizes come from the library's ``*_workspace_size`` queries; call
+    each shape once outside capture (a warm-up) so capture finds the
+    workspace already large enough.
     """
-    key = (device.type, device.index)
+    if stream is None:
+        stream = torch.cuda.current_stream(device)
+    key = (device.type, device.index, int(stream.cuda_stream))
     buf = _ws_cache.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-        buf[:256].zero_()  # the device status word starts clean
+        size = max(int(nbytes), 1 << 20)
+        if buf is not None:
+            size = max(size, 2 * buf.numel())
+            _ws_retired.append(buf)
+        with torch.cuda.stream(stream):
+            buf = torch.empty(size, dtype=torch.uint8, device=device)
+            buf[:256].zero_()  # the device status word starts clean
         _ws_cache[key] = buf
     return buf
+
+
+def device_workspaces(device: torch.device) -> list[torch.Tensor]:
+    """Every workspace handed out on ``device`` (current and retained)."""
+    out = [b for k, b in _ws_cache.items() if k[0] == device.type and k[1] == device.index]
+    return out + [b for b in _ws_retired if b.device == device]

@@ -144,6 +144,17 @@ class NvlinkEpWindow:
     def set_peers(self, addrs: list[int]) -> None:
         self.peers = torch.tensor(addrs, dtype=torch.int64, device=self.device)
 
+    def status_tensor(self) -> torch.Tensor:
+        """The window's device status word as a one-element int32 tensor
+        (a view of the library-owned window, not a copy)."""
+        addr, dev = self.window + 4, self.device
+
+        class _View:
+            __cuda_array_interface__ = {"shape": (1,), "typestr": "<i4", "data": (addr, False), "version": 3}
+
+        with torch.cuda.device(dev):
+            return torch.as_tensor(_View(), device=dev)
+
     def status(self, clear: bool = True) -> int:
         """The window's device status word (4 = a peer wait timed out)."""
         v = _n.I32(0)
@@ -214,6 +225,13 @@ class Exl3ExpertParallel(torch.nn.Module):
         self.last_counts: tuple[list[int], list[int]] | None = None
         self.profile = False  # record CUDA events between the step's phases (benchmarks)
         self._events: list = []
+        # NVLink transport: the window's status word, copied to pinned host
+        # memory at the end of every step (asynchronously, so it also works
+        # inside a captured graph); a nonzero value means a bounded peer wait
+        # gave up in that step, whose output and every later step's are then
+        # invalid, so the next forward() raises
+        self._status_host: torch.Tensor | None = None
+        self._status_dev: torch.Tensor | None = None
 
     PHASES = ("dispatch", "counts", "exchange", "local", "return", "combine")
     # NVLink transport: dispatch stores rows into the owners' windows,
@@ -352,6 +370,20 @@ class Exl3ExpertParallel(torch.nn.Module):
         self._mark()
         return y
 
+    def _raise_on_status(self, status: int) -> None:
+        if status:
+            raise RuntimeError(
+                f"expert-parallel NVLink exchange failed on rank {self.rank}: device status {status} "
+                "(4 = a peer's rows or partial rows did not arrive within the wait budget); this step's "
+                "output and every later step's are invalid -- close this group and build a new one")
+
+    def check_status(self) -> None:
+        """Synchronise this rank's stream and raise if any step so far
+        recorded a failure in the window's status word (the word is kept, so
+        every later call raises too)."""
+        if self._win is not None:
+            self._raise_on_status(self._win.status(clear=False))
+
     def window(self, x_dtype: torch.dtype, topk: int, hidden: int) -> NvlinkEpWindow:
         """The NVLink window, created on first use (every rank must call it
         at the same point: the IPC handles are exchanged collectively)."""
@@ -361,6 +393,8 @@ class Exl3ExpertParallel(torch.nn.Module):
                                        self.combine_dtype, dev, group=self.group)
             self._pair_idx = torch.empty(self.capacity, self.world, dtype=torch.int32, device=dev)
             self._partial = torch.empty(self.world * self.capacity, hidden, dtype=self.combine_dtype, device=dev)
+            self._status_dev = self._win.status_tensor()
+            self._status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         return self._win
 
     def _forward_nvlink(self, x, ids, w, limit, n_valid, out):
@@ -370,6 +404,9 @@ class Exl3ExpertParallel(torch.nn.Module):
             raise ValueError(f"{T} tokens exceed the exchange capacity {C}")
         topk = ids.shape[1]
         win = self.window(x.dtype, topk, H)
+        # an earlier step (its status copy has landed by the time the host
+        # gets here again in all but the last few steps in flight) failed
+        self._raise_on_status(int(self._status_host[0]))
         lib = win.lib
         stream = _n.stream_of(x)
         if out is None:
@@ -394,6 +431,7 @@ class Exl3ExpertParallel(torch.nn.Module):
         _n.check(lib.exl3_ep_p2p_combine(win.window, G, self.rank, C, H, topk, xc, pc, self._pair_idx.data_ptr(),
                                          T, _n.ptr(n_valid), out.data_ptr(), _n.dtype_code(out), stream),
                  "exl3_ep_p2p_combine")
+        self._status_host.copy_(self._status_dev, non_blocking=True)
         self._mark()
         return out
 

@@ -220,15 +220,34 @@ class Exl3RoutedExperts(torch.nn.Module):
     forward = apply
 
 
-def layer_from_pack(pack, device, expert_map: torch.Tensor | None = None) -> Exl3RoutedExperts:
-    """Upload a :class:`exl3_b200.synthetic.MoEPack` and build its layer."""
+def upload_experts(experts, device) -> list[dict]:
+    """GPU projections of synthetic experts ({"gate", "up", "down"} dicts of
+    :class:`exl3_b200.synthetic.Projection`; "gate" may be None)."""
     inners = []
-    for e in pack.experts:
+    for e in experts:
         d = {}
         for which in ("gate", "up", "down"):
-            p = e[which]
-            d[which] = Exl3Projection(torch.from_numpy(p.trellis).to(device),
-                                      torch.from_numpy(p.suh).to(device),
-                                      torch.from_numpy(p.svh).to(device), p.codebook)
+            p = e.get(which)
+            d[which] = None if p is None else Exl3Projection(
+                torch.from_numpy(p.trellis).to(device), torch.from_numpy(p.suh).to(device),
+                torch.from_numpy(p.svh).to(device), p.codebook)
         inners.append(d)
-    return Exl3RoutedExperts(inners, pack.hidden, pack.inter, expert_map=expert_map)
+    return inners
+
+
+def layer_from_pack(pack, device, expert_map: torch.Tensor | None = None, act: int = _n.ACT_SILU
+                    ) -> Exl3RoutedExperts:
+    """Upload a :class:`exl3_b200.synthetic.MoEPack` and build its layer."""
+    return Exl3RoutedExperts(upload_experts(pack.experts, device), pack.hidden, pack.inter,
+                             expert_map=expert_map, act=act)
+
+
+def layer_from_slices(make_slice, n_experts: int, hidden: int, inter: int, device, chunk: int = 32,
+                      act: int = _n.ACT_SILU) -> Exl3RoutedExperts:
+    """A layer built ``chunk`` experts at a time from ``make_slice(lo, hi)``
+    (a :class:`exl3_b200.synthetic.MoEPack` of experts [lo, hi)), so the host
+    never holds every expert of a large layer at once."""
+    inners = []
+    for lo in range(0, n_experts, chunk):
+        inners += upload_experts(make_slice(lo, min(n_experts, lo + chunk)).experts, device)
+    return Exl3RoutedExperts(inners, hidden, inter, act=act)

@@ -454,14 +454,22 @@ def exl3_moe(x, out, gate_trellis_ptrs, gate_suh_ptrs, gate_svh_ptrs, up_trellis
 
 
 def device_status(workspace=None, clear=True) -> int:
-    """Device-side status word of the shared workspace (0 = clean)."""
+    """Device-side status word of a workspace (0 = clean).  Without one: the
+    first nonzero word among every workspace of the current device (all
+    streams; synchronises the device first)."""
     import ctypes
 
-    ws = workspace
-    if ws is None:
+    lib = _n.load()
+    if workspace is not None:
+        spaces = [workspace]
+    else:
         dev = torch.device("cuda", torch.cuda.current_device())
-        ws = _n.workspace(dev, 1 << 20)
-    v = ctypes.c_int(0)
-    _n.check(_n.load().exl3_device_status(ws.data_ptr(), int(bool(clear)), _n.stream_of(ws),
-                                          ctypes.byref(v)))
-    return int(v.value)
+        torch.cuda.synchronize(dev)
+        spaces = _n.device_workspaces(dev) or [_n.workspace(dev, 1 << 20)]
+    first = 0
+    for ws in spaces:
+        v = ctypes.c_int(0)
+        _n.check(lib.exl3_device_status(ws.data_ptr(), int(bool(clear)), _n.stream_of(ws), ctypes.byref(v)))
+        if v.value and not first:
+            first = int(v.value)
+    return first
