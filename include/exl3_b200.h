@@ -40,7 +40,9 @@ enum {
 
 enum { EXL3_DT_F32 = 0, EXL3_DT_F16 = 1, EXL3_DT_BF16 = 2, EXL3_DT_I32 = 3, EXL3_DT_I64 = 4 };
 enum { EXL3_CB_3INST = 0, EXL3_CB_MCG = 1, EXL3_CB_MUL1 = 2 };
-enum { EXL3_ACT_SILU = 0, EXL3_ACT_SWIGLU_OAI = 3 };
+/* MoE activations (src/vllm_exl3/exl3.py:143-154): SiLU-gated; non-gated relu^2
+ * (no gate projection: the gate tables are not read); clamped SwiGLU-OAI. */
+enum { EXL3_ACT_SILU = 0, EXL3_ACT_RELU2 = 2, EXL3_ACT_SWIGLU_OAI = 3 };
 
 int exl3_abi_version(void);
 const char* exl3_last_error(void);
@@ -88,7 +90,10 @@ int exl3_linear(const void* x, int x_dtype, int64_t m, const void* trellis, cons
  * that are negative, out of range or map outside [0, n_local) are skipped.
  * n_valid (int32[1] device, may be NULL) limits live tokens; rows at or past
  * it are written as zeros (p2b_fused_moe_padded).  swiglu_limit > 0 clamps
- * gate from above and up on both sides (p2b_moe.cu:755-768).  out [tokens][hidden]
+ * gate from above and up on both sides (p2b_moe.cu:755-768).  activation:
+ * EXL3_ACT_SILU silu(g) * u; EXL3_ACT_SWIGLU_OAI (u + 1) g sigmoid(1.702 g);
+ * EXL3_ACT_RELU2 relu(u)^2 for non-gated layers (exl3.py:2386-2391), whose
+ * gate tables may alias the up tables and are never read.  out [tokens][hidden]
  * in out_dtype.  `kmax` bounds every K in the tables (2..8). */
 size_t exl3_moe_workspace_size(int64_t tokens, int topk, int64_t hidden, int64_t intermediate,
                                int n_local, int kmax);

@@ -80,20 +80,34 @@ def expert_dense_fn(expert_of, blocks: list[int] | None = None):
     return get
 
 
-def check_moe(got_rows, x_rows, ids_rows, w_rows, expert_of, n_local: int, blocks: list[int] | None = None,
-              limit: float | None = None, act: str = "silu", expert_map=None) -> dict:
-    """Compare device output rows (fp32 [t, H], or [t, 128 * len(blocks)]
-    already restricted to `blocks`) with the eager loop on the same rows."""
-    want = oracle.moe_eager(np.asarray(x_rows), np.asarray(ids_rows), np.asarray(w_rows),
+def expected_moe(x_rows, ids_rows, w_rows, expert_of, n_local: int, blocks: list[int] | None = None,
+                 limit: float | None = None, act: str = "silu", expert_map=None) -> np.ndarray:
+    """The eager loop's fp32 output on these rows (the listed column blocks,
+    concatenated, when `blocks` is given)."""
+    return oracle.moe_eager(np.asarray(x_rows), np.asarray(ids_rows), np.asarray(w_rows),
                             expert_dense_fn(expert_of, blocks), expert_map=expert_map, limit=limit, act=act,
                             n_local=n_local)
+
+
+def compare(got_rows, want: np.ndarray, blocks: list[int] | None = None) -> dict:
+    """Statistics and verdict of device rows (full width, or already the
+    listed blocks) against :func:`expected_moe`'s result."""
     got = np.asarray(got_rows, np.float32)
     if blocks is not None and got.shape[1] != want.shape[1]:
         got = np.concatenate([got[:, 128 * b:128 * (b + 1)] for b in blocks], axis=1)
     st = stats(got, want)
+    st["pass"] = passes(st)
+    return st
+
+
+def check_moe(got_rows, x_rows, ids_rows, w_rows, expert_of, n_local: int, blocks: list[int] | None = None,
+              limit: float | None = None, act: str = "silu", expert_map=None) -> dict:
+    """Compare device output rows (fp32 [t, H], or [t, 128 * len(blocks)]
+    already restricted to `blocks`) with the eager loop on the same rows."""
+    want = expected_moe(x_rows, ids_rows, w_rows, expert_of, n_local, blocks, limit, act, expert_map)
+    st = compare(got_rows, want, blocks)
     st["tokens"] = int(np.asarray(x_rows).shape[0])
     st["col_blocks"] = None if blocks is None else len(blocks)
-    st["pass"] = passes(st)
     return st
 
 

@@ -74,9 +74,9 @@ def _dequant(trellis, suh, svh, K: int, cb: int):
     import torch
     kind, mod = ref_module()
     if kind == "reference":
-        return mod.dequant_trellis(torch.from_numpy(np.ascontiguousarray(trellis)),
-                                   torch.from_numpy(np.ascontiguousarray(suh)),
-                                   torch.from_numpy(np.ascontiguousarray(svh)), int(K), cb == 1)
+        # np.array copies the memory-mapped (read-only) arrays into writable ones
+        return mod.dequant_trellis(torch.from_numpy(np.array(trellis)), torch.from_numpy(np.array(suh)),
+                                   torch.from_numpy(np.array(svh)), int(K), cb == 1)
     return torch.from_numpy(mod.dequant(trellis, suh, svh, int(K), cb=cb))
 
 

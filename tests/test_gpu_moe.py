@@ -34,7 +34,8 @@ def _close(actual, expected):
 
 
 def _dense(pack):
-    return [{w: oracle.dequant(e[w].trellis, e[w].suh, e[w].svh, e[w].K, cb=e[w].codebook)
+    return [{w: None if e.get(w) is None else oracle.dequant(e[w].trellis, e[w].suh, e[w].svh, e[w].K,
+                                                             cb=e[w].codebook)
              for w in ("gate", "up", "down")} for e in pack.experts]
 
 
@@ -342,3 +343,55 @@ def test_graph_survives_workspace_growth(native, cuda):
     _close(out.cpu().numpy(), oracle.moe_eager(x2, ids, w, dense))
     assert all(bool(torch.all(f == 7.0)) for f in fillers), "graph replay wrote into freed memory"
     del g
+
+
+@pytest.mark.parametrize("tokens", [6, 160])
+@pytest.mark.parametrize("limit", [None, 0.75])
+def test_swiglu_oai_activation(native, cuda, tokens, limit):
+    """Clamped SwiGLU-OAI (exl3.py:2392-2402: (up + 1) * gate * sigmoid(1.702
+    gate), gate clamped from above, up on both sides) on the decode GEMV
+    (6 tokens) and the tcgen05 GEMM path (160 tokens: >= 32 rows per expert)."""
+    import torch
+    from exl3_b200 import _native, moe, synthetic
+    pack, x, ids, w = synthetic.make_config("cfg2", seed=300 + tokens, tokens=tokens, n_experts=8, topk=2,
+                                            hidden=512, inter=256, k_choices=(2, 3, 4), k_probs=None)
+    layer = moe.layer_from_pack(pack, cuda, act=_native.ACT_SWIGLU_OAI)
+    want = oracle.moe_eager(x, ids, w, _dense(pack), limit=limit, act="swiglu_oai")
+    _close(_run(layer, cuda, x, ids, w, dtype=torch.float32, limit=limit), want)
+
+
+@pytest.mark.parametrize("tokens", [6, 160])
+@pytest.mark.parametrize("cb", [1, 2])
+def test_gateless_relu2_layer(native, cuda, tokens, cb):
+    """Non-gated relu^2 layer (exl3.py:2386-2391, NemotronH): experts carry no
+    gate projection, the fused state aliases the up tables into the gate
+    slots, and both paths compute relu(clamp(up))^2 without a gate GEMM."""
+    import torch
+    from exl3_b200 import _native, moe, synthetic
+    pack, x, ids, w = synthetic.make_config("cfg2", seed=400 + tokens + cb, tokens=tokens, n_experts=8, topk=2,
+                                            hidden=512, inter=384, codebook=cb, k_choices=(2, 3, 4),
+                                            k_probs=None, gateless=True)
+    layer = moe.layer_from_pack(pack, cuda)
+    assert layer._exl3_gateless and layer._exl3_moe_act == _native.ACT_RELU2
+    assert torch.equal(layer._exl3_ptrs["gate_trellis"], layer._exl3_ptrs["up_trellis"])
+    dense = _dense(pack)
+    for limit in (None, 0.5):
+        want = oracle.moe_eager(x, ids, w, dense, limit=limit)
+        _close(_run(layer, cuda, x, ids, w, dtype=torch.float32, limit=limit), want)
+
+
+@pytest.mark.parametrize("gateless", [False, True])
+def test_layer_loaded_from_safetensors(native, cuda, tmp_path, gateless):
+    """A layer built by the safetensors loader (per-expert keys, markers,
+    mixed K per expert) runs on the GPU and matches the eager loop."""
+    import torch
+    from exl3_b200 import loader, synthetic
+    pack, x, ids, w = synthetic.make_config("cfg2", seed=500 + gateless, tokens=12, n_experts=8, topk=2,
+                                            hidden=512, inter=256, k_choices=(2, 3, 4), k_probs=None,
+                                            gateless=gateless)
+    path = str(tmp_path / "pack.safetensors")
+    loader.save_routed_experts(path, "model.layers.0.mlp", pack.experts)
+    layer = loader.load_routed_experts(path, "model.layers.0.mlp", 8, 512, 256, cuda)
+    assert layer._exl3_gateless == gateless
+    want = oracle.moe_eager(x, ids, w, _dense(pack))
+    _close(_run(layer, cuda, x, ids, w, dtype=torch.float32), want)

@@ -184,7 +184,7 @@ int exl3_moe_forward(const void* x, int x_dtype, int64_t tokens, int64_t hidden,
         return fail(EXL3_ERR_ARG,
                     "%s SwiGLU limit must be finite and nonnegative (0 disables clipping)", who);
     if (cb < 0 || cb > 2) return fail(EXL3_ERR_ARG, "%s: codebook must be 0, 1 or 2", who);
-    if (act != EXL3_ACT_SILU && act != EXL3_ACT_SWIGLU_OAI)
+    if (act != EXL3_ACT_SILU && act != EXL3_ACT_SWIGLU_OAI && act != EXL3_ACT_RELU2)
         return fail(EXL3_ERR_ARG, "%s: unsupported activation %d", who, act);
     if (kmax < 2 || kmax > 8) return fail(EXL3_ERR_ARG, "%s: kmax must be in 2..8", who);
     const bool tables = kg || ku || kd;

@@ -42,7 +42,7 @@
 namespace exl3 {
 
 enum Epi : int { EPI_GATEUP = 0, EPI_DOWN = 1, EPI_LINEAR = 2, EPI_ROUTE = 3 };
-enum Act : int { ACT_SILU = 0, ACT_SWIGLU_OAI = 3 };
+enum Act : int { ACT_SILU = 0, ACT_RELU2 = 2, ACT_SWIGLU_OAI = 3 };
 
 constexpr int kPrepThreads = 1024;
 constexpr int kMaxLocal = 2048;
@@ -994,10 +994,12 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
         named_bar_sync(1, NCT);
 
         if constexpr (EPI == EPI_GATEUP) {
+            // NPROJ == 2: gate (row block 0) and up (block 1); NPROJ == 1: the
+            // up projection alone (non-gated relu^2)
             const __half* dsuh = proj_suh(a.down, I.e);
             for (int r = cw; r < I.rows; r += kCW) {
                 const float* gr = sm.ys + r * kYsPitch;
-                const float* ur = sm.ys + (16 + r) * kYsPitch;
+                const float* ur = sm.ys + ((NPROJ - 1) * 16 + r) * kYsPitch;
                 float x[4];
                 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -1008,8 +1010,14 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                         u = fminf(fmaxf(u, -a.limit), a.limit);
                     }
                     float act;
-                    if (a.act == ACT_SWIGLU_OAI) act = (u + 1.0f) * g / (1.0f + expf(-1.702f * g));
-                    else act = silu_f(g) * u;
+                    if (NPROJ == 1) {
+                        const float rl = fmaxf(u, 0.f);
+                        act = rl * rl;
+                    } else if (a.act == ACT_SWIGLU_OAI) {
+                        act = (u + 1.0f) * g / (1.0f + expf(-1.702f * g));
+                    } else {
+                        act = silu_f(g) * u;
+                    }
                     const float h = __half2float(__float2half_rn(act));  // the reference's act.half()
                     x[i] = h * (dsuh ? __half2float(dsuh[I.cb * 128 + c]) : 0.f);
                 }
@@ -1332,8 +1340,10 @@ static cudaError_t run_moe_gemm(const MoePlan& p, const MoeCall& c, const WsPtrs
     t.yrows = w.g;
     t.max_split = p.tc_split1;
     const int mt = p.tile_m / 128;
-    if ((e = run_tc_gemm(c.cb, mt, t, w.xr, p.rpad, tc_grid(p.t128max * t.ncb, t.max_split, t.ctas), p.tc_smem, s)) !=
-        cudaSuccess)
+    const bool gateless = c.act == ACT_RELU2;  // no gate projection: its launch is skipped
+    if (!gateless &&
+        (e = run_tc_gemm(c.cb, mt, t, w.xr, p.rpad, tc_grid(p.t128max * t.ncb, t.max_split, t.ctas), p.tc_smem,
+                         s)) != cudaSuccess)
         return e;
     // up, fused with SwiGLU and the down input rotation (reads the gate rows)
     t.proj = c.up;
@@ -1343,7 +1353,7 @@ static cudaError_t run_moe_gemm(const MoePlan& p, const MoeCall& c, const WsPtrs
     t.down = c.down;
     t.limit = c.limit;
     t.act = c.act;
-    if ((e = run_tc_gemm(c.cb, mt, t, w.xr + size_t(p.rpad) * p.hidden, p.rpad,
+    if ((e = run_tc_gemm(c.cb, mt, t, gateless ? w.xr : w.xr + size_t(p.rpad) * p.hidden, p.rpad,
                          tc_grid(p.t128max * t.ncb, t.max_split, t.ctas), p.tc_smem, s)) != cudaSuccess)
         return e;
     prof_mark(s);
@@ -1408,12 +1418,14 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     if (e != cudaSuccess) return e;
     prof_mark(s);
 
+    // non-gated relu^2: only the up projection exists (the gate tables are not read)
+    const bool gateless = !p.linear && c.act == ACT_RELU2;
     RotArgs ra;
     ra.x = c.x;
     ra.x_dtype = c.x_dtype;
     ra.in_f = p.hidden;
-    ra.nproj = p.linear ? 1 : 2;
-    ra.proj[0] = p.linear ? c.up : c.gate;
+    ra.nproj = (p.linear || gateless) ? 1 : 2;
+    ra.proj[0] = (p.linear || gateless) ? c.up : c.gate;
     ra.proj[1] = c.up;
     ra.nslots = w.nslots;
     ra.slots = w.slots;
@@ -1466,7 +1478,7 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
         return e;
     }
 
-    g.proj[0] = c.gate;
+    g.proj[0] = gateless ? c.up : c.gate;
     g.proj[1] = c.up;
     g.in_f = p.hidden;
     g.out_f = p.inter;
@@ -1482,7 +1494,9 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     g.part = w.part1;
     g.cnt = w.cnt1;
     g.sched = w.sched;
-    if ((e = launch_gemv<2, EPI_GATEUP>(c.cb, g, p.grid1, p.smem1, s)) != cudaSuccess) return e;
+    e = gateless ? launch_gemv<1, EPI_GATEUP>(c.cb, g, p.grid1, p.smem1, s)
+                 : launch_gemv<2, EPI_GATEUP>(c.cb, g, p.grid1, p.smem1, s);
+    if (e != cudaSuccess) return e;
     prof_mark(s);
 
     GemvArgs d = g;

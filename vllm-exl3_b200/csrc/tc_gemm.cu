@@ -400,6 +400,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
             // in flight ahead of the one being processed (latency hiding)
             float gq[2][4];
             float su[4] = {0.f, 0.f, 0.f, 0.f};
+            const bool use_gate = a.epi == TC_EPI_UPACT && a.act != 2;  // act 2: non-gated relu^2
             if (a.epi == TC_EPI_UPACT) {
                 const __half* sup = proj_suh(a.down, e);  // every row of the tile is expert e
                 #pragma unroll
@@ -409,7 +410,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                     const int rr = d + 8 * j;
                     const float* gr = a.g_rows + (p0 + 128 * h + rr) * int64_t(a.out_f) + cb * 128;
                     #pragma unroll
-                    for (int i = 0; i < 4; ++i) gq[j][i] = rr < rows_h ? gr[lane + 32 * i] : 0.f;
+                    for (int i = 0; i < 4; ++i) gq[j][i] = (use_gate && rr < rows_h) ? gr[lane + 32 * i] : 0.f;
                 }
             }
             for (int r = d; r < rows_h; r += 8) {
@@ -446,7 +447,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                         gv[i] = gq[0][i];
                         gq[0][i] = gq[1][i];
                     }
-                    if (r + 16 < rows_h) {
+                    if (use_gate && r + 16 < rows_h) {
                         const float* gr = a.g_rows + (p + 16) * a.out_f + cb * 128;
                         #pragma unroll
                         for (int i = 0; i < 4; ++i) gq[1][i] = gr[lane + 32 * i];
@@ -458,8 +459,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                             g = fminf(g, a.limit);
                             u = fminf(fmaxf(u, -a.limit), a.limit);
                         }
-                        const float act = a.act == 3 ? (u + 1.0f) * g / (1.0f + expf(-1.702f * g))
-                                                     : g / (1.0f + expf(-g)) * u;
+                        float act;
+                        if (a.act == 2) {
+                            const float rl = fmaxf(u, 0.f);
+                            act = rl * rl;
+                        } else if (a.act == 3) {
+                            act = (u + 1.0f) * g / (1.0f + expf(-1.702f * g));
+                        } else {
+                            act = g / (1.0f + expf(-g)) * u;
+                        }
                         x[i] = __half2float(__float2half_rn(act)) * su[i];
                     }
                     fwht128_warp(x, lane);

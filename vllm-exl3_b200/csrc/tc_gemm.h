@@ -35,7 +35,7 @@ struct TcArgs {
     __half* x2;           // [rows][out_f] fp16 down input
     ProjRef down;         // suh of the down projection
     float limit;          // SwiGLU clamp (0 = off)
-    int act;              // 0 SiLU, 3 SwiGLU-OAI
+    int act;              // 0 SiLU, 2 non-gated relu^2 (no gate rows), 3 SwiGLU-OAI
     // split-K: with max_split > 1 the kernel splits each (tile, column block)
     // over 1..max_split CTAs, chosen from the device-side tile count so the
     // CTAs fill `ctas` slots; each split writes fp32 partials to `part`

@@ -21,7 +21,7 @@ _lib = None
 EXL3_OK, EXL3_ERR_ARG, EXL3_ERR_CUDA, EXL3_ERR_WORKSPACE = 0, 1, 2, 3
 DT_F32, DT_F16, DT_BF16, DT_I32, DT_I64 = 0, 1, 2, 3, 4
 CB_3INST, CB_MCG, CB_MUL1 = 0, 1, 2
-ACT_SILU, ACT_SWIGLU_OAI = 0, 3
+ACT_SILU, ACT_RELU2, ACT_SWIGLU_OAI = 0, 2, 3
 
 _DTYPE_CODE = {
     torch.float32: DT_F32,

@@ -85,14 +85,20 @@ class Exl3Projection:
 
 
 def build_exl3_fused_state(layer, inners: list[dict]) -> None:
-    """Pointer tables + per-expert K tables, once after load (no per-token alloc)."""
+    """Pointer tables + per-expert K tables, once after load (no per-token alloc).
+
+    Gateless layers (every expert's "gate" is None: non-gated relu^2,
+    exl3.py:2455-2491) alias the up tables into the gate slots, as the
+    reference does, and select the relu^2 activation; the kernels never read
+    the gate tables then."""
     if not inners:
         raise ValueError("EXL3 experts were not built after weight load")
     device = inners[0]["up"].trellis.device
     gateless = all(pack.get("gate") is None for pack in inners)
-    if gateless:
-        raise ValueError("gateless (relu^2) EXL3 layers are not supported by the B200 path yet")
-    cbs = {pack[p].codebook for pack in inners for p in ("gate", "up", "down")}
+    if not gateless and any(pack.get("gate") is None for pack in inners):
+        raise ValueError("EXL3 gateless layer must not carry gate projections")
+    projs = ("up", "down") if gateless else ("gate", "up", "down")
+    cbs = {pack[p].codebook for pack in inners for p in projs}
     if len(cbs) != 1:
         raise ValueError("EXL3 layer mixes codebooks across experts")
 
@@ -100,8 +106,9 @@ def build_exl3_fused_state(layer, inners: list[dict]) -> None:
         return torch.tensor([int(getattr(pack[which], attr).data_ptr()) for pack in inners],
                             dtype=torch.int64, device=device)
 
+    src = {"gate": "up" if gateless else "gate", "up": "up", "down": "down"}
     layer._exl3_ptrs = {
-        f"{p}_{a}": _ptrs(p, a) for p in ("gate", "up", "down") for a in ("trellis", "suh", "svh")
+        f"{p}_{a}": _ptrs(src[p], a) for p in ("gate", "up", "down") for a in ("trellis", "suh", "svh")
     }
     layer._exl3_ptrs.update({
         f"{p}_{'t' if a == 'trellis' else a}_ptrs": layer._exl3_ptrs[f"{p}_{a}"]
@@ -109,11 +116,11 @@ def build_exl3_fused_state(layer, inners: list[dict]) -> None:
     })
 
     def _k(which: str) -> torch.Tensor:
-        return torch.tensor([int(pack[which].trellis.shape[-1]) // 16 for pack in inners],
+        return torch.tensor([int(pack[src[which]].trellis.shape[-1]) // 16 for pack in inners],
                             dtype=torch.int8, device=device)
 
     kg, ku, kd = _k("gate"), _k("up"), _k("down")
-    ks = {int(pack[p].K) for pack in inners for p in ("gate", "up", "down")}
+    ks = {int(pack[p].K) for pack in inners for p in projs}
     if min(ks) < 2 or max(ks) > 8:
         raise ValueError(f"EXL3 K outside 2..8: {sorted(ks)}")
     layer._exl3_k_tables = (kg, ku, kd)
@@ -121,7 +128,11 @@ def build_exl3_fused_state(layer, inners: list[dict]) -> None:
     layer._exl3_mixed_k = len(ks) > 1
     layer._exl3_k = None if layer._exl3_mixed_k else next(iter(ks))
     layer._exl3_codebook = next(iter(cbs))
-    layer._exl3_gateless = False
+    layer._exl3_gateless = gateless
+    if gateless:
+        layer._exl3_moe_act = _n.ACT_RELU2
+    elif getattr(layer, "_exl3_moe_act", _n.ACT_SILU) == _n.ACT_RELU2:
+        raise ValueError("EXL3 relu^2 (non-gated) activation on a layer with gate projections")
 
 
 def apply_exl3_experts(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, layer,

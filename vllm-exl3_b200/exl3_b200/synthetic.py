@@ -58,6 +58,10 @@ class MoEPack:
     def k_table(self, which: str) -> np.ndarray:
         return np.array([e[which].K for e in self.experts], dtype=np.int8)
 
+    @property
+    def gateless(self) -> bool:
+        return bool(self.experts) and all(e.get("gate") is None for e in self.experts)
+
 
 def make_projection(rng: np.random.Generator, in_f: int, out_f: int, K: int, codebook: int,
                     scale: bool = True) -> Projection:
@@ -71,14 +75,16 @@ def make_projection(rng: np.random.Generator, in_f: int, out_f: int, K: int, cod
 
 
 def make_moe_pack(seed: int, n_experts: int, hidden: int, inter: int, codebook: int,
-                  k_choices=(4,), k_probs=None) -> MoEPack:
+                  k_choices=(4,), k_probs=None, gateless: bool = False) -> MoEPack:
+    """Experts drawn from one generator in order; ``gateless`` packs have no
+    gate projection (non-gated relu^2 layers)."""
     rng = np.random.default_rng(seed)
     ks = rng.choice(np.asarray(k_choices), size=n_experts, p=k_probs)
     pack = MoEPack(hidden, inter, codebook)
     for e in range(n_experts):
         K = int(ks[e])
         pack.experts.append({
-            "gate": make_projection(rng, hidden, inter, K, codebook),
+            "gate": None if gateless else make_projection(rng, hidden, inter, K, codebook),
             "up": make_projection(rng, hidden, inter, K, codebook),
             "down": make_projection(rng, inter, hidden, K, codebook),
         })
@@ -160,7 +166,7 @@ def make_config(name: str, seed: int = 0, tokens: int | None = None, **over):
     c.update(over)
     T = int(tokens if tokens is not None else c["tokens"])
     pack = make_moe_pack(seed, c["n_experts"], c["hidden"], c["inter"], c["codebook"],
-                         c["k_choices"], c.get("k_probs"))
+                         c["k_choices"], c.get("k_probs"), c.get("gateless", False))
     rng = np.random.default_rng(seed + 1_000_003)
     x = activations(rng, T, c["hidden"])
     if c["routing"] == "sigmoid_zipf":
