@@ -13,6 +13,8 @@ one batch; 8 different routings/batches rotate across steps.
 The same line carries, as sub-objects measured in the same run:
 * `prefill`: configs[2] (160 experts, H5120 I1536, K2/3 mul1, T=2048), the
   tcgen05 grouped-GEMM path, one GPU;
+* `dense`: configs[3] (8192x28672 then 28672x8192, K3 MCG, M = 1, 16, 256,
+  4096 rows) through the dense layer API, one GPU;
 * `ep_cfg4`: configs[4] (256 experts top-8 sigmoid+Zipf, H7168 I2048,
   K2/3/4 MCG, 8192 tokens split over the N ranks: strong scaling), the
   expert-parallel step with per-phase in-graph times and the per-rank
@@ -86,6 +88,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the configs[2] prefill sub-object")
     ap.add_argument("--no-ep-cfg4", action="store_true", help="skip the configs[4] expert-parallel sub-object")
+    ap.add_argument("--no-dense", action="store_true", help="skip the configs[3] dense-linear sub-object")
     ap.add_argument("--no-parity", action="store_true", help="skip the output checks against the oracle")
     ap.add_argument("--no-graph", action="store_true", help="time the expert-parallel step eagerly")
     ap.add_argument("--ep-transport", default="nvlink", choices=["nvlink", "nccl"],
@@ -561,6 +564,98 @@ def run_prefill(args, local_rank, steps, warmup, tokens=None):
 
 
 # ---------------------------------------------------------------------------
+# dense EXL3 linear, MLP-sized, one GPU
+# ---------------------------------------------------------------------------
+DENSE = dict(n=8192, f=28672, K=3, ms=(1, 16, 256, 4096),
+             name="configs[3] dense EXL3 linear: 8192x28672 then 28672x8192, K3 MCG")
+
+
+def run_dense(args, local_rank, steps, warmup):
+    """The two projections of an MLP (x W1 then y W2) through the dense layer
+    API (exl3_b200.linear.Exl3Linear) at each row count; per row count a step
+    is both projections, bf16 in and out."""
+    import numpy as np
+    import torch
+    from exl3_b200 import linear as lin
+    from exl3_b200 import synthetic
+
+    c = DENSE
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    rng = np.random.default_rng(4)
+    p1 = synthetic.make_projection(rng, c["n"], c["f"], c["K"], synthetic.CB_MCG)
+    p2 = synthetic.make_projection(rng, c["f"], c["n"], c["K"], synthetic.CB_MCG)
+    l1 = lin.linear_from_projections([p1], dev)
+    l2 = lin.linear_from_projections([p2], dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    hbm, tpk, kind = peaks()
+    wbytes = 2 * (c["n"] // 16) * (c["f"] // 16) * 32 * c["K"] + 2 * (c["n"] + c["f"]) * 2
+    out = {"workload": c["name"], "peak_kind": kind}
+    for M in c["ms"]:
+        x = torch.from_numpy(np.random.default_rng(10 + M).normal(0, 1, (M, c["n"])).astype(np.float32)).to(dev)
+        x = x.to(torch.bfloat16)
+        ys = {}
+
+        def step():
+            ys["y"] = l2(l1(x))
+
+        g = _capture(step, dev)
+        with ClockSampler(local_rank) as clk:
+            evs = _timed_replays(g, warmup + steps, flush, lambda i: None)[warmup:]
+            torch.cuda.synchronize(dev)
+        us = statistics.median(a.elapsed_time(b) for a, b in evs) * 1e3
+        # each projection timed alone (eager, events on the launching stream)
+        t1, t2 = [], []
+        for _ in range(5):
+            flush.zero_()
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record()
+            y1 = l1(x)
+            e1.record()
+            l2(y1)
+            e2.record()
+            torch.cuda.synchronize(dev)
+            t1.append(e0.elapsed_time(e1) * 1e3)
+            t2.append(e1.elapsed_time(e2) * 1e3)
+        u1, u2 = statistics.median(t1[1:]), statistics.median(t2[1:])
+        act_bytes = 2 * M * (c["n"] + c["f"]) * 2  # bf16 in and out of both projections
+        flops = 2.0 * M * c["n"] * c["f"] * 2
+        if M <= 16:
+            ach = (wbytes + act_bytes) / (us / 1e6) / 1e9
+            roof = {"bound": "hbm", "unit": "GB/s", "achieved": ach, "peak": hbm, "frac": ach / hbm,
+                    "bytes_per_step": wbytes + act_bytes}
+        else:
+            ach = flops / (us / 1e6) / 1e12
+            roof = {"bound": "tensor", "unit": "TFLOP/s", "achieved": ach, "peak": tpk, "frac": ach / tpk,
+                    "flops_per_step": flops}
+        r = {"us_per_step": us, "us_w1": u1, "us_w2": u2, "roofline": roof, "clocks": clk.summary()}
+        if not args.no_parity:
+            import parity
+            rows = parity.sample_tokens(M, 8, seed=M)
+            idx = torch.from_numpy(rows).to(dev)
+            xh = x.float().cpu().numpy()[rows].astype(np.float16).astype(np.float32)
+            y1f = l1._exl3_linears[0]
+            import vllm_exl3_c
+            f1 = vllm_exl3_c.exl3_linear(x, y1f.trellis, y1f.suh, y1f.svh, y1f.K, 1, out_dtype=torch.float32)
+            b1 = parity.col_blocks(c["f"], 4, seed=M)
+            st1 = parity.compare(f1[idx].cpu().numpy(), xh @ parity.projection_dense(p1, b1).astype(np.float32), b1)
+            y1 = l1(x)
+            y2f = l2._exl3_linears[0]
+            f2 = vllm_exl3_c.exl3_linear(y1, y2f.trellis, y2f.suh, y2f.svh, y2f.K, 1, out_dtype=torch.float32)
+            x2 = y1.float().cpu().numpy()[rows].astype(np.float16).astype(np.float32)
+            b2 = parity.col_blocks(c["n"], 4, seed=M + 1)
+            st2 = parity.compare(f2[idx].cpu().numpy(), x2 @ parity.projection_dense(p2, b2).astype(np.float32), b2)
+            r["parity"] = {"w1": st1, "w2": st2, "pass": st1["pass"] and st2["pass"],
+                           "note": f"fp32 rows of each projection vs the oracle's dequant matmul, {len(rows)} "
+                                   "sampled rows x 4 128-column blocks"}
+        out[f"M={M}"] = r
+        del g
+    del l1, l2
+    torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------------------
 # expert-parallel workloads
 # ---------------------------------------------------------------------------
 EP_WORKLOADS = {
@@ -905,6 +1000,8 @@ def main():
         sub_steps, sub_warm = max(3, min(args.steps, 20)), max(3, min(args.warmup, 5))
         if world == 1 and not args.no_prefill:
             res["prefill"] = run_prefill(args, local_rank, sub_steps, sub_warm)
+        if world == 1 and not args.no_dense:
+            res["dense"] = run_dense(args, local_rank, sub_steps, sub_warm)
         if not args.no_ep_cfg4:
             res["ep_cfg4"] = run_ep(args, rank, local_rank, world, "ep", sub_steps, sub_warm)
     if cpu is not None:

@@ -153,6 +153,25 @@ int exl3_linear_noalloc(const void* x, int x_dtype, int64_t m, const void* trell
                         const void* svh, int64_t in_features, int64_t out_features, int K,
                         int codebook, void* y, int y_dtype, void* stream);
 
+/* Row-wise EXL3 embedding tables in the n-gram format (replaces ExLlamaV3's
+ * ngram_dequant, call site src/vllm_exl3/exl3.py:5536-5544, restated by the
+ * reference as ngram_dequant_rows_torch, exl3.py:5213-5239).  A row of `bits`
+ * (1..8) is 1 + 10 * bits int16 words: an fp16 scale, then a ring bitstream of
+ * 160 states; out[r][i] = fp16(mul1(state_i) * scale + head_bias[head][i]),
+ * written in out_dtype.  exl3_ngram_dequant decodes `n` packed rows with a
+ * head index each (int32 [n], clamped to [0, num_heads)).  exl3_ngram_lookup
+ * is the whole lookup of Exl3EmbeddingMethod._embedding_impl (exl3.py:
+ * 5576-5587) in one launch: row ids [n] (int32/int64) gathered from a table
+ * of n_rows rows, each id's head = (number of head_offsets <= id) - 1
+ * clamped (searchsorted, right), then decoded; ids outside the table give
+ * zero rows and record status 7 in `status` (an int32 device word, may be
+ * NULL).  head_bias fp16 [num_heads][160]. */
+int exl3_ngram_dequant(const void* packed, int64_t n, int bits, const int32_t* heads, const void* head_bias,
+                       int num_heads, void* out, int out_dtype, void* stream);
+int exl3_ngram_lookup(const void* table, int64_t n_rows, int bits, const void* ids, int ids_dtype, int64_t n,
+                      const int64_t* head_offsets, int num_heads, const void* head_bias, void* out, int out_dtype,
+                      int* status, void* stream);
+
 /* Expert-parallel dispatch, source side (no counterpart in the reference,
  * which leaves the exchange to vLLM's all-to-all backends and consumes only
  * the resulting expert_map, src/vllm_exl3/exl3.py:2310-2354).  Rank g of

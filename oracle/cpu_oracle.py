@@ -223,3 +223,32 @@ def moe_eager(x: np.ndarray, ids: np.ndarray, weights: np.ndarray, dense,
     if out is None:
         out = np.zeros((T, H), dtype=np.float32)
     return out
+
+
+NGRAM_ROW_DIM = 160
+
+
+def ngram_dequant(packed: np.ndarray, bits: int, heads: np.ndarray, head_bias: np.ndarray) -> np.ndarray:
+    """Row-wise EXL3 embedding decode (``ngram_dequant_rows_torch``,
+    ``exl3.py:5213-5239``; ring layout ``_ngram_bit_tables`` :5198-5208;
+    codebook ``ngram_mul1_codebook`` :5186-5195).  packed int16 [N, 1 + 10K];
+    element i's state takes bit m from stream bit ((i - m // K) mod 160) * K +
+    m % K (LSB-first words after the scale word); value =
+    fp16(codebook[state] * scale + head_bias[head]) in fp32 arithmetic."""
+    K = int(bits)
+    p = np.asarray(packed, dtype=np.int16)
+    words = p.astype(np.int64) & 0xFFFF
+    i = np.arange(NGRAM_ROW_DIM)[:, None]
+    m = np.arange(16)[None, :]
+    sb = ((i - m // K) % NGRAM_ROW_DIM) * K + m % K
+    widx, bidx = 1 + (sb >> 4), sb & 15
+    state = (((words[:, widx] >> bidx) & 1) << m).sum(-1)               # [N, 160]
+    prod = (np.arange(65536, dtype=np.int64) * 0x83DCD12D) & 0xFFFFFFFF
+    h = (1024 + (prod & 0xFF) + ((prod >> 8) & 0xFF) + ((prod >> 16) & 0xFF) + (prod >> 24)).astype(np.float32)
+    kinv = np.float32(np.array([0x1EEE], np.uint16).view(np.float16)[0])
+    kbias = np.float32(np.array([0xC931], np.uint16).view(np.float16)[0])
+    codebook = ((h * kinv).astype(np.float32) + kbias).astype(np.float16)
+    scale = p[:, 0].view(np.float16).astype(np.float32)
+    vals = codebook[state].astype(np.float32)
+    bias = np.asarray(head_bias, np.float16)[np.asarray(heads, np.int64)].astype(np.float32)
+    return ((vals * scale[:, None]).astype(np.float32) + bias).astype(np.float16)

@@ -18,7 +18,9 @@ Every expected value comes from reference code, never from this repository:
   (src/vllm_exl3/exl3.py:2357-2413) with projections realised as
   ``x.float() @ dequant_trellis(...).float()`` (the CPU branch of exl3_gemv,
   csrc/bindings.cpp:144-146), on small seeded layers: uniform-K MCG,
-  mixed-K mul1 with a SwiGLU limit, and an expert_map with non-local routes.
+  mixed-K mul1 with a SwiGLU limit, and an expert_map with non-local routes;
+* ``ngram.npz`` -- the reference's n-gram row decode ngram_dequant_rows_torch
+  (src/vllm_exl3/exl3.py:5213-5239) for K in 1..8.
 """
 
 from __future__ import annotations
@@ -40,6 +42,8 @@ def main() -> None:
     # the reference checkout: EXL3_REFERENCE_ROOT, else a sibling of this repository
     ref_root = os.environ.get("EXL3_REFERENCE_ROOT", os.path.join(os.path.dirname(ROOT), "reference"))
     ap.add_argument("--ref-src", default=os.path.join(ref_root, "src"))
+    ap.add_argument("--only", choices=["all", "ngram"], default="all",
+                    help="ngram: write only ngram.npz (the other fixtures stay as they are)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref_src)
     sys.path.insert(0, os.path.join(ROOT, "oracle", "_ref"))
@@ -49,6 +53,9 @@ def main() -> None:
     from vllm_exl3 import exl3 as ref_exl3
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    if args.only == "ngram":
+        make_ngram(ref_exl3)
+        return
 
     # ---- half conversion and codebook KATs
     values = [2.0**-15, 1.00075, -1.00075, 2.0**-24, 2.0**-25, 1.0 + 2.0**-11, 1.0 + 3 * 2.0**-11,
@@ -150,7 +157,34 @@ def main() -> None:
     np.savez_compressed(os.path.join(HERE, "moe.npz"), **moe)
     with open(os.path.join(HERE, "moe_cases.json"), "w") as f:
         json.dump(meta, f, indent=1)
+    make_ngram(ref_exl3)
     print("golden fixtures written to", HERE)
+
+
+def make_ngram(ref_exl3) -> None:
+    """``ngram.npz``: the reference's own n-gram row decode,
+    ``ngram_dequant_rows_torch`` (src/vllm_exl3/exl3.py:5213-5239), on seeded
+    packed rows for every K in 1..8 with edge scale words and 3 heads."""
+    import torch
+    rng = np.random.default_rng(20261202)
+    out = {}
+    for K in range(1, 9):
+        n = 12
+        words = ref_exl3.ngram_words_per_row(K)
+        packed = rng.integers(-32768, 32768, (n, words), dtype=np.int16)
+        scales = rng.normal(0, 0.05, n).astype(np.float16)
+        scales[0] = np.float16(0.0)
+        scales[1] = np.float16(-1.5)
+        packed[:, 0] = scales.view(np.int16)
+        heads = rng.integers(0, 3, n).astype(np.int32)
+        bias = rng.normal(0, 0.02, (3, ref_exl3.NGRAM_ROW_DIM)).astype(np.float16)
+        got = ref_exl3.ngram_dequant_rows_torch(torch.from_numpy(packed), K, torch.from_numpy(heads),
+                                                torch.from_numpy(bias)).numpy()
+        out[f"K{K}_packed"] = packed
+        out[f"K{K}_heads"] = heads
+        out[f"K{K}_bias"] = bias
+        out[f"K{K}_out"] = got
+    np.savez_compressed(os.path.join(HERE, "ngram.npz"), **out)
 
 
 if __name__ == "__main__":

@@ -179,3 +179,75 @@ def test_fat_gemm_and_scatter(native, cuda, K, mcg, mul1):
     exp = acc0.copy()
     exp[tok.cpu().numpy()] += want * rw.float().cpu().numpy()[:, None]
     _close(acc.cpu().numpy(), exp)
+
+
+@pytest.mark.parametrize("rows", [1, 5, 40, 300])
+def test_dense_linear_method_shards(native, cuda, rows):
+    """Exl3LinearMethod mirror (exl3.py:6656-6739) on the GPU: three EXL3
+    shards (QKV-like, K 2/3/4) through the opaque custom op, fp32 per shard
+    rounded once to bf16, concatenated, 3-D input shape restored; the decode
+    GEMV (< 32 rows) and the tcgen05 GEMM path (>= 32)."""
+    import torch
+    from exl3_b200 import linear as lin
+    from exl3_b200 import synthetic
+    rng = np.random.default_rng(600 + rows)
+    projs = [synthetic.make_projection(rng, 512, o, K, synthetic.CB_MCG) for o, K in ((512, 4), (256, 2), (256, 3))]
+    layer = lin.linear_from_projections(projs, cuda, name=f"test.dense.{rows}")
+    x = torch.from_numpy(rng.normal(0, 1, (rows, 1, 512)).astype(np.float32)).to(cuda).to(torch.bfloat16)
+    y = layer(x)
+    assert y.shape == (rows, 1, 1024) and y.dtype == torch.bfloat16
+    xh = x.reshape(rows, 512).float().cpu().numpy().astype(np.float16).astype(np.float32)
+    want = np.concatenate([xh @ oracle.dequant(p.trellis, p.suh, p.svh, p.K, cb=1).astype(np.float32)
+                           for p in projs], axis=1)
+    # fp32 kernel output (the pass/fail comparison), then the bf16 layer output
+    # equals that fp32 result rounded once
+    f32 = torch.cat([native.exl3_linear(x.reshape(rows, 512), s.trellis, s.suh, s.svh, s.K, 1,
+                                        out_dtype=torch.float32) for s in layer._exl3_linears], dim=1)
+    _close(f32.cpu().numpy(), want)
+    assert torch.equal(y.reshape(rows, 1024), f32.to(torch.bfloat16))
+
+
+def test_ngram_dequant_bit_exact_with_reference_fixtures(native, cuda):
+    """exl3_ngram_dequant (ExLlamaV3 ngram_dequant, exl3.py:5536-5544) against
+    the reference's ngram_dequant_rows_torch outputs, K = 1..8, bit for bit."""
+    import torch
+    data = np.load(os.path.join(GOLDEN, "ngram.npz"))
+    for K in range(1, 9):
+        packed = torch.from_numpy(data[f"K{K}_packed"]).to(cuda)
+        heads = torch.from_numpy(data[f"K{K}_heads"]).to(cuda)
+        bias = torch.from_numpy(data[f"K{K}_bias"]).to(cuda)
+        out = torch.empty(packed.shape[0], 160, dtype=torch.float16, device=cuda)
+        native.ngram_dequant(packed, K, heads, bias, out)
+        assert np.array_equal(out.cpu().numpy().view(np.uint16), data[f"K{K}_out"].view(np.uint16)), K
+
+
+@pytest.mark.parametrize("K", [2, 3, 4, 8])
+def test_ngram_embedding_lookup(native, cuda, K):
+    """The fused lookup (gather, head search, decode, cast; exl3.py:5576-5587)
+    against the oracle; an id outside the table gives a zero row and status 7."""
+    import torch
+    from exl3_b200.ngram import Exl3NgramEmbedding, ngram_words_per_row
+    rng = np.random.default_rng(700 + K)
+    n_rows, words = 5000, ngram_words_per_row(K)
+    table = rng.integers(-32768, 32768, (n_rows, words), dtype=np.int16)
+    table[:, 0] = rng.normal(0, 0.05, n_rows).astype(np.float16).view(np.int16)
+    offsets = np.array([0, 1000, 1700, 4000], dtype=np.int64)
+    bias = rng.normal(0, 0.02, (4, 160)).astype(np.float16)
+    emb = Exl3NgramEmbedding(torch.from_numpy(table).to(cuda), K, torch.from_numpy(offsets),
+                             torch.from_numpy(bias).to(cuda), dtype=torch.bfloat16)
+    ids = rng.integers(0, n_rows, (3, 37)).astype(np.int64)
+    ids[0, :4] = [0, 999, 1000, 4999]
+    got = emb(torch.from_numpy(ids).to(cuda))
+    assert got.shape == (3, 37, 160) and got.dtype == torch.bfloat16
+    flat = ids.reshape(-1)
+    heads = np.clip(np.searchsorted(offsets, flat, side="right") - 1, 0, 3)
+    want = oracle.ngram_dequant(table[flat], K, heads, bias)
+    want_bf16 = torch.from_numpy(want.astype(np.float32)).to(torch.bfloat16)
+    assert torch.equal(got.reshape(-1, 160).cpu(), want_bf16)
+    assert emb.status() == 0
+    bad = torch.tensor([[5, n_rows, -1]], dtype=torch.int32, device=cuda)
+    got_bad = emb(bad)
+    assert emb.status() == 7
+    assert torch.all(got_bad[0, 1:] == 0)
+    want5 = oracle.ngram_dequant(table[[5]], K, np.array([0]), bias).astype(np.float32)
+    assert torch.equal(got_bad[0, 0].cpu(), torch.from_numpy(want5[0]).to(torch.bfloat16))

@@ -172,3 +172,12 @@ def test_activation_reference_values():
     assert out[0, 0] == pytest.approx(400.0, abs=1e-4)
     out = oracle.moe_eager(x, np.array([[0]]), np.array([[1.0]]), dense, limit=10.0)
     assert out[0, 0] == pytest.approx(99.9954605, abs=0.01)
+
+
+def test_ngram_decode_matches_reference_fixtures():
+    """The n-gram row decode restatement against the reference's own
+    ngram_dequant_rows_torch outputs (tests/golden/ngram.npz), bit for bit."""
+    data = np.load(os.path.join(GOLDEN, "ngram.npz"))
+    for K in range(1, 9):
+        got = oracle.ngram_dequant(data[f"K{K}_packed"], K, data[f"K{K}_heads"], data[f"K{K}_bias"])
+        assert np.array_equal(got.view(np.uint16), data[f"K{K}_out"].view(np.uint16)), K

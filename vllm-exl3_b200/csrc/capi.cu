@@ -559,4 +559,40 @@ int exl3_profile_read(float* ms, int max_phases, int* n_phases) {
     return EXL3_OK;
 }
 
+
+int exl3_ngram_dequant(const void* packed, int64_t n, int bits, const int32_t* heads, const void* head_bias,
+                       int num_heads, void* out, int out_dtype, void* stream) {
+    const char* who = "exl3_ngram_dequant";
+    if (n < 0) return fail(EXL3_ERR_ARG, "%s: n must be >= 0", who);
+    if (bits < 1 || bits > 8) return fail(EXL3_ERR_ARG, "%s: bits must be in 1..8 (got %d)", who, bits);
+    if (num_heads < 1) return fail(EXL3_ERR_ARG, "%s: num_heads must be >= 1", who);
+    if (!float_dtype(out_dtype)) return fail(EXL3_ERR_ARG, "%s: out dtype must be fp32, fp16 or bf16", who);
+    if (n == 0) return EXL3_OK;
+    if (!packed || !heads || !head_bias || !out) return fail(EXL3_ERR_ARG, "%s: null pointer", who);
+    if (!aligned(packed, 2) || !aligned(head_bias, 2)) return fail(EXL3_ERR_ARG, "%s: misaligned fp16/int16 data", who);
+    cudaError_t e = exl3::run_ngram(static_cast<const uint16_t*>(packed), n, n, bits, nullptr, EXL3_DT_I32, heads,
+                                    nullptr, num_heads, head_bias, out, out_dtype, nullptr,
+                                    static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, who);
+}
+
+int exl3_ngram_lookup(const void* table, int64_t n_rows, int bits, const void* ids, int ids_dtype, int64_t n,
+                      const int64_t* head_offsets, int num_heads, const void* head_bias, void* out, int out_dtype,
+                      int* status, void* stream) {
+    const char* who = "exl3_ngram_lookup";
+    if (n < 0 || n_rows < 0) return fail(EXL3_ERR_ARG, "%s: n and n_rows must be >= 0", who);
+    if (bits < 1 || bits > 8) return fail(EXL3_ERR_ARG, "%s: bits must be in 1..8 (got %d)", who, bits);
+    if (num_heads < 1) return fail(EXL3_ERR_ARG, "%s: num_heads must be >= 1", who);
+    if (ids_dtype != EXL3_DT_I32 && ids_dtype != EXL3_DT_I64)
+        return fail(EXL3_ERR_ARG, "%s: ids must be int32 or int64", who);
+    if (!float_dtype(out_dtype)) return fail(EXL3_ERR_ARG, "%s: out dtype must be fp32, fp16 or bf16", who);
+    if (n == 0) return EXL3_OK;
+    if (!table || !ids || !head_offsets || !head_bias || !out) return fail(EXL3_ERR_ARG, "%s: null pointer", who);
+    if (!aligned(table, 2) || !aligned(head_bias, 2)) return fail(EXL3_ERR_ARG, "%s: misaligned fp16/int16 data", who);
+    cudaError_t e = exl3::run_ngram(static_cast<const uint16_t*>(table), n, n_rows, bits, ids, ids_dtype, nullptr,
+                                    head_offsets, num_heads, head_bias, out, out_dtype, status,
+                                    static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? EXL3_OK : cuda_fail(e, who);
+}
+
 }  // extern "C"

@@ -38,6 +38,7 @@ enum DevStatus : int {
     DEV_WAIT_TIMEOUT = 4,   // an mbarrier wait exceeded its bound
     DEV_BAD_ROUTE = 5,      // routing table inconsistent (internal)
     DEV_BAD_LAUNCH = 6,     // launch shape inconsistent with the kernel's needs (internal)
+    DEV_BAD_INDEX = 7,      // a row id outside its table (n-gram lookup); the row is written as zeros
 };
 
 __device__ __forceinline__ void set_status(int* status, int code) {

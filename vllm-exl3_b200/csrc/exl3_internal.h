@@ -185,6 +185,13 @@ cudaError_t run_ep_p2p(const EpP2pCall& c, cudaStream_t s);
 cudaError_t run_ep_combine(const void* partial, int pdt, const int32_t* pair_idx, int64_t tokens, int world,
                            int hidden, const int32_t* n_valid, void* out, int odt, cudaStream_t s);
 
+// n-gram embedding rows (ngram.cu): decode `n` packed rows given in order
+// (ids == nullptr, heads per row) or gather rows `ids` of a table of n_rows
+// (heads from head_offsets)
+cudaError_t run_ngram(const uint16_t* rows, int64_t n, int64_t n_rows, int bits, const void* ids, int ids_dtype,
+                      const int32_t* heads, const int64_t* head_offsets, int num_heads, const void* head_bias,
+                      void* out, int out_dtype, int* status, cudaStream_t s);
+
 int num_sms_current();
 // stages and dynamic smem of the GEMM for mt 128-row halves per tile; false
 // if two stages do not fit at two CTAs per SM

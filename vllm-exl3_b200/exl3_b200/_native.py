@@ -71,6 +71,8 @@ SIGNATURES = {
     "exl3_ep_p2p_combine": (I32, [P, I32, I32, I64, I64, I32, I32, I32, P, I64, P, P, I32, P]),
     "exl3_ep_window_recv": (I32, [I32, I64, I64, I32, I32, I32, ctypes.POINTER(SZ), ctypes.POINTER(SZ),
                                   ctypes.POINTER(SZ)]),
+    "exl3_ngram_dequant": (I32, [P, I64, I32, P, P, I32, P, I32, P]),
+    "exl3_ngram_lookup": (I32, [P, I64, I32, P, I32, I64, P, I32, P, P, I32, P, P]),
     "exl3_profile_enable": (I32, [I32, ctypes.c_longlong]),
     "exl3_profile_read": (I32, [ctypes.POINTER(F32), I32, ctypes.POINTER(I32)]),
 }

@@ -17,7 +17,7 @@ ROOT = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(ROOT, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libexl3_b200.so")
 
-SOURCES = ["capi.cu", "moe.cu", "reconstruct.cu", "noalloc.cu", "tc_gemm.cu", "ep.cu"]
+SOURCES = ["capi.cu", "moe.cu", "reconstruct.cu", "noalloc.cu", "tc_gemm.cu", "ep.cu", "ngram.cu"]
 HEADERS = ["exl3_common.cuh", "exl3_internal.h", "tc_common.cuh", "tc_gemm.h"]
 
 NVCC_FLAGS = [

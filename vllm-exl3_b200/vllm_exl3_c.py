@@ -453,6 +453,32 @@ def exl3_moe(x, out, gate_trellis_ptrs, gate_suh_ptrs, gate_svh_ptrs, up_trellis
                      n_valid=n_valid, act=int(activation))
 
 
+def ngram_dequant(packed, bits, heads, head_bias, out):
+    """ExLlamaV3 ``ngram_dequant`` semantics (the reference's call site
+    src/vllm_exl3/exl3.py:5536-5544; pure-torch twin exl3.py:5213-5239):
+    packed int16 [N, 1 + 10 * bits] rows, heads int [N], head_bias fp16
+    [heads, 160] -> out [N, 160] (fp16, bf16 or fp32), written in place."""
+    _n.require_cuda(packed, heads, head_bias, out, who="ngram_dequant")
+    bits = int(bits)
+    if not 1 <= bits <= 8:
+        raise RuntimeError("ngram_dequant: bits must be in 1..8")
+    if packed.dtype != torch.int16 or packed.dim() != 2 or packed.size(1) != 1 + 10 * bits:
+        raise RuntimeError("ngram_dequant: packed must be int16 [N, 1 + 160 * bits / 16]")
+    if head_bias.dtype != torch.float16 or head_bias.dim() != 2 or head_bias.size(1) != 160:
+        raise RuntimeError("ngram_dequant: head_bias must be fp16 [heads, 160]")
+    if out.shape != (packed.size(0), 160) or not out.is_contiguous():
+        raise RuntimeError("ngram_dequant: out must be a contiguous [N, 160] tensor")
+    h = heads.to(torch.int32).contiguous().view(-1)
+    if h.numel() != packed.size(0):
+        raise RuntimeError("ngram_dequant: one head per row")
+    p, b = packed.contiguous(), head_bias.contiguous()
+    with torch.cuda.device(packed.device):
+        _n.check(_n.load().exl3_ngram_dequant(p.data_ptr(), int(p.size(0)), bits, h.data_ptr(), b.data_ptr(),
+                                              int(b.size(0)), out.data_ptr(), _n.dtype_code(out),
+                                              _n.stream_of(p)), "ngram_dequant")
+    return out
+
+
 def device_status(workspace=None, clear=True) -> int:
     """Device-side status word of a workspace (0 = clean).  Without one: the
     first nonzero word among every workspace of the current device (all
