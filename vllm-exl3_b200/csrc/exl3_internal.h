@@ -40,9 +40,9 @@ struct MoePlan {
     int64_t routes = 0;   // t_max * topk
     int64_t rpad = 0;     // sorted rows incl. per-expert padding to 16
     int64_t smax = 0;     // max work slots
-    // per phase: column blocks, k splits, k-tiles per split, grid
-    int ncb1 = 0, nsplit1 = 1, ktps1 = 0, grid1 = 0, stages1 = 0;
-    int ncb2 = 0, nsplit2 = 1, ktps2 = 0, grid2 = 0, stages2 = 0;
+    // per GEMV phase: column blocks, grid, ring stages
+    int ncb1 = 0, grid1 = 0, stages1 = 0;
+    int ncb2 = 0, grid2 = 0, stages2 = 0;
     size_t smem1 = 0, smem2 = 0;
     // prefill path: tcgen05 grouped GEMM over 128-row expert tiles
     bool gemm = false;
@@ -56,7 +56,7 @@ struct MoePlan {
     int tc_split1 = 1, tc_split2 = 1;
     size_t off_tcpart = 0, off_tccnt = 0;
     // offsets
-    size_t off_status = 0, off_nslots = 0, off_sched = 0, off_slots = 0, off_route_pos = 0, off_sorted_tok = 0,
+    size_t off_status = 0, off_nslots = 0, off_slots = 0, off_route_pos = 0, off_sorted_tok = 0,
            off_sorted_route = 0, off_ntiles128 = 0, off_tiles128 = 0, off_g = 0, off_u = 0, off_x2 = 0,
            off_sorted_exp = 0, off_sorted_w = 0, off_xr = 0, off_a2 = 0, off_yd = 0,
            off_part1 = 0, off_part2 = 0, off_cnt1 = 0, off_cnt2 = 0, off_hist = 0;

@@ -22,13 +22,15 @@
 //  2. rotate   fp16 H128(x o suh)/sqrt128 per (route, projection, 128-block),
 //              stored [proj][kblock][row][136] (rows padded to 272 bytes so a
 //              1-D bulk copy lands ldmatrix-conflict-free).
-//  3. gemv<2>  gate+up: work item = (slot, 128-column block, k split).  A
-//              producer thread streams the item's trellis rows and rotated
-//              inputs into a shared-memory ring with cp.async.bulk; 8 consumer
-//              warps (one 16-column tile each, gate and up together) decode
-//              each 16x16 tile in registers straight into mma.m16n8k16 A
-//              fragments and accumulate in fp32.  Split-K partials are reduced
-//              in fixed order by the last CTA of the group (deterministic).
+//  3. gemv<2>  gate+up: group = (slot, 128-column block), split stream-K:
+//              every CTA takes the same number of 128-deep k stages of the
+//              group sequence, so no wave is left half full.  A producer
+//              thread streams the trellis rows and rotated inputs into a
+//              shared-memory ring with cp.async.bulk; 8 consumer warps (one
+//              16-column tile each, gate and up together) decode each 16x16
+//              tile in registers straight into mma.m16n8k16 A fragments and
+//              accumulate in fp32.  A group cut between CTAs is reduced in
+//              stage order by the CTA that completes it (deterministic).
 //              Epilogue: output FWHT o svh, SwiGLU (+clamp), fp16 round,
 //              down-input rotation o suh_down -> rotated down inputs.
 //  4. gemv<1>  down: same engine; epilogue FWHT o svh * route weight -> per-route rows.
@@ -78,7 +80,6 @@ struct WsPtrs {
     int* cnt2;
     int* ntiles128;
     float* tcpart;  // GEMM split-K partials
-    int* sched;     // GEMV dynamic item counters [gate/up or linear, down]
     int4* tiles128;  // {expert, first sorted row, rows <= tile_rows, 0}: the GEMM path's work tiles
     float* g;
     float* u;
@@ -106,7 +107,6 @@ static WsPtrs ws_ptrs(const MoePlan& p, void* ws) {
     w.cnt2 = reinterpret_cast<int*>(b + p.off_cnt2);
     w.ntiles128 = reinterpret_cast<int*>(b + p.off_ntiles128);
     w.tcpart = reinterpret_cast<float*>(b + p.off_tcpart);
-    w.sched = reinterpret_cast<int*>(b + p.off_sched);
     w.tiles128 = reinterpret_cast<int4*>(b + p.off_tiles128);
     w.g = reinterpret_cast<float*>(b + p.off_g);
     w.u = reinterpret_cast<float*>(b + p.off_u);
@@ -296,7 +296,6 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
 
     for (int i = tid; i < a.cnt1_n; i += kPrepThreads) a.w.cnt1[i] = 0;
     for (int i = tid; i < a.cnt2_n; i += kPrepThreads) a.w.cnt2[i] = 0;
-    if (tid < 2) a.w.sched[tid] = 0;
     for (int e = tid; e < E; e += kPrepThreads) cnt[e] = 0;
     __syncthreads();
     #pragma unroll
@@ -340,7 +339,6 @@ __global__ void __launch_bounds__(kPrepThreads) prep_plan_kernel(const PrepArgs 
     const int64_t R = prep_routes(a), Rmax = a.t_max * a.topk;
     for (int i = tid; i < a.cnt1_n; i += kPrepThreads) a.w.cnt1[i] = 0;
     for (int i = tid; i < a.cnt2_n; i += kPrepThreads) a.w.cnt2[i] = 0;
-    if (tid < 2) a.w.sched[tid] = 0;
     for (int e = tid; e < E; e += kPrepThreads) {
         int n = 0;
         for (int c = 0; c < nchunks; ++c) n += a.w.hist[int64_t(c) * E + e];
@@ -562,7 +560,7 @@ static void launch_rotate_rows(const RotArgs& ra, const int* sorted_exp, int gri
 struct GemvArgs {
     int* status;
     ProjRef proj[2];
-    int in_f, out_f, ncb, nsplit, ktps, stages, kmax;
+    int in_f, out_f, ncb, stages, kmax;
     const int* nslots;
     const int4* slots;
     const __half* xin;
@@ -584,19 +582,36 @@ struct GemvArgs {
     const __half* scatter_w;
     int64_t t_max;
     int topk;
-    // split-K
+    // split-K: partial tiles [2 * gridDim.x][kCW][NPROJ * 256], one counter per group
     float* part;
     int* cnt;
-    int* sched;  // dynamic item counter (zeroed by the routing prep)
 };
 
-constexpr int kGemvItemQueue = 16;  // > the most stages the producer runs ahead
+// Item ring: the producer stages each work item's description and the
+// vectors its epilogue needs (svh slices, the down suh slice, per-row route
+// data) in shared memory ahead of the consumers, so no consumer waits on a
+// global load at an item's start or in its epilogue.  Slot j % kItemRing
+// holds item j; the consumers release it after the item's epilogue.
+constexpr int kItemRing = 4;
+enum ItemField : int { IF_E = 0, IF_P0, IF_ROWS, IF_CB, IF_KT0, IF_KT1, IF_K0, IF_K1, IF_OK0, IF_OK1,
+                       IF_SVH0, IF_SVH1, IF_DSUH };
+// vector modes: 0 = absent (zeros), 1 = staged in the slot, 2 = read from global memory
+struct ItemSlot {
+    int info[16];
+    __half svh[2][128];
+    __half dsuh[128];
+    float w[16];
+    int tok[16];
+    int route[16];
+};
+static_assert(sizeof(ItemSlot) == 1024, "item slot layout");
 
 struct GemvSmem {
     uint64_t* full;
     uint64_t* empty;
+    uint64_t* item_empty;  // [kItemRing]
     int* flags;  // [0] abort, [1] last-of-group
-    int* items;  // [kGemvItemQueue] item ids the producer claimed, in order (-1: no more)
+    ItemSlot* items;  // [kItemRing]
     float* ys;   // [NPROJ][16][kYsPitch]
     char* stages;
 };
@@ -609,43 +624,90 @@ __host__ __device__ inline size_t gemv_trellis_bytes(int nproj, int kmax) {
 __host__ __device__ inline size_t gemv_stage_bytes(int nproj, int kmax, bool dup) {
     return (gemv_trellis_bytes(nproj, kmax) + size_t(nproj) * x_slice(dup) + 127) & ~size_t(127);
 }
+__host__ __device__ inline size_t gemv_bar_bytes(int stages) {
+    return (size_t(stages) * 2 * 8 + kItemRing * 8 + 8 * 4 + 127) & ~size_t(127);
+}
 __host__ __device__ inline size_t gemv_fixed_bytes(int nproj, int stages) {
-    const size_t bars = (size_t(stages) * 2 * 8 + 8 * 4 + kGemvItemQueue * 4 + 127) & ~size_t(127);
     const size_t ys = (size_t(nproj) * 16 * kYsPitch * 4 + 127) & ~size_t(127);
-    return bars + ys;
+    return gemv_bar_bytes(stages) + kItemRing * sizeof(ItemSlot) + ys;
 }
 
 __device__ __forceinline__ GemvSmem gemv_smem(char* base, int nproj, int stages) {
     GemvSmem s;
     s.full = reinterpret_cast<uint64_t*>(base);
     s.empty = s.full + stages;
-    s.flags = reinterpret_cast<int*>(s.empty + stages);
-    s.items = s.flags + 8;
-    const size_t bars = (size_t(stages) * 2 * 8 + 8 * 4 + kGemvItemQueue * 4 + 127) & ~size_t(127);
-    s.ys = reinterpret_cast<float*>(base + bars);
+    s.item_empty = s.empty + stages;
+    s.flags = reinterpret_cast<int*>(s.item_empty + kItemRing);
+    s.items = reinterpret_cast<ItemSlot*>(base + gemv_bar_bytes(stages));
+    s.ys = reinterpret_cast<float*>(base + gemv_bar_bytes(stages) + kItemRing * sizeof(ItemSlot));
     s.stages = base + gemv_fixed_bytes(nproj, stages);
     return s;
 }
 
-struct ItemInfo {
-    int e, p0, rows, cb, sp, kt0, kt1, group;
+// Stream-K work split.  The work is the sequence of (group, stage) pairs,
+// group g = (slot g / ncb, 128-column block g % ncb) holding NS = in_f / 128
+// stages; CTA i takes the stages [i W, (i + 1) W) with W = ceil(total / grid),
+// so every CTA gets the same number of stages whatever the batch (no tail
+// wave).  A group cut by CTA boundaries becomes pieces, one per CTA: each
+// piece writes its fp32 partial tile, and the CTA that completes the group's
+// count adds the pieces in stage order (deterministic) and runs the epilogue.
+// A CTA cuts at most its first and last group, so the partials take two
+// slots per CTA.  Every thread derives the same split from the slot count.
+// (Stage counts stay far below 2^31: groups <= slots * out/128.)
+struct StreamK {
+    int groups, W, NS;
 };
 
-__device__ __forceinline__ ItemInfo gemv_item(const GemvArgs& a, int64_t it) {
+__device__ __forceinline__ StreamK gemv_streamk(const GemvArgs& a) {
+    StreamK k;
+    k.NS = a.in_f / 128;
+    k.groups = *a.nslots * a.ncb;
+    k.W = (k.groups * k.NS + int(gridDim.x) - 1) / int(gridDim.x);
+    return k;
+}
+
+// first group of CTA c's range
+__device__ __forceinline__ int sk_first_group(const StreamK& k, int c) { return c * k.W / k.NS; }
+
+struct ItemInfo {
+    int e, p0, rows, cb, kt0, kt1, group;
+};
+
+// the CTA's piece of group g (g inside the CTA's range)
+__device__ __forceinline__ ItemInfo gemv_item(const GemvArgs& a, const StreamK& k, int g) {
     ItemInfo I;
-    const int per = a.ncb * a.nsplit;
-    const int64_t slot = it / per;
-    const int rem = int(it % per);
-    I.cb = rem / a.nsplit;
-    I.sp = rem % a.nsplit;
+    const int c = blockIdx.x;
+    const int gs0 = g * k.NS;
+    I.kt0 = (max(c * k.W, gs0) - gs0) * kKtPerStage;
+    I.kt1 = (min((c + 1) * k.W, gs0 + k.NS) - gs0) * kKtPerStage;
+    const int slot = g / a.ncb;
+    I.cb = g - slot * a.ncb;
     const int4 sl = a.slots[slot];
     I.e = sl.x;
     I.p0 = sl.y;
     I.rows = sl.z;
-    I.kt0 = I.sp * a.ktps;
-    I.kt1 = min(I.kt0 + a.ktps, a.in_f / 16);
-    I.group = int(slot * a.ncb + I.cb);
+    I.group = g;
     return I;
+}
+
+// CTAs holding the first and last pieces of group g
+__device__ __forceinline__ int sk_cta0(const StreamK& k, int g) { return g * k.NS / k.W; }
+__device__ __forceinline__ int sk_cta1(const StreamK& k, int g) { return (g * k.NS + k.NS - 1) / k.W; }
+// partial slot of CTA c's piece of group g: its first group or its last
+__device__ __forceinline__ int sk_pslot(const StreamK& k, int c, int g) {
+    return 2 * c + (g == sk_first_group(k, c) ? 0 : 1);
+}
+
+// the CTA's group range [g0, g1)
+__device__ __forceinline__ void sk_range(const StreamK& k, int& g0, int& g1) {
+    const int c = blockIdx.x;
+    const int s0 = c * k.W, s1 = min((c + 1) * k.W, k.groups * k.NS);
+    if (s0 >= s1) {
+        g0 = g1 = 0;
+        return;
+    }
+    g0 = s0 / k.NS;
+    g1 = (s1 - 1) / k.NS + 1;
 }
 
 // is projection usable for this expert (pointer present, aligned, K valid)?
@@ -779,13 +841,16 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], kCW);
         }
+        for (int j = 0; j < kItemRing; ++j) mbar_init(&sm.item_empty[j], 1);
         sm.flags[0] = 0;
         sm.flags[1] = 0;
         mbar_fence_init();
     }
     __syncthreads();
 
-    const int64_t n_items = int64_t(*a.nslots) * a.ncb * a.nsplit;
+    const StreamK sk = gemv_streamk(a);
+    int g0, g1;
+    sk_range(sk, g0, g1);
     const int nkb = a.in_f / 128;
     const int ntiles_out = a.out_f / 16;
 
@@ -795,14 +860,10 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
         uint32_t q = 0;   // stages issued
         int ps = 0;       // ring slot and parity of stage q
         uint32_t pph = 0u;
-        // items: the CTA's own first, then claimed from the shared counter
-        // (dynamic: SMs that finish early take more), each published in the
-        // item queue before its first stage is issued
-        uint32_t jq = 0;
-        for (int64_t it = blockIdx.x; it < n_items && !*abort_flag;
-             it = int64_t(gridDim.x) + atomicAdd(a.sched, 1), ++jq) {
-            const ItemInfo I = gemv_item(a, it);
-            sm.items[jq % kGemvItemQueue] = int(it);
+        int ji = 0;  // item ring slot and parity
+        uint32_t jph = 0u;
+        for (int g = g0; g < g1 && !*abort_flag; ++g, ring_next(ji, jph, kItemRing)) {
+            const ItemInfo I = gemv_item(a, sk, g);
             bool ok[NPROJ];
             int Kp[NPROJ];
             const uint16_t* tp[NPROJ];
@@ -812,11 +873,53 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 Kp[p] = proj_k(a.proj[p], I.e);
                 tp[p] = proj_trellis(a.proj[p], I.e);
             }
+            // the item's slot (free once the consumers finished item j - kItemRing)
+            if (!guarded_wait(&sm.item_empty[ji], jph ^ 1u, a.status, abort_flag)) break;
+            ItemSlot& is = sm.items[ji];
+            is.info[IF_E] = I.e;
+            is.info[IF_P0] = I.p0;
+            is.info[IF_ROWS] = I.rows;
+            is.info[IF_CB] = I.cb;
+            is.info[IF_KT0] = I.kt0;
+            is.info[IF_KT1] = I.kt1;
+            #pragma unroll
+            for (int p = 0; p < NPROJ; ++p) {
+                is.info[IF_K0 + p] = Kp[p];
+                is.info[IF_OK0 + p] = ok[p] ? 1 : 0;
+            }
+            // the item's vectors ride on its first stage's barrier
+            const __half* vsrc[3] = {nullptr, nullptr, nullptr};
+            void* vdst[3] = {is.svh[0], is.svh[1], is.dsuh};
+            #pragma unroll
+            for (int p = 0; p < NPROJ; ++p) vsrc[p] = proj_svh(a.proj[p], I.e);
+            if (EPI == EPI_GATEUP) vsrc[2] = proj_suh(a.down, I.e);
+            uint32_t vbytes = 0;
+            #pragma unroll
+            for (int v = 0; v < 3; ++v) {
+                if (v >= NPROJ && v < 2) continue;
+                if (v == 2 && EPI != EPI_GATEUP) continue;
+                int mode = 0;
+                if (vsrc[v]) {
+                    vsrc[v] += size_t(I.cb) * 128;
+                    mode = (reinterpret_cast<uintptr_t>(vsrc[v]) & 15) ? 2 : 1;
+                    if (mode == 1) vbytes += 256;
+                }
+                is.info[IF_SVH0 + v] = mode;
+            }
+            const void* rsrc = EPI == EPI_DOWN ? static_cast<const void*>(a.sorted_w + I.p0)
+                             : EPI == EPI_LINEAR ? static_cast<const void*>(a.sorted_tok + I.p0)
+                                                 : static_cast<const void*>(a.sorted_route + I.p0);
+            void* rdst = EPI == EPI_DOWN ? static_cast<void*>(is.w)
+                       : EPI == EPI_LINEAR ? static_cast<void*>(is.tok) : static_cast<void*>(is.route);
+            const bool rows_v = EPI != EPI_GATEUP;
+            if (rows_v) vbytes += 64;
+            bool first_stage = true;
             for (int kt = I.kt0; kt < I.kt1; kt += kKtPerStage, ++q, ring_next(ps, pph, S)) {
                 const int s = ps;
                 if (!guarded_wait(&sm.empty[s], pph ^ 1u, a.status, abort_flag)) break;
                 char* st = sm.stages + size_t(s) * stage_bytes;
                 uint32_t bytes = NPROJ * XS;
+                if (first_stage) bytes += vbytes;
                 #pragma unroll
                 for (int p = 0; p < NPROJ; ++p)
                     if (ok[p]) bytes += kKtPerStage * 256 * Kp[p];
@@ -840,22 +943,22 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                     const __half* src = a.xin + ((int64_t(p) * nkb + kb) * a.rpad + I.p0) * XP;
                     bulk_g2s(st + xs_off + size_t(p) * XS, src, uint32_t(XS), &sm.full[s]);
                 }
+                if (first_stage) {
+                    #pragma unroll
+                    for (int v = 0; v < 3; ++v)
+                        if (is.info[IF_SVH0 + v] == 1 && (v < NPROJ || (v == 2 && EPI == EPI_GATEUP)))
+                            bulk_g2s(vdst[v], vsrc[v], 256u, &sm.full[s]);
+                    if (rows_v) bulk_g2s(rdst, rsrc, 64u, &sm.full[s]);
+                    first_stage = false;
+                }
             }
         }
-        // drain: every issued stage must land before the CTA exits.  This
-        // comes before the end marker below, which advances the full barrier
-        // of slot q % S, the slot of stage q - S: a parity wait for that
-        // stage after the marker would see the barrier two phases on.
+        // drain: every issued stage must land before the CTA exits (the
+        // consumers may have stopped early on an abort)
         const uint32_t first = q > uint32_t(S) ? q - uint32_t(S) : 0u;
         for (uint32_t r = first; r < q; ++r) {
             const int s = int(r % uint32_t(S));
             mbar_wait(&sm.full[s], (r / uint32_t(S)) & 1u, a.status);
-        }
-        // no more items: publish the end marker through the next ring slot
-        // (an arrival without data, once the slot's previous use is consumed)
-        if (guarded_wait(&sm.empty[ps], pph ^ 1u, a.status, abort_flag)) {
-            sm.items[jq % kGemvItemQueue] = -1;
-            mbar_arrive(&sm.full[ps]);
         }
         return;
     }
@@ -867,18 +970,26 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
     const uint32_t xs_lane = uint32_t(brow * XP * 2 + ((lane >> 3) & 1) * 16);
     int cs = 0;  // ring slot and parity of the next stage
     uint32_t cph = 0u;
-    for (uint32_t jc = 0;; ++jc) {
-        // the next stage's arrival publishes its item (or the end marker)
+    int ji = 0;  // item ring slot
+    uint32_t jph = 0u;
+    for (int g = g0; g < g1; ++g, ring_next(ji, jph, kItemRing)) {
+        // the item's first stage has landed: its slot is filled
         if (!guarded_wait(&sm.full[cs], cph, a.status, abort_flag)) break;
-        const int it = sm.items[jc % kGemvItemQueue];
-        if (it < 0) break;
-        const ItemInfo I = gemv_item(a, it);
+        const ItemSlot& is = sm.items[ji];
+        ItemInfo I;
+        I.e = is.info[IF_E];
+        I.p0 = is.info[IF_P0];
+        I.rows = is.info[IF_ROWS];
+        I.cb = is.info[IF_CB];
+        I.kt0 = is.info[IF_KT0];
+        I.kt1 = is.info[IF_KT1];
+        I.group = g;
         bool ok[NPROJ];
         int Kp[NPROJ];
         #pragma unroll
         for (int p = 0; p < NPROJ; ++p) {
-            ok[p] = proj_ok(a.proj[p], I.e, a.kmax, a.status, false);
-            Kp[p] = proj_k(a.proj[p], I.e);
+            ok[p] = is.info[IF_OK0 + p] != 0;
+            Kp[p] = is.info[IF_K0 + p];
         }
         bool same = ok[0];
         #pragma unroll
@@ -930,9 +1041,10 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             if (lane == 0) mbar_arrive(&sm.empty[s]);
         }
 
-        // ---- split-K: last CTA of the group reduces partials in split order
-        if (a.nsplit > 1) {
-            float* pp = a.part + ((int64_t(I.group) * a.nsplit + I.sp) * kCW + cw) * (NPROJ * 256);
+        // ---- split group: the CTA completing it adds the pieces in stage order
+        const int c0 = sk_cta0(sk, g), c1 = sk_cta1(sk, g);
+        if (c0 != c1) {
+            float* pp = a.part + (int64_t(sk_pslot(sk, blockIdx.x, g)) * kCW + cw) * (NPROJ * 256);
             #pragma unroll
             for (int p = 0; p < NPROJ; ++p)
                 #pragma unroll
@@ -941,19 +1053,22 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             named_bar_sync(1, NCT);
             if (threadIdx.x == 0) {
                 const int old = atomicAdd(&a.cnt[I.group], 1);
-                const int last = old == a.nsplit - 1;
+                const int last = old == c1 - c0;
                 if (last) a.cnt[I.group] = 0;
                 sm.flags[1] = last;
             }
             named_bar_sync(1, NCT);
-            if (!sm.flags[1]) continue;
+            if (!sm.flags[1]) {
+                if (threadIdx.x == 0) mbar_arrive(&sm.item_empty[ji]);
+                continue;
+            }
             __threadfence();
             #pragma unroll
             for (int p = 0; p < NPROJ; ++p)
                 #pragma unroll
                 for (int i = 0; i < 8; ++i) acc[p][i >> 2][i & 3] = 0.f;
-            for (int sp = 0; sp < a.nsplit; ++sp) {
-                const float* rp = a.part + ((int64_t(I.group) * a.nsplit + sp) * kCW + cw) * (NPROJ * 256);
+            for (int c = c0; c <= c1; ++c) {
+                const float* rp = a.part + (int64_t(sk_pslot(sk, c, g)) * kCW + cw) * (NPROJ * 256);
                 #pragma unroll
                 for (int p = 0; p < NPROJ; ++p)
                     #pragma unroll
@@ -984,10 +1099,11 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             #pragma unroll
             for (int i = 0; i < 4; ++i) x[i] = row[lane + 32 * i];
             fwht128_warp(x, lane);
-            const __half* svh = proj_svh(a.proj[p], I.e);
+            const int vm = is.info[IF_SVH0 + p];
+            const __half* svh = vm == 1 ? is.svh[p] : vm == 2 ? proj_svh(a.proj[p], I.e) + I.cb * 128 : nullptr;
             #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float sv = svh ? __half2float(svh[I.cb * 128 + lane + 32 * i]) : 0.f;
+                const float sv = svh ? __half2float(svh[lane + 32 * i]) : 0.f;
                 row[lane + 32 * i] = x[i] * kHadNorm * sv;
             }
         }
@@ -996,7 +1112,8 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
         if constexpr (EPI == EPI_GATEUP) {
             // NPROJ == 2: gate (row block 0) and up (block 1); NPROJ == 1: the
             // up projection alone (non-gated relu^2)
-            const __half* dsuh = proj_suh(a.down, I.e);
+            const int dm = is.info[IF_DSUH];
+            const __half* dsuh = dm == 1 ? is.dsuh : dm == 2 ? proj_suh(a.down, I.e) + I.cb * 128 : nullptr;
             for (int r = cw; r < I.rows; r += kCW) {
                 const float* gr = sm.ys + r * kYsPitch;
                 const float* ur = sm.ys + ((NPROJ - 1) * 16 + r) * kYsPitch;
@@ -1019,7 +1136,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                         act = silu_f(g) * u;
                     }
                     const float h = __half2float(__float2half_rn(act));  // the reference's act.half()
-                    x[i] = h * (dsuh ? __half2float(dsuh[I.cb * 128 + c]) : 0.f);
+                    x[i] = h * (dsuh ? __half2float(dsuh[c]) : 0.f);
                 }
                 fwht128_warp(x, lane);
                 const int64_t p = I.p0 + r;
@@ -1038,7 +1155,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             for (int r = cw; r < I.rows; r += kCW) {
                 const float* row = sm.ys + r * kYsPitch;
                 const int64_t p = I.p0 + r;
-                const float w = a.sorted_w[p];
+                const float w = is.w[r];
                 float* dst = a.yd + p * a.out_f + I.cb * 128;
                 #pragma unroll
                 for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = row[lane + 32 * i] * w;
@@ -1046,7 +1163,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
         } else if constexpr (EPI == EPI_LINEAR) {
             for (int r = cw; r < I.rows; r += kCW) {
                 const float* row = sm.ys + r * kYsPitch;
-                const int tok = a.sorted_tok[I.p0 + r];
+                const int tok = is.tok[r];
                 if (tok < 0) continue;
                 if (a.scatter_idx) {
                     // one route per destination row per call: plain read-modify-write
@@ -1065,7 +1182,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             // EPI_ROUTE: route r = t * topk + j -> output row j * t_max + t
             for (int r = cw; r < I.rows; r += kCW) {
                 const float* row = sm.ys + r * kYsPitch;
-                const int rt = a.sorted_route[I.p0 + r];
+                const int rt = is.route[r];
                 if (rt < 0) continue;
                 const int64_t orow = int64_t(rt % a.topk) * a.t_max + rt / a.topk;
                 #pragma unroll
@@ -1075,6 +1192,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             }
         }
         named_bar_sync(1, NCT);
+        if (threadIdx.x == 0) mbar_arrive(&sm.item_empty[ji]);
     }
 }
 
@@ -1127,18 +1245,6 @@ static void pick_stages(int nproj, int kmax, bool dup, int& stages, size_t& smem
     smem = gemv_fixed_bytes(nproj, s) + size_t(s) * sb;
 }
 
-static void pick_split(int64_t groups_est, int grid, int nkt, int& nsplit, int& ktps) {
-    // at least 2 waves of items.  (A 4-wave target once the groups fill a
-    // wave trims the last partial wave at T = 64 but measured slower at
-    // T = 8 and 32, where the split-K reduction costs more than the tail.)
-    const int64_t target = 2 * int64_t(grid);
-    int ns = 1;
-    if (groups_est < target) ns = int((target + groups_est - 1) / groups_est);
-    ns = std::max(1, std::min(ns, nkt / kKtPerStage));
-    ktps = ((nkt + ns - 1) / ns + kKtPerStage - 1) / kKtPerStage * kKtPerStage;
-    nsplit = (nkt + ktps - 1) / ktps;
-}
-
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_local, int kmax,
@@ -1165,12 +1271,10 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     p.dup = cb != CB_MUL1;  // unknown codebook (-1): size for the larger layout
     pick_stages(linear ? 1 : 2, kmax, p.dup, p.stages1, p.smem1);
     p.grid1 = grid;
-    pick_split(p.smax * p.ncb1, grid, hidden / 16, p.nsplit1, p.ktps1);
     if (!linear) {
         p.ncb2 = hidden / 128;
         pick_stages(1, kmax, p.dup, p.stages2, p.smem2);
         p.grid2 = grid;
-        pick_split(act_max * p.ncb2, grid, inter / 16, p.nsplit2, p.ktps2);
     }
 
     // prefill-sized batches (>= 32 rows per active expert on average) take the
@@ -1191,7 +1295,6 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     };
     p.off_status = take(64);
     p.off_nslots = take(64);
-    p.off_sched = take(64);
     p.off_slots = take(size_t(p.smax) * 16);
     p.off_route_pos = take(size_t(p.routes) * 4);
     p.off_sorted_tok = take(size_t(p.rpad) * 4);
@@ -1210,7 +1313,6 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
         p.off_x2 = take(linear ? 0 : size_t(p.rpad) * inter * 2);
         p.off_yd = take(linear ? 0 : size_t(p.rpad) * hidden * 4);
         p.off_a2 = p.off_part1 = p.off_part2 = take(0);
-        p.nsplit1 = p.nsplit2 = 1;
         // split-K for the fused layer when few (tile, column block) items
         // can exist: fp32 partials per split and one counter per item
         if (!linear) {
@@ -1227,8 +1329,9 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
         p.off_xr = take(size_t(nproj1) * (hidden / 128) * p.rpad * x_pitch(p.dup) * 2);
         p.off_a2 = take(linear ? 0 : size_t(inter / 128) * p.rpad * x_pitch(p.dup) * 2);
         p.off_yd = take(linear ? 0 : size_t(p.rpad) * hidden * 4);
-        p.off_part1 = take(p.nsplit1 > 1 ? size_t(p.smax) * p.ncb1 * p.nsplit1 * kCW * nproj1 * 256 * 4 : 0);
-        p.off_part2 = take(!linear && p.nsplit2 > 1 ? size_t(p.smax) * p.ncb2 * p.nsplit2 * kCW * 256 * 4 : 0);
+        // stream-K partial tiles: two per CTA (exl3::gemv_item)
+        p.off_part1 = take(size_t(2) * p.grid1 * kCW * nproj1 * 256 * 4);
+        p.off_part2 = take(linear ? 0 : size_t(2) * p.grid2 * kCW * 256 * 4);
         p.off_cnt1 = take(size_t(p.smax) * p.ncb1 * 4);
         p.off_cnt2 = take(linear ? 0 : size_t(p.smax) * p.ncb2 * 4);
         p.off_g = p.off_u = p.off_x2 = take(0);
@@ -1463,15 +1566,12 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
         g.in_f = p.hidden;
         g.out_f = p.inter;
         g.ncb = p.ncb1;
-        g.nsplit = p.nsplit1;
-        g.ktps = p.ktps1;
         g.stages = p.stages1;
         g.xin = w.xr;
         g.y = c.out;
         g.y_dtype = c.out_dtype;
         g.part = w.part1;
         g.cnt = w.cnt1;
-        g.sched = w.sched;
         e = c.batched ? launch_gemv<1, EPI_ROUTE>(c.cb, g, p.grid1, p.smem1, s)
                       : launch_gemv<1, EPI_LINEAR>(c.cb, g, p.grid1, p.smem1, s);
         prof_mark(s);
@@ -1483,8 +1583,6 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     g.in_f = p.hidden;
     g.out_f = p.inter;
     g.ncb = p.ncb1;
-    g.nsplit = p.nsplit1;
-    g.ktps = p.ktps1;
     g.stages = p.stages1;
     g.xin = w.xr;
     g.down = c.down;
@@ -1493,7 +1591,6 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     g.act = c.act;
     g.part = w.part1;
     g.cnt = w.cnt1;
-    g.sched = w.sched;
     e = gateless ? launch_gemv<1, EPI_GATEUP>(c.cb, g, p.grid1, p.smem1, s)
                  : launch_gemv<2, EPI_GATEUP>(c.cb, g, p.grid1, p.smem1, s);
     if (e != cudaSuccess) return e;
@@ -1505,14 +1602,11 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     d.in_f = p.inter;
     d.out_f = p.hidden;
     d.ncb = p.ncb2;
-    d.nsplit = p.nsplit2;
-    d.ktps = p.ktps2;
     d.stages = p.stages2;
     d.xin = w.a2;
     d.yd = w.yd;
     d.part = w.part2;
     d.cnt = w.cnt2;
-    d.sched = w.sched + 1;
     if ((e = launch_gemv<1, EPI_DOWN>(c.cb, d, p.grid2, p.smem2, s)) != cudaSuccess) return e;
     prof_mark(s);
 

@@ -18,7 +18,7 @@
 //  * every call reuses the array and it keeps the previous call's contents;
 //    the status word, the one word that must start at zero, is cleared on
 //    the call's stream before the kernels run; the routing prep kernel then
-//    rewrites the slot count and clears the split-K and scheduling counters;
+//    rewrites the slot count and clears the split-K counters;
 //  * calls whose GPU work overlaps (two streams, or two host threads on one
 //    device without ordering) race on the array and corrupt each other;
 //  * a call whose work buffers would exceed the array is rejected before
