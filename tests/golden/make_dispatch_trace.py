@@ -205,7 +205,10 @@ class Proj:
         self.trellis = torch.from_numpy(rng.integers(-32768, 32768, (in_f // 16, out_f // 16, 16 * K),
                                                      dtype=np.int16))
         self.suh = torch.from_numpy(rng.choice([-1.0, 1.0], in_f).astype(np.float16))
-        self.svh = torch.from_numpy(rng.choice([-1.0, 1.0], out_f).astype(np.float16))
+        # output signs with a per-tensor scale folded in, ~1/sqrt(in) (the
+        # magnitudes of real packs: outputs stay O(1) and fp16-safe)
+        scale = rng.uniform(0.5, 1.5) / np.sqrt(in_f)
+        self.svh = torch.from_numpy((rng.choice([-1.0, 1.0], out_f) * scale).astype(np.float16))
         self.K, self.mcg, self.mul1 = K, True, False
         self.in_features, self.out_features = in_f, out_f
 
