@@ -417,7 +417,13 @@ __device__ __forceinline__ uint32_t load_x2_h(const void* x, int64_t i) {
 // rows are padded to 16); padding rows enter as zeros and are not stored.
 // Output: GEMM path (rowmajor) fp16 [proj][row][in]; GEMV path fp16
 // [proj][in/128][row][pitch], each feature stored twice in the dup_pos
-// order for MCG / 3INST (dup).
+// order for MCG / 3INST (dup).  Each warp assembles its 16 x 128 result in a
+// shared-memory tile laid out like the destination rows (pitch 136, or 264
+// for dup: conflict-free fragment stores) and writes it out with 16-byte
+// stores: whole 256-byte rows (rowmajor) or the whole contiguous 16-row slice
+// (GEMV layouts), instead of 4-byte stores scattered over 8 rows.  Padding
+// rows of a group go out as zeros (their inputs are zero); no kernel reads
+// them as data.
 __device__ __forceinline__ void rot_store2(__half* row, int f, bool dup, float v0, float v1) {
     if (dup) {
         *reinterpret_cast<__half2*>(row + dup_pos(f)) = __half2half2(__float2half_rn(v0));
@@ -429,8 +435,14 @@ __device__ __forceinline__ void rot_store2(__half* row, int f, bool dup, float v
 
 enum RotLayout : int { ROT_ROWMAJOR = 0, ROT_PITCH = 1, ROT_DUP = 2 };
 
+// fp16 pitch of a warp's shared-memory output tile
+__host__ __device__ constexpr int rot_tile_pitch(int layout) { return layout == ROT_DUP ? kXPitchD : kXPitch; }
+
 template <int XDT, bool VEC, int LAYOUT>
 __global__ void __launch_bounds__(256) rotate_rows_mma_kernel(const RotArgs a, const int* __restrict__ sorted_exp) {
+    constexpr int SP = rot_tile_pitch(LAYOUT);
+    extern __shared__ __align__(16) __half rot_tiles[];
+    __half* tile = rot_tiles + (threadIdx.x >> 5) * (16 * SP);
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int nkb = a.in_f / 128;
     const int64_t ngroups = min(int64_t(a.nslots[1]), int64_t(a.rpad)) / 16;
@@ -463,30 +475,47 @@ __global__ void __launch_bounds__(256) rotate_rows_mma_kernel(const RotArgs a, c
             af[blk][2] = tok0 >= 0 ? load_x2_h<XDT, VEC>(a.x, int64_t(tok0) * a.in_f + c + 8) : 0u;
             af[blk][3] = tok1 >= 0 ? load_x2_h<XDT, VEC>(a.x, int64_t(tok1) * a.in_f + c + 8) : 0u;
         }
-        // row pointers of output block kb for projection pj (features relative to the block)
         constexpr bool dup = LAYOUT == ROT_DUP;
-        auto out_row = [&](int pj, int64_t p) -> __half* {
-            if constexpr (LAYOUT == ROT_ROWMAJOR) return a.xr + (int64_t(pj) * a.rpad + p) * a.in_f + kb * 128;
-            else return a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p) * x_pitch(dup);
+        // rows of the group that carry a route (row g: lane 4g's tok0; row g + 8: its tok1)
+        const unsigned v0 = __ballot_sync(0xffffffffu, tok0 >= 0), v1 = __ballot_sync(0xffffffffu, tok1 >= 0);
+        // the warp's tile -> output block kb of projection pj: 16-byte stores of
+        // the rows in use (padding rows are never read as data)
+        auto flush_tile = [&](int pj) {
+            __syncwarp();
+            if constexpr (LAYOUT == ROT_ROWMAJOR) {
+                #pragma unroll 4
+                for (int i = lane; i < 16 * 16; i += 32) {
+                    const int r = i >> 4, c = (i & 15) * 8;
+                    if ((((r < 8 ? v0 : v1) >> (4 * (r & 7))) & 1u) == 0) continue;
+                    *reinterpret_cast<uint4*>(a.xr + (int64_t(pj) * a.rpad + p0 + r) * a.in_f + kb * 128 + c) =
+                        *reinterpret_cast<const uint4*>(tile + r * SP + c);
+                }
+            } else {
+                constexpr int RC = SP / 8;  // 16-byte chunks per row
+                uint4* dst = reinterpret_cast<uint4*>(a.xr + ((int64_t(pj) * nkb + kb) * a.rpad + p0) * SP);
+                const uint4* src = reinterpret_cast<const uint4*>(tile);
+                #pragma unroll 4
+                for (int i = lane; i < 16 * RC; i += 32) {
+                    const int r = i / RC;
+                    if ((((r < 8 ? v0 : v1) >> (4 * (r & 7))) & 1u) == 0) continue;
+                    dst[i] = src[i];
+                }
+            }
+            __syncwarp();
         };
         if (a.prerotated) {
             // input already rotated (the fat GEMM's contract): copy the fp16 rows
-            __half* out0 = out_row(0, p0 + g);
-            __half* out1 = out_row(0, p0 + g + 8);
             #pragma unroll
             for (int blk = 0; blk < 8; ++blk)
                 #pragma unroll
                 for (int q = 0; q < 2; ++q) {
                     const int f = 16 * blk + 8 * q + 2 * t;
-                    if (tok0 >= 0) {
-                        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&af[blk][2 * q]));
-                        rot_store2(out0, f, dup, v.x, v.y);
-                    }
-                    if (tok1 >= 0) {
-                        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&af[blk][2 * q + 1]));
-                        rot_store2(out1, f, dup, v.x, v.y);
-                    }
+                    const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&af[blk][2 * q]));
+                    const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&af[blk][2 * q + 1]));
+                    rot_store2(tile + g * SP, f, dup, v0.x, v0.y);
+                    rot_store2(tile + (g + 8) * SP, f, dup, v1.x, v1.y);
                 }
+            flush_tile(0);
             continue;
         }
         for (int pj = 0; pj < a.nproj; ++pj) {
@@ -526,16 +555,15 @@ __global__ void __launch_bounds__(256) rotate_rows_mma_kernel(const RotArgs a, c
                                 d[blk + st][j][i] = __fsub_rn(u, v);
                             }
             // D fragment (j, i): row g (i < 2) or g + 8, feature 16 blk + 8 j + 2 t + (i & 1)
-            __half* out0 = out_row(pj, p0 + g);
-            __half* out1 = out_row(pj, p0 + g + 8);
             #pragma unroll
             for (int blk = 0; blk < 8; ++blk)
                 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
                     const int f = 16 * blk + 8 * j + 2 * t;
-                    if (tok0 >= 0) rot_store2(out0, f, dup, d[blk][j][0] * kHadNorm, d[blk][j][1] * kHadNorm);
-                    if (tok1 >= 0) rot_store2(out1, f, dup, d[blk][j][2] * kHadNorm, d[blk][j][3] * kHadNorm);
+                    rot_store2(tile + g * SP, f, dup, d[blk][j][0] * kHadNorm, d[blk][j][1] * kHadNorm);
+                    rot_store2(tile + (g + 8) * SP, f, dup, d[blk][j][2] * kHadNorm, d[blk][j][3] * kHadNorm);
                 }
+            flush_tile(pj);
         }
     }
 }
@@ -543,8 +571,11 @@ __global__ void __launch_bounds__(256) rotate_rows_mma_kernel(const RotArgs a, c
 template <int XDT, int LAYOUT>
 static void launch_rotate_layout(const RotArgs& ra, const int* sorted_exp, int grid, cudaStream_t s) {
     const bool vec = (reinterpret_cast<uintptr_t>(ra.x) & 15) == 0;
-    if (vec) rotate_rows_mma_kernel<XDT, true, LAYOUT><<<grid, 256, 0, s>>>(ra, sorted_exp);
-    else rotate_rows_mma_kernel<XDT, false, LAYOUT><<<grid, 256, 0, s>>>(ra, sorted_exp);
+    const int smem = 8 * 16 * rot_tile_pitch(LAYOUT) * 2;  // one 16-row tile per warp
+    void (*k)(const RotArgs, const int*) = vec ? rotate_rows_mma_kernel<XDT, true, LAYOUT>
+                                                : rotate_rows_mma_kernel<XDT, false, LAYOUT>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    k<<<grid, 256, smem, s>>>(ra, sorted_exp);
 }
 
 template <int XDT>
