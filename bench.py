@@ -70,7 +70,7 @@ H, I, E, TOPK, KBITS = 2048, 768, 128, 8, 4
 # with its source; it belongs to the kernel build named there, not
 # necessarily to the build being timed.
 DRAM_TRAFFIC = {
-    "decode": {"bytes": 241.6e6, "kernel": "gemv_kernel<2,GATEUP,MCG>, T=64",
+    "decode": {"bytes": 264.5e6, "kernel": "gemv_kernel<2,GATEUP,MCG>, T=64",
                "source": "profiles/gemv_gateup_cfg2_T64.md"},
     "prefill": {"bytes": 695.5e6, "kernel": "tc_gemm_kernel gate/up launches (mean), T=2048",
                 "source": "profiles/tc_gemm_cfg3_T2048.md"},
