@@ -378,6 +378,16 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
         : "memory");
 }
 
+// Programmatic dependent launch (griddepcontrol).  launch_dependents lets the
+// next kernel of the stream, when it is launched with programmatic stream
+// serialization, be scheduled before this one ends; wait blocks the calling
+// thread until the kernel before it has completed and its writes are
+// visible.  Both are no-ops for kernels launched the ordinary way.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
 }

@@ -36,6 +36,7 @@
 //  4. gemv<1>  down: same engine; epilogue FWHT o svh * route weight -> per-route rows.
 //  5. combine  out_t = sum over t's routes in top-k order (no atomics).
 #include <algorithm>
+#include <utility>
 
 #include "exl3_common.cuh"
 #include "exl3_internal.h"
@@ -443,6 +444,7 @@ __global__ void __launch_bounds__(256) rotate_rows_mma_kernel(const RotArgs a, c
     constexpr int SP = rot_tile_pitch(LAYOUT);
     extern __shared__ __align__(16) __half rot_tiles[];
     __half* tile = rot_tiles + (threadIdx.x >> 5) * (16 * SP);
+    pdl_launch_dependents();  // the GEMV that follows may start its prologue now
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int nkb = a.in_f / 128;
     const int64_t ngroups = min(int64_t(a.nslots[1]), int64_t(a.rpad)) / 16;
@@ -858,6 +860,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
 gemv_kernel(const __grid_constant__ GemvArgs a) {
     constexpr int NCT = kCW * 32;
     extern __shared__ __align__(128) char smem_raw[];
+    pdl_launch_dependents();  // the next kernel may be scheduled as this one's CTAs retire
     constexpr bool DUP = CB != CB_MUL1;  // duplicated activation layout
     constexpr int XP = x_pitch(DUP), XS = x_slice(DUP);
     const int S = a.stages;
@@ -888,6 +891,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
     if (warp == kCW) {
         // ------------------------------ producer ------------------------------
         if (lane != 0) return;
+        bool pred_done = false;  // griddepcontrol.wait issued
         uint32_t q = 0;   // stages issued
         int ps = 0;       // ring slot and parity of stage q
         uint32_t pph = 0u;
@@ -969,6 +973,14 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                     region += size_t(kKtPerStage) * (ok[p] ? rowb : 0);
                 }
                 const int kb = kt / kKtPerStage;
+                // the inputs are the previous kernel's output (rotation, or
+                // the gate/up epilogue): with a programmatic launch, the
+                // routing tables, the item's metadata and this first stage's
+                // trellis rows were fetched while that kernel was running
+                if (!pred_done) {
+                    pdl_wait();
+                    pred_done = true;
+                }
                 #pragma unroll
                 for (int p = 0; p < NPROJ; ++p) {
                     const __half* src = a.xin + ((int64_t(p) * nkb + kb) * a.rpad + I.p0) * XP;
@@ -995,6 +1007,8 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
     }
 
     // ------------------------------ consumers ------------------------------
+    // every consumer read and write comes after the previous kernel ends
+    pdl_wait();
     const int cw = warp;  // 16-column tile of the 128-column block
     // per-lane ldmatrix row address inside an input slice (rows padded to 272 B)
     const int brow = (lane & 7) + ((lane >> 4) << 3);
@@ -1233,6 +1247,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
 __global__ void __launch_bounds__(256)
 combine_kernel(const int* __restrict__ route_pos, const float* __restrict__ yd, int64_t t_max, int topk,
                int hidden, const int32_t* n_valid, void* out, int out_dtype) {
+    pdl_wait();  // the per-route rows come from the kernel before
     int64_t T = t_max;
     if (n_valid) T = min(T, int64_t(max(0, *n_valid)));
     const int h4 = hidden / 4;
@@ -1243,14 +1258,26 @@ combine_kernel(const int* __restrict__ route_pos, const float* __restrict__ yd, 
         const int c = int(i % h4) * 4;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         if (t < T) {
-            for (int k = 0; k < topk; ++k) {
-                const int p = route_pos[t * topk + k];
-                if (p < 0) continue;
-                const float4 v = *reinterpret_cast<const float4*>(yd + int64_t(p) * hidden + c);
-                acc.x += v.x;
-                acc.y += v.y;
-                acc.z += v.z;
-                acc.w += v.w;
+            // eight routes at a time: their row indices, then their rows, are
+            // loaded together (two memory round trips per eight routes, not
+            // two per route); the sum still runs in top-k order
+            for (int k0 = 0; k0 < topk; k0 += 8) {
+                int pos[8];
+                #pragma unroll
+                for (int u = 0; u < 8; ++u) pos[u] = k0 + u < topk ? route_pos[t * topk + k0 + u] : -1;
+                float4 v[8];
+                #pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    v[u] = pos[u] >= 0 ? *reinterpret_cast<const float4*>(yd + int64_t(pos[u]) * hidden + c)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+                #pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    if (pos[u] < 0) continue;
+                    acc.x += v[u].x;
+                    acc.y += v[u].y;
+                    acc.z += v[u].z;
+                    acc.w += v[u].w;
+                }
             }
         }
         const int64_t o = t * hidden + c;
@@ -1371,6 +1398,26 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     return true;
 }
 
+// Launch with programmatic stream serialization: the kernel may start while
+// the one before it in the stream is still running and orders itself with
+// griddepcontrol.wait (gemv_kernel, combine_kernel); captured into a CUDA
+// graph as a programmatic edge.
+template <typename... P, typename... A>
+static cudaError_t launch_programmatic(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                       A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...);
+}
+
 template <int NPROJ, int EPI>
 static cudaError_t launch_gemv(int cb, const GemvArgs& g, int grid, size_t smem, cudaStream_t s) {
     void (*kern)(GemvArgs);
@@ -1379,8 +1426,7 @@ static cudaError_t launch_gemv(int cb, const GemvArgs& g, int grid, size_t smem,
     else kern = gemv_kernel<NPROJ, EPI, CB_3INST>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
-    kern<<<grid, kGemvThreads, smem, s>>>(g);
-    return cudaGetLastError();
+    return launch_programmatic(kern, dim3(grid), dim3(kGemvThreads), smem, s, g);
 }
 
 // ---------------------------------------------------------------------------
@@ -1643,9 +1689,9 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
 
     const int64_t total = p.t_max * (p.hidden / 4);
     const int64_t blocks = std::min<int64_t>((total + 255) / 256, int64_t(nsm) * 16);
-    combine_kernel<<<unsigned(std::max<int64_t>(blocks, 1)), 256, 0, s>>>(
-        w.route_pos, w.yd, p.t_max, p.topk, p.hidden, c.n_valid, c.out, c.out_dtype);
-    e = cudaGetLastError();
+    e = launch_programmatic(combine_kernel, dim3(unsigned(std::max<int64_t>(blocks, 1))), dim3(256), 0, s,
+                            static_cast<const int*>(w.route_pos), static_cast<const float*>(w.yd), p.t_max, p.topk,
+                            p.hidden, static_cast<const int32_t*>(c.n_valid), c.out, c.out_dtype);
     prof_mark(s);
     return e;
 }
