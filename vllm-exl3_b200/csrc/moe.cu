@@ -654,8 +654,10 @@ struct GemvSmem {
 __host__ __device__ inline size_t gemv_trellis_bytes(int nproj, int kmax) {
     return size_t(nproj) * kKtPerStage * 256 * kmax;
 }
-__host__ __device__ inline size_t gemv_stage_bytes(int nproj, int kmax, bool dup) {
-    return (gemv_trellis_bytes(nproj, kmax) + size_t(nproj) * x_slice(dup) + 127) & ~size_t(127);
+// nx: input slices per stage (one per projection; one for a paired launch,
+// whose two column blocks share the input)
+__host__ __device__ inline size_t gemv_stage_bytes(int nproj, int kmax, bool dup, int nx) {
+    return (gemv_trellis_bytes(nproj, kmax) + size_t(nx) * x_slice(dup) + 127) & ~size_t(127);
 }
 __host__ __device__ inline size_t gemv_bar_bytes(int stages) {
     return (size_t(stages) * 2 * 8 + kItemRing * 8 + 8 * 4 + 127) & ~size_t(127);
@@ -775,7 +777,9 @@ __device__ __forceinline__ bool guarded_wait(uint64_t* bar, uint32_t parity, int
 // for the scheduler) and multiplied by the 16-row input slice.
 //   tiles: trellis region of the stage + this warp's tile offset (uint32 words)
 //   xs:    per-lane ldmatrix address of projection 0's input slice
-template <int K, int CB, int NP>
+// SHX: every "projection" reads the same input slice (a paired launch: two
+// column blocks of one projection)
+template <int K, int CB, int NP, bool SHX = false>
 __device__ __forceinline__ void stage_mma(const uint32_t* __restrict__ tiles, uint32_t xs, int lane,
                                           bool two, float (&acc)[NP][2][4]) {
     constexpr int ROW = 64 * K;                // words per k-tile row (8 tiles of 8K words)
@@ -791,8 +795,8 @@ __device__ __forceinline__ void stage_mma(const uint32_t* __restrict__ tiles, ui
             #pragma unroll
             for (int p = 0; p < NP; ++p) {
                 uint32_t b[4], c[4];
-                ldmatrix_x4(b, xs + p * kXSliceD + kk * 64);
-                ldmatrix_x4(c, xs + p * kXSliceD + kk * 64 + 32);
+                ldmatrix_x4(b, xs + (SHX ? 0 : p * kXSliceD) + kk * 64);
+                ldmatrix_x4(c, xs + (SHX ? 0 : p * kXSliceD) + kk * 64 + 32);
                 const uint32_t a0[4] = {h[p][0], h[p][4], h[p][1], h[p][5]};
                 const uint32_t a1[4] = {h[p][2], h[p][6], h[p][3], h[p][7]};
                 mma_16816(acc[p][0], a0, b[0], b[1]);
@@ -812,7 +816,7 @@ __device__ __forceinline__ void stage_mma(const uint32_t* __restrict__ tiles, ui
             #pragma unroll
             for (int p = 0; p < NP; ++p) {
                 uint32_t b[4];
-                ldmatrix_x4(b, xs + p * kXSlice + kk * 32);
+                ldmatrix_x4(b, xs + (SHX ? 0 : p * kXSlice) + kk * 32);
                 mma_16816(acc[p][0], af[p], b[0], b[1]);
                 if (two) mma_16816(acc[p][1], af[p], b[2], b[3]);
             }
@@ -837,7 +841,7 @@ __device__ __forceinline__ void stage_mma_k(int K, const uint32_t* tiles, uint32
 
 // A work item's stages when every projection has bit width K (the usual
 // case); advances the ring position (s, ph).
-template <int K, int CB, int NP>
+template <int K, int CB, int NP, bool SHX>
 __device__ __forceinline__ void gemv_same_k_loop(const GemvSmem& sm, int S, size_t stage_bytes, size_t xs_off,
                                                  uint32_t xs_lane, int cw, int kt0, int kt1, int& s, uint32_t& ph,
                                                  bool two, float (&acc)[NP][2][4], int* status,
@@ -846,7 +850,7 @@ __device__ __forceinline__ void gemv_same_k_loop(const GemvSmem& sm, int S, size
         if (guarded_wait(&sm.full[s], ph, status, abort_flag)) {
             const char* st = sm.stages + size_t(s) * stage_bytes;
             const uint32_t xs = smem_u32(st + xs_off) + xs_lane;
-            stage_mma<K, CB, NP>(reinterpret_cast<const uint32_t*>(st) + cw * 8 * K, xs, lane, two, acc);
+            stage_mma<K, CB, NP, SHX>(reinterpret_cast<const uint32_t*>(st) + cw * 8 * K, xs, lane, two, acc);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[s]);
@@ -863,9 +867,14 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
     pdl_launch_dependents();  // the next kernel may be scheduled as this one's CTAs retire
     constexpr bool DUP = CB != CB_MUL1;  // duplicated activation layout
     constexpr int XP = x_pitch(DUP), XS = x_slice(DUP);
+    // paired launch (down projection): "projections" 0 and 1 are column
+    // blocks 2cb and 2cb + 1 of one projection; they share the input slice,
+    // so a stage carries 16 tiles per warp on one slice, as gate/up does
+    constexpr bool PAIRED = EPI == EPI_DOWN && NPROJ == 2;
+    constexpr int NX = PAIRED ? 1 : NPROJ;
     const int S = a.stages;
     GemvSmem sm = gemv_smem(smem_raw, NPROJ, S);
-    const size_t stage_bytes = gemv_stage_bytes(NPROJ, a.kmax, DUP);
+    const size_t stage_bytes = gemv_stage_bytes(NPROJ, a.kmax, DUP, NX);
     const size_t xs_off = gemv_trellis_bytes(NPROJ, a.kmax);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     volatile int* abort_flag = sm.flags;
@@ -904,10 +913,13 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             const uint16_t* tp[NPROJ];
             #pragma unroll
             for (int p = 0; p < NPROJ; ++p) {
-                ok[p] = proj_ok(a.proj[p], I.e, a.kmax, a.status, true);
-                Kp[p] = proj_k(a.proj[p], I.e);
-                tp[p] = proj_trellis(a.proj[p], I.e);
+                const ProjRef& pr = a.proj[PAIRED ? 0 : p];
+                ok[p] = proj_ok(pr, I.e, a.kmax, a.status, p == 0 || !PAIRED);
+                Kp[p] = proj_k(pr, I.e);
+                tp[p] = proj_trellis(pr, I.e);
             }
+            // output column block of "projection" p
+            auto pcb = [&](int p) { return PAIRED ? 2 * I.cb + p : I.cb; };
             // the item's slot (free once the consumers finished item j - kItemRing)
             if (!guarded_wait(&sm.item_empty[ji], jph ^ 1u, a.status, abort_flag)) break;
             ItemSlot& is = sm.items[ji];
@@ -926,7 +938,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             const __half* vsrc[3] = {nullptr, nullptr, nullptr};
             void* vdst[3] = {is.svh[0], is.svh[1], is.dsuh};
             #pragma unroll
-            for (int p = 0; p < NPROJ; ++p) vsrc[p] = proj_svh(a.proj[p], I.e);
+            for (int p = 0; p < NPROJ; ++p) vsrc[p] = proj_svh(a.proj[PAIRED ? 0 : p], I.e);
             if (EPI == EPI_GATEUP) vsrc[2] = proj_suh(a.down, I.e);
             uint32_t vbytes = 0;
             #pragma unroll
@@ -935,7 +947,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 if (v == 2 && EPI != EPI_GATEUP) continue;
                 int mode = 0;
                 if (vsrc[v]) {
-                    vsrc[v] += size_t(I.cb) * 128;
+                    vsrc[v] += size_t(v < 2 ? pcb(v) : I.cb) * 128;
                     mode = (reinterpret_cast<uintptr_t>(vsrc[v]) & 15) ? 2 : 1;
                     if (mode == 1) vbytes += 256;
                 }
@@ -953,7 +965,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 const int s = ps;
                 if (!guarded_wait(&sm.empty[s], pph ^ 1u, a.status, abort_flag)) break;
                 char* st = sm.stages + size_t(s) * stage_bytes;
-                uint32_t bytes = NPROJ * XS;
+                uint32_t bytes = NX * XS;
                 if (first_stage) bytes += vbytes;
                 #pragma unroll
                 for (int p = 0; p < NPROJ; ++p)
@@ -966,7 +978,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                     if (ok[p]) {
                         const int tw = 16 * Kp[p];  // int16 per tile
                         for (int kk = 0; kk < kKtPerStage; ++kk) {
-                            const uint16_t* src = tp[p] + (int64_t(kt + kk) * ntiles_out + int64_t(I.cb) * 8) * tw;
+                            const uint16_t* src = tp[p] + (int64_t(kt + kk) * ntiles_out + int64_t(pcb(p)) * 8) * tw;
                             bulk_g2s(st + region + size_t(kk) * rowb, src, uint32_t(rowb), &sm.full[s]);
                         }
                     }
@@ -982,7 +994,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                     pred_done = true;
                 }
                 #pragma unroll
-                for (int p = 0; p < NPROJ; ++p) {
+                for (int p = 0; p < NX; ++p) {
                     const __half* src = a.xin + ((int64_t(p) * nkb + kb) * a.rpad + I.p0) * XP;
                     bulk_g2s(st + xs_off + size_t(p) * XS, src, uint32_t(XS), &sm.full[s]);
                 }
@@ -1048,7 +1060,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
         // the common case (every projection at one K) runs a loop specialised
         // for that K: the switch on K happens once per item, not per stage
         #define EXL3_GEMV_SAME(KK)                                                                           \
-            gemv_same_k_loop<KK, CB, NPROJ>(sm, S, stage_bytes, xs_off, xs_lane, cw, I.kt0, I.kt1, cs, cph, two, \
+            gemv_same_k_loop<KK, CB, NPROJ, PAIRED>(sm, S, stage_bytes, xs_off, xs_lane, cw, I.kt0, I.kt1, cs, cph, two, \
                                             acc, a.status, abort_flag, lane)
         if (same) {
             switch (Kp[0]) {
@@ -1076,7 +1088,7 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                             const uint32_t* tiles =
                                 reinterpret_cast<const uint32_t*>(st + region) + cw * 8 * Kp[p];
                             float (&accp)[1][2][4] = *reinterpret_cast<float (*)[1][2][4]>(&acc[p]);
-                            stage_mma_k<CB, 1>(Kp[p], tiles, xs + p * XS, lane, two, accp);
+                            stage_mma_k<CB, 1>(Kp[p], tiles, xs + (PAIRED ? 0 : p * XS), lane, two, accp);
                             region += size_t(kKtPerStage) * 256 * Kp[p];
                         }
                     }
@@ -1145,7 +1157,9 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             for (int i = 0; i < 4; ++i) x[i] = row[lane + 32 * i];
             fwht128_warp(x, lane);
             const int vm = is.info[IF_SVH0 + p];
-            const __half* svh = vm == 1 ? is.svh[p] : vm == 2 ? proj_svh(a.proj[p], I.e) + I.cb * 128 : nullptr;
+            const __half* svh = vm == 1   ? is.svh[p]
+                                : vm == 2 ? proj_svh(a.proj[PAIRED ? 0 : p], I.e) + (PAIRED ? 2 * I.cb + p : I.cb) * 128
+                                          : nullptr;
             #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const float sv = svh ? __half2float(svh[lane + 32 * i]) : 0.f;
@@ -1197,11 +1211,12 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 }
             }
         } else if constexpr (EPI == EPI_DOWN) {
-            for (int r = cw; r < I.rows; r += kCW) {
-                const float* row = sm.ys + r * kYsPitch;
+            for (int v = cw; v < NPROJ * I.rows; v += kCW) {
+                const int pj = v / I.rows, r = v - pj * I.rows;
+                const float* row = sm.ys + (pj * 16 + r) * kYsPitch;
                 const int64_t p = I.p0 + r;
                 const float w = is.w[r];
-                float* dst = a.yd + p * a.out_f + I.cb * 128;
+                float* dst = a.yd + p * a.out_f + (PAIRED ? 2 * I.cb + pj : I.cb) * 128;
                 #pragma unroll
                 for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = row[lane + 32 * i] * w;
             }
@@ -1294,9 +1309,9 @@ combine_kernel(const int* __restrict__ route_pos, const float* __restrict__ yd, 
 static constexpr size_t kSmemPerSm = 228 * 1024;
 static constexpr int kCtasPerSm = 2;
 
-static void pick_stages(int nproj, int kmax, bool dup, int& stages, size_t& smem) {
+static void pick_stages(int nproj, int kmax, bool dup, int nx, int& stages, size_t& smem) {
     const size_t per_cta = kSmemPerSm / kCtasPerSm - 1024;
-    const size_t sb = gemv_stage_bytes(nproj, kmax, dup);
+    const size_t sb = gemv_stage_bytes(nproj, kmax, dup, nx);
     int s = 8;
     while (s > 2 && gemv_fixed_bytes(nproj, s) + size_t(s) * sb > per_cta) --s;
     stages = s;
@@ -1327,11 +1342,13 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     const int grid = num_sms * kCtasPerSm;
     p.ncb1 = inter / 128;
     p.dup = cb != CB_MUL1;  // unknown codebook (-1): size for the larger layout
-    pick_stages(linear ? 1 : 2, kmax, p.dup, p.stages1, p.smem1);
+    pick_stages(linear ? 1 : 2, kmax, p.dup, linear ? 1 : 2, p.stages1, p.smem1);
     p.grid1 = grid;
     if (!linear) {
         p.ncb2 = hidden / 128;
-        pick_stages(1, kmax, p.dup, p.stages2, p.smem2);
+        // down: pairs of 128-column blocks per work item when they pair up
+        p.pair2 = p.ncb2 % 2 == 0;
+        pick_stages(p.pair2 ? 2 : 1, kmax, p.dup, 1, p.stages2, p.smem2);
         p.grid2 = grid;
     }
 
@@ -1389,7 +1406,7 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
         p.off_yd = take(linear ? 0 : size_t(p.rpad) * hidden * 4);
         // stream-K partial tiles: two per CTA (exl3::gemv_item)
         p.off_part1 = take(size_t(2) * p.grid1 * kCW * nproj1 * 256 * 4);
-        p.off_part2 = take(linear ? 0 : size_t(2) * p.grid2 * kCW * 256 * 4);
+        p.off_part2 = take(linear ? 0 : size_t(2) * p.grid2 * kCW * (p.pair2 ? 2 : 1) * 256 * 4);
         p.off_cnt1 = take(size_t(p.smax) * p.ncb1 * 4);
         p.off_cnt2 = take(linear ? 0 : size_t(p.smax) * p.ncb2 * 4);
         p.off_g = p.off_u = p.off_x2 = take(0);
@@ -1678,13 +1695,15 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
     d.proj[1] = ProjRef();
     d.in_f = p.inter;
     d.out_f = p.hidden;
-    d.ncb = p.ncb2;
+    d.ncb = p.pair2 ? p.ncb2 / 2 : p.ncb2;
     d.stages = p.stages2;
     d.xin = w.a2;
     d.yd = w.yd;
     d.part = w.part2;
     d.cnt = w.cnt2;
-    if ((e = launch_gemv<1, EPI_DOWN>(c.cb, d, p.grid2, p.smem2, s)) != cudaSuccess) return e;
+    e = p.pair2 ? launch_gemv<2, EPI_DOWN>(c.cb, d, p.grid2, p.smem2, s)
+                : launch_gemv<1, EPI_DOWN>(c.cb, d, p.grid2, p.smem2, s);
+    if (e != cudaSuccess) return e;
     prof_mark(s);
 
     const int64_t total = p.t_max * (p.hidden / 4);
