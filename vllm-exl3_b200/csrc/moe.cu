@@ -147,6 +147,45 @@ __device__ __forceinline__ int local_expert(const PrepArgs& a, int64_t r) {
 }
 
 // Block-wide exclusive scan of one int per thread (kPrepThreads threads).
+// Exclusive scan of three values at once (one pass: two barriers in the
+// scan itself instead of two per value); sh96 holds 3 x 32 ints.
+__device__ int3 block_excl_scan3(int3 v, int3* total, int* sh96) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int3 x = v;
+    #pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y0 = __shfl_up_sync(0xffffffffu, x.x, o);
+        const int y1 = __shfl_up_sync(0xffffffffu, x.y, o);
+        const int y2 = __shfl_up_sync(0xffffffffu, x.z, o);
+        if (lane >= o) {
+            x.x += y0;
+            x.y += y1;
+            x.z += y2;
+        }
+    }
+    if (lane == 31) {
+        sh96[warp] = x.x;
+        sh96[32 + warp] = x.y;
+        sh96[64 + warp] = x.z;
+    }
+    __syncthreads();
+    if (warp < 3) {
+        int s = sh96[32 * warp + lane];
+        #pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += y;
+        }
+        sh96[32 * warp + lane] = s;
+    }
+    __syncthreads();
+    int3 pre = make_int3(0, 0, 0);
+    if (warp) pre = make_int3(sh96[warp - 1], sh96[32 + warp - 1], sh96[64 + warp - 1]);
+    *total = make_int3(sh96[31], sh96[63], sh96[95]);
+    __syncthreads();
+    return make_int3(pre.x + x.x - v.x, pre.y + x.y - v.y, pre.z + x.z - v.z);
+}
+
 __device__ int block_excl_scan(int v, int* total, int* sh32) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int x = v;
@@ -196,10 +235,9 @@ __device__ void prep_layout(const PrepArgs& a, const int* cnt, int* poff, int* s
         ss += (cnt[e] + 15) >> 4;
         st += (cnt[e] + TR - 1) / TR;
     }
-    int tot_p, tot_s, tot_t;
-    int xp = block_excl_scan(sp, &tot_p, sh32);
-    int xs = block_excl_scan(ss, &tot_s, sh32);
-    int xt = block_excl_scan(st, &tot_t, sh32);
+    int3 tot;
+    const int3 x0 = block_excl_scan3(make_int3(sp, ss, st), &tot, sh32);
+    int xp = x0.x, xs = x0.y, xt = x0.z;
     for (int e = e0; e < e1; ++e) {
         const int n = cnt[e];
         poff[e] = xp;
@@ -209,19 +247,27 @@ __device__ void prep_layout(const PrepArgs& a, const int* cnt, int* poff, int* s
             for (int j = 0; j < (n + TR - 1) / TR; ++j)
                 a.w.tiles128[xt + j] = make_int4(e, xp + TR * j, min(TR, n - TR * j), 0);
         xt += (n + TR - 1) / TR;
-        for (int q = xp + n; q < xp + ((n + 15) & ~15); ++q) {
+        xp += (n + 15) & ~15;
+        xs += (n + 15) >> 4;
+    }
+    if (tid == 0) {
+        a.w.nslots[0] = tot.y;
+        a.w.nslots[1] = tot.x;  // sorted rows in use (each expert padded to 16); rows past it are stale
+        if (a.w.ntiles128) *a.w.ntiles128 = tot.z;
+    }
+    __syncthreads();
+    // padding rows (fewer than 16 per expert): one warp per expert, one
+    // coalesced store per array instead of one thread's serial row loop
+    const int lane = tid & 31;
+    for (int e = tid >> 5; e < E; e += kPrepThreads / 32) {
+        const int n = cnt[e];
+        if (lane < ((n + 15) & ~15) - n) {
+            const int q = poff[e] + n + lane;
             a.w.sorted_tok[q] = -1;
             a.w.sorted_route[q] = -1;
             a.w.sorted_exp[q] = e;
             a.w.sorted_w[q] = 0.f;
         }
-        xp += (n + 15) & ~15;
-        xs += (n + 15) >> 4;
-    }
-    if (tid == 0) {
-        a.w.nslots[0] = tot_s;
-        a.w.nslots[1] = tot_p;  // sorted rows in use (each expert padded to 16); rows past it are stale
-        if (a.w.ntiles128) *a.w.ntiles128 = tot_t;
     }
     __syncthreads();
 }
@@ -277,7 +323,7 @@ __device__ __forceinline__ int64_t prep_routes(const PrepArgs& a) {
 __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const PrepArgs a) {
     __shared__ int cnt[kMaxLocal];
     __shared__ int poff[kMaxLocal];
-    __shared__ int sh32[32];
+    __shared__ int sh32[96];  // block scans of up to three values
     const int tid = threadIdx.x;
     const int E = a.n_local;
     const int64_t R = prep_routes(a), Rmax = a.t_max * a.topk;
@@ -334,7 +380,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_count_kernel(const PrepArgs
 __global__ void __launch_bounds__(kPrepThreads) prep_plan_kernel(const PrepArgs a, int nchunks) {
     __shared__ int cnt[kMaxLocal];
     __shared__ int poff[kMaxLocal];
-    __shared__ int sh32[32];
+    __shared__ int sh32[96];  // block scans of up to three values
     const int tid = threadIdx.x;
     const int E = a.n_local;
     const int64_t R = prep_routes(a), Rmax = a.t_max * a.topk;
