@@ -43,6 +43,7 @@ struct MoePlan {
     // per GEMV phase: column blocks, grid, ring stages
     int ncb1 = 0, grid1 = 0, stages1 = 0;
     int ncb2 = 0, grid2 = 0, stages2 = 0;
+    bool pair1 = false;  // single-projection GEMV: two 128-column blocks per work item (ncb1 even)
     bool pair2 = false;  // down GEMV: two 128-column blocks per work item (ncb2 even)
     size_t smem1 = 0, smem2 = 0;
     // prefill path: tcgen05 grouped GEMM over 128-row expert tiles

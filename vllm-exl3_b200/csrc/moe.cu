@@ -913,10 +913,11 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
     pdl_launch_dependents();  // the next kernel may be scheduled as this one's CTAs retire
     constexpr bool DUP = CB != CB_MUL1;  // duplicated activation layout
     constexpr int XP = x_pitch(DUP), XS = x_slice(DUP);
-    // paired launch (down projection): "projections" 0 and 1 are column
-    // blocks 2cb and 2cb + 1 of one projection; they share the input slice,
-    // so a stage carries 16 tiles per warp on one slice, as gate/up does
-    constexpr bool PAIRED = EPI == EPI_DOWN && NPROJ == 2;
+    // paired launch (every single-projection epilogue): "projections" 0 and 1
+    // are column blocks 2cb and 2cb + 1 of one projection; they share the
+    // input slice, so a stage carries 16 tiles per warp on one slice, as
+    // gate/up does
+    constexpr bool PAIRED = EPI != EPI_GATEUP && NPROJ == 2;
     constexpr int NX = PAIRED ? 1 : NPROJ;
     const int S = a.stages;
     GemvSmem sm = gemv_smem(smem_raw, NPROJ, S);
@@ -1267,13 +1268,15 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = row[lane + 32 * i] * w;
             }
         } else if constexpr (EPI == EPI_LINEAR) {
-            for (int r = cw; r < I.rows; r += kCW) {
-                const float* row = sm.ys + r * kYsPitch;
+            for (int v = cw; v < NPROJ * I.rows; v += kCW) {
+                const int pj = v / I.rows, r = v - pj * I.rows;
+                const float* row = sm.ys + (pj * 16 + r) * kYsPitch;
+                const int col0 = (PAIRED ? 2 * I.cb + pj : I.cb) * 128;
                 const int tok = is.tok[r];
                 if (tok < 0) continue;
                 if (a.scatter_idx) {
                     // one route per destination row per call: plain read-modify-write
-                    float* dst = static_cast<float*>(a.y) + a.scatter_idx[tok] * a.out_f + I.cb * 128;
+                    float* dst = static_cast<float*>(a.y) + a.scatter_idx[tok] * a.out_f + col0;
                     const float w = __half2float(a.scatter_w[tok]);
                     #pragma unroll
                     for (int i = 0; i < 4; ++i) dst[lane + 32 * i] += w * row[lane + 32 * i];
@@ -1281,20 +1284,21 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 }
                 #pragma unroll
                 for (int i = 0; i < 4; ++i)
-                    store_from_float(a.y, int64_t(tok) * a.out_f + I.cb * 128 + lane + 32 * i, a.y_dtype,
+                    store_from_float(a.y, int64_t(tok) * a.out_f + col0 + lane + 32 * i, a.y_dtype,
                                      row[lane + 32 * i]);
             }
         } else {
             // EPI_ROUTE: route r = t * topk + j -> output row j * t_max + t
-            for (int r = cw; r < I.rows; r += kCW) {
-                const float* row = sm.ys + r * kYsPitch;
+            for (int v = cw; v < NPROJ * I.rows; v += kCW) {
+                const int pj = v / I.rows, r = v - pj * I.rows;
+                const float* row = sm.ys + (pj * 16 + r) * kYsPitch;
+                const int col0 = (PAIRED ? 2 * I.cb + pj : I.cb) * 128;
                 const int rt = is.route[r];
                 if (rt < 0) continue;
                 const int64_t orow = int64_t(rt % a.topk) * a.t_max + rt / a.topk;
                 #pragma unroll
                 for (int i = 0; i < 4; ++i)
-                    store_from_float(a.y, orow * a.out_f + I.cb * 128 + lane + 32 * i, a.y_dtype,
-                                     row[lane + 32 * i]);
+                    store_from_float(a.y, orow * a.out_f + col0 + lane + 32 * i, a.y_dtype, row[lane + 32 * i]);
             }
         }
         named_bar_sync(1, NCT);
@@ -1388,7 +1392,9 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
     const int grid = num_sms * kCtasPerSm;
     p.ncb1 = inter / 128;
     p.dup = cb != CB_MUL1;  // unknown codebook (-1): size for the larger layout
-    pick_stages(linear ? 1 : 2, kmax, p.dup, linear ? 1 : 2, p.stages1, p.smem1);
+    // single projection: pairs of 128-column blocks per work item when they pair up
+    p.pair1 = linear && p.ncb1 % 2 == 0;
+    pick_stages(linear && !p.pair1 ? 1 : 2, kmax, p.dup, linear ? 1 : 2, p.stages1, p.smem1);
     p.grid1 = grid;
     if (!linear) {
         p.ncb2 = hidden / 128;
@@ -1451,7 +1457,7 @@ bool plan_moe(MoePlan& p, int64_t t_max, int topk, int hidden, int inter, int n_
         p.off_a2 = take(linear ? 0 : size_t(inter / 128) * p.rpad * x_pitch(p.dup) * 2);
         p.off_yd = take(linear ? 0 : size_t(p.rpad) * hidden * 4);
         // stream-K partial tiles: two per CTA (exl3::gemv_item)
-        p.off_part1 = take(size_t(2) * p.grid1 * kCW * nproj1 * 256 * 4);
+        p.off_part1 = take(size_t(2) * p.grid1 * kCW * (linear && !p.pair1 ? 1 : 2) * 256 * 4);
         p.off_part2 = take(linear ? 0 : size_t(2) * p.grid2 * kCW * (p.pair2 ? 2 : 1) * 256 * 4);
         p.off_cnt1 = take(size_t(p.smax) * p.ncb1 * 4);
         p.off_cnt2 = take(linear ? 0 : size_t(p.smax) * p.ncb2 * 4);
@@ -1705,15 +1711,19 @@ cudaError_t run_moe(const MoePlan& p, const MoeCall& c, void* ws, cudaStream_t s
         g.proj[0] = c.up;
         g.in_f = p.hidden;
         g.out_f = p.inter;
-        g.ncb = p.ncb1;
+        g.ncb = p.pair1 ? p.ncb1 / 2 : p.ncb1;
         g.stages = p.stages1;
         g.xin = w.xr;
         g.y = c.out;
         g.y_dtype = c.out_dtype;
         g.part = w.part1;
         g.cnt = w.cnt1;
-        e = c.batched ? launch_gemv<1, EPI_ROUTE>(c.cb, g, p.grid1, p.smem1, s)
-                      : launch_gemv<1, EPI_LINEAR>(c.cb, g, p.grid1, p.smem1, s);
+        if (p.pair1)
+            e = c.batched ? launch_gemv<2, EPI_ROUTE>(c.cb, g, p.grid1, p.smem1, s)
+                          : launch_gemv<2, EPI_LINEAR>(c.cb, g, p.grid1, p.smem1, s);
+        else
+            e = c.batched ? launch_gemv<1, EPI_ROUTE>(c.cb, g, p.grid1, p.smem1, s)
+                          : launch_gemv<1, EPI_LINEAR>(c.cb, g, p.grid1, p.smem1, s);
         prof_mark(s);
         return e;
     }
