@@ -121,6 +121,26 @@ def test_linear_matches_dense(native, cuda, m, K, cb):
     _close(y.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("m", [1, 7, 16, 40])
+@pytest.mark.parametrize("out_f", [256, 768])
+@pytest.mark.parametrize("K,cb", [(4, 1), (3, 2), (3, 0)])
+def test_linear_paired_column_blocks(native, cuda, m, out_f, K, cb):
+    """An even number of 128-column blocks: the GEMV takes two blocks per work
+    item on one shared input slice (m < 32), every codebook including 3INST;
+    m = 40 takes the tensor-core GEMM on the same shapes."""
+    import torch
+    rng = np.random.default_rng(7 * m + out_f + 10 * K + cb)
+    in_f = 384
+    t, u, v = _rand_packed(rng, in_f, out_f, K)
+    w = oracle.dequant(t, u, v, K, cb=cb).astype(np.float32)
+    x = rng.normal(0, 1, (m, in_f)).astype(np.float32)
+    want = x.astype(np.float16).astype(np.float32) @ w
+    y = native.exl3_linear(torch.from_numpy(x).to(cuda), torch.from_numpy(t).to(cuda),
+                           torch.from_numpy(u).to(cuda), torch.from_numpy(v).to(cuda), K, cb,
+                           out_dtype=torch.float32)
+    _close(y.cpu().numpy(), want)
+
+
 def test_gemv_and_gemm_entries(native, cuda):
     import torch
     rng = np.random.default_rng(3)
