@@ -1153,10 +1153,18 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
             for (int p = 0; p < NPROJ; ++p)
                 #pragma unroll
                 for (int i = 0; i < 8; ++i) __stcg(pp + (p * 8 + i) * 32 + lane, acc[p][i >> 2][i & 3]);
-            __threadfence();
+            // publish the piece: the CTA barrier orders every thread's partial
+            // stores before thread 0's acquire-release add on the group's
+            // counter (one gpu-scope operation per piece instead of a fence in
+            // every thread); the CTA that completes the count reads the other
+            // pieces after the barrier that follows its acquire
             named_bar_sync(1, NCT);
             if (threadIdx.x == 0) {
-                const int old = atomicAdd(&a.cnt[I.group], 1);
+                int old;
+                asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                             : "=r"(old)
+                             : "l"(a.cnt + I.group)
+                             : "memory");
                 const int last = old == c1 - c0;
                 if (last) a.cnt[I.group] = 0;
                 sm.flags[1] = last;
@@ -1166,7 +1174,6 @@ gemv_kernel(const __grid_constant__ GemvArgs a) {
                 if (threadIdx.x == 0) mbar_arrive(&sm.item_empty[ji]);
                 continue;
             }
-            __threadfence();
             #pragma unroll
             for (int p = 0; p < NPROJ; ++p)
                 #pragma unroll
