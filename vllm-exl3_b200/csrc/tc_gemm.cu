@@ -339,17 +339,23 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__
                 }
                 named_bar_sync(1, 8 * 32);  // the tile is refilled next
             }
-            __threadfence();
+            // publish: the CTA barrier orders every thread's partial stores
+            // before one thread's acquire-release add on the item's counter;
+            // the last split reads the others after the barrier that follows
+            // its acquire (no gpu-scope fence in every thread)
             named_bar_sync(1, 8 * 32);
             if (et == 0) {
-                const int prev = atomicAdd(&a.cnt[base], 1);
+                int prev;
+                asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                             : "=r"(prev)
+                             : "l"(a.cnt + base)
+                             : "memory");
                 const bool last = prev == nsplit - 1;
                 if (last) a.cnt[base] = 0;  // ready for the next launch
                 *last_flag = last ? 1 : 0;
             }
             named_bar_sync(1, 8 * 32);
             run_epi = *last_flag != 0;
-            if (run_epi) __threadfence();
         }
         for (int h = 0; run_epi && h < nh; ++h) {
             const int rows_h = min(128, rows - 128 * h);
