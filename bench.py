@@ -93,6 +93,9 @@ def parse():
     ap.add_argument("--no-graph", action="store_true", help="time the expert-parallel step eagerly")
     ap.add_argument("--ep-transport", default="nvlink", choices=["nvlink", "nccl"],
                     help="expert-parallel exchange: the library's NVLink peer-store kernels or NCCL")
+    ap.add_argument("--ep-placement", default="balanced", choices=["balanced", "contiguous"],
+                    help="configs[4] expert placement over the ranks: even 128-row route tiles per rank from "
+                         "a calibration batch's counts, or contiguous blocks of E/G experts")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep"],
                     help="decode = configs[1] (the default, reported line, with the prefill and ep_cfg4 "
                          "sub-objects); prefill = configs[2] alone; ep = configs[4] alone")
@@ -676,7 +679,7 @@ def run_ep(args, rank, local_rank, world, which, steps, warmup):
     import torch
     import torch.distributed as dist
     from exl3_b200 import _native, moe, synthetic
-    from exl3_b200.ep import Exl3ExpertParallel
+    from exl3_b200.ep import Exl3ExpertParallel, balanced_placement, experts_of_rank
 
     c = EP_WORKLOADS[which]
     dev = torch.device("cuda", local_rank)
@@ -697,18 +700,41 @@ def run_ep(args, rank, local_rank, world, which, steps, warmup):
     def expert_of(e):
         return make(e, e + 1).experts[0]
 
-    layer = moe.layer_from_slices(lambda a, b: make(lo + a, lo + b), epr, H_, I_, dev)
+    # the router's per-expert Zipf bias is a property of the layer: every
+    # batch of it uses the same popularity ranks
+    zipf_ranks = np.random.default_rng([899]).permutation(E_) if c["router"] != "softmax" else None
+
+    def route(seed):
+        rng = np.random.default_rng(seed)
+        if c["router"] == "softmax":
+            return synthetic.softmax_topk(rng, Tt, E_, k, c["sigma"])
+        return synthetic.sigmoid_zipf_topk(rng, Tt, E_, k, ranks=zipf_ranks)
+
+    # load-aware placement (skewed routing only): slots from the routing
+    # counts of a calibration batch that is not one of the timed batches
+    slot = None
+    if which == "ep" and world > 1 and args.ep_placement == "balanced":
+        cal_ids, _ = route([950])
+        slot = np.asarray(balanced_placement(np.bincount(cal_ids.ravel(), minlength=E_), world))
+    if slot is None:
+        layer = moe.layer_from_slices(lambda a, b: make(lo + a, lo + b), epr, H_, I_, dev)
+    else:
+        held = experts_of_rank(slot, world, rank)
+
+        def make_held(a, b):
+            pk = make(0, 0)
+            pk.experts = [expert_of(e) for e in held[a:b]]
+            return pk
+
+        layer = moe.layer_from_slices(make_held, epr, H_, I_, dev)
     kbits = [int(inn["gate"].K) for inn in layer._exl3_inners]
-    ep = Exl3ExpertParallel(layer, E_, capacity=Tr, transport=args.ep_transport)
+    ep = Exl3ExpertParallel(layer, E_, capacity=Tr, transport=args.ep_transport,
+                            placement=None if slot is None else slot.tolist())
     NB = 4 if which == "decode" else 2
     batches, np_batches, local_routes, local_experts, rank_routes = [], [], [], [], []
     for b in range(NB):
-        rng = np.random.default_rng([900 + b])  # routing of all tokens: identical on every rank
-        if c["router"] == "softmax":
-            ids, w = synthetic.softmax_topk(rng, Tt, E_, k, c["sigma"])
-        else:
-            ids, w = synthetic.sigmoid_zipf_topk(rng, Tt, E_, k)
-        owner = ids // epr
+        ids, w = route([900 + b])  # routing of all tokens: identical on every rank
+        owner = (ids if slot is None else slot[ids]) // epr
         rank_routes.append([int((owner == g).sum()) for g in range(world)])
         mine = owner == rank
         local_routes.append(int(mine.sum()))
@@ -928,6 +954,9 @@ def run_ep(args, rank, local_rank, world, which, steps, warmup):
         "config": {"workload": f"{c['name']}, T={Tt} tokens/step ({Tr} per rank)", "experts": E_,
                    "experts_per_rank": epr, "topk": k, "hidden": H_, "intermediate": I_,
                    "parallelism": f"ep{world}",
+                   "placement": ("contiguous: rank g holds experts [g*E/G, (g+1)*E/G)" if slot is None else
+                                 "balanced: E/G experts per rank, longest-first by 128-row route tiles of "
+                                 "a calibration batch (seed 950, not a timed batch)"),
                    "exchange": ("NVLink peer stores into IPC-mapped windows (library kernels), per-step flags"
                                 if args.ep_transport == "nvlink" else "NCCL grouped send/recv")
                    + ", fixed capacity %d rows/rank" % Tr,

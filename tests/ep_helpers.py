@@ -149,14 +149,20 @@ def gloo_worker(rank: int, world: int, port: int, cfg: dict, result_q) -> None:
     try:
         pack = synthetic.make_moe_pack(cfg["seed"], cfg["E"], cfg["H"], cfg["I"], synthetic.CB_MCG, (4,))
         epr = cfg["E"] // world
-        layer = DenseLocalLayer(dense_experts(pack, rank * epr, (rank + 1) * epr))
+        placement = cfg.get("placement")
+        if placement is None:
+            layer = DenseLocalLayer(dense_experts(pack, rank * epr, (rank + 1) * epr))
+        else:
+            from exl3_b200.ep import experts_of_rank
+            dense = dense_experts(pack, 0, cfg["E"])
+            layer = DenseLocalLayer([dense[e] for e in experts_of_rank(placement, world, rank)])
         rng = np.random.default_rng(cfg["seed"] + 7)
         x = synthetic.activations(rng, cfg["T"] * world, cfg["H"])
         ids, w = synthetic.softmax_topk(rng, cfg["T"] * world, cfg["E"], cfg["topk"])
         ids[::5, 0] = -1  # dropped routes
         sl = slice(rank * cfg["T"], (rank + 1) * cfg["T"])
         ep = Exl3ExpertParallel(layer, cfg["E"], combine_dtype=torch.float32, ops=CpuEpOps(),
-                                capacity=cfg.get("capacity"))
+                                capacity=cfg.get("capacity"), placement=placement)
         nv = None
         if cfg.get("n_valid") is not None:
             nv = torch.tensor([cfg["n_valid"]], dtype=torch.int32)

@@ -49,11 +49,14 @@ def _close(got: np.ndarray, want: np.ndarray, rel: float = 2e-2, cos_min: float 
 # ---------------------------------------------------------------------------
 # CPU: gloo ranks, exchange logic with CPU stand-ins for the kernels
 # ---------------------------------------------------------------------------
-@pytest.mark.parametrize("n_valid,capacity", [(None, None), (7, None), (None, 12), (5, 16)])
-def test_ep_gloo_world2_matches_single_rank(n_valid, capacity):
+@pytest.mark.parametrize("n_valid,capacity,placement", [
+    (None, None, None), (7, None, None), (None, 12, None), (5, 16, None),
+    (None, None, [5, 0, 7, 2, 1, 6, 3, 4]), (6, 12, [1, 2, 3, 4, 5, 6, 7, 0])])
+def test_ep_gloo_world2_matches_single_rank(n_valid, capacity, placement):
     from exl3_b200 import synthetic
 
-    cfg = dict(seed=11, E=8, H=256, I=128, topk=2, T=12, n_valid=n_valid, capacity=capacity)
+    cfg = dict(seed=11, E=8, H=256, I=128, topk=2, T=12, n_valid=n_valid, capacity=capacity,
+               placement=placement)
     world = 2
     got, counts = {}, {}
     for r, y, c in _run_ranks(ep_helpers.gloo_worker, world, cfg, 60):
@@ -100,6 +103,41 @@ def test_ep_cpu_dispatch_contract():
                 mine = 0 <= gid < E and gid // (E // G) == g
                 assert int(sid[p, k]) == (gid - g * (E // G) if mine else -1)
                 assert float(sw[p, k]) == (float(w[t, k]) if mine else 0.0)
+
+
+def test_balanced_placement_properties():
+    """Every rank keeps E/G experts, the result is a permutation, and the
+    most-loaded rank (in 128-row tiles) is no worse than under the
+    contiguous split, within the greedy's bound of one expert's cost above
+    the mean."""
+    from exl3_b200 import synthetic
+    from exl3_b200.ep import balanced_placement, experts_of_rank
+
+    E, topk = 256, 8
+    ranks = np.random.default_rng(5).permutation(E)
+    ids, _ = synthetic.sigmoid_zipf_topk(np.random.default_rng(6), 8192, E, topk, ranks=ranks)
+    counts = np.bincount(ids.ravel(), minlength=E)
+    tiles = (counts + 127) // 128
+    for G in (1, 2, 4, 8):
+        slot = balanced_placement(counts, G)
+        assert sorted(slot) == list(range(E))
+        held = [experts_of_rank(slot, G, g) for g in range(G)]
+        assert sorted(e for h in held for e in h) == list(range(E))
+        for g in range(G):
+            assert all(slot[e] == g * (E // G) + j for j, e in enumerate(held[g]))
+        load = [int(tiles[h].sum()) for h in held]
+        contiguous = [int(tiles[g * (E // G):(g + 1) * (E // G)].sum()) for g in range(G)]
+        assert max(load) <= max(contiguous)
+        assert max(load) <= tiles.sum() / G + tiles.max()
+    with pytest.raises(ValueError):
+        balanced_placement(counts[:255], 4)
+
+
+def test_ep_rejects_bad_placement():
+    from exl3_b200.ep import Exl3ExpertParallel
+    layer = ep_helpers.DenseLocalLayer([None] * 8)
+    with pytest.raises(ValueError, match="permutation"):
+        Exl3ExpertParallel(layer, 8, ops=ep_helpers.CpuEpOps(), placement=[0, 1, 2, 3, 4, 5, 6, 6])
 
 
 def test_ep_rejects_uneven_split():
@@ -295,6 +333,39 @@ def test_ep_nvlink_wait_times_out_with_status(native, cuda):
     finally:
         for wn in wins:
             wn.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("transport,cap", [("nccl", None), ("nccl", 48), ("nvlink", 48)])
+def test_ep_world1_placement_matches_layer(native, cuda, transport, cap):
+    """A permuted placement: the rank holds the experts in slot order and
+    the layer relabels global ids, so the output equals the unpermuted
+    layer's for the same global ids (dropped routes included)."""
+    import torch
+    from exl3_b200 import moe, synthetic
+    from exl3_b200.ep import Exl3ExpertParallel, experts_of_rank
+    pack = synthetic.make_moe_pack(7, 8, 256, 128, synthetic.CB_MCG, (3, 4))
+    ref = moe.layer_from_pack(pack, cuda)
+    slot = [5, 0, 7, 2, 1, 6, 3, 4]
+    moved = synthetic.MoEPack(256, 128, synthetic.CB_MCG)
+    moved.experts = [pack.experts[e] for e in experts_of_rank(slot, 1, 0)]
+    layer = moe.layer_from_pack(moved, cuda)
+    ep = Exl3ExpertParallel(layer, 8, combine_dtype=torch.float32, capacity=cap, transport=transport,
+                            placement=slot)
+    try:
+        for step in range(2):
+            rng = np.random.default_rng(20 + step)
+            x = torch.from_numpy(synthetic.activations(rng, 40, 256)).to(torch.bfloat16).to(cuda)
+            ids, w = synthetic.softmax_topk(rng, 40, 8, 2)
+            ids[::7, 1] = -1
+            idt, wt = torch.from_numpy(ids).to(cuda), torch.from_numpy(w).to(cuda)
+            f32 = torch.empty(40, 256, dtype=torch.float32, device=cuda)
+            got = ep(x, wt, idt, out=f32).cpu().numpy()
+            want = torch.empty_like(f32)
+            ref.apply(x, wt, idt, out=want)
+            _close(got, want.cpu().numpy(), rel=1e-3)
+    finally:
+        ep.close()
 
 
 @pytest.mark.gpu

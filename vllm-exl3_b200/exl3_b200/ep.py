@@ -20,6 +20,12 @@ token exchange to vLLM's all-to-all backends.  One layer step:
 6. ``exl3_ep_combine`` (native): per-token sum over ranks in rank order --
    deterministic, no atomics.
 
+``placement`` (optional) is a permutation of expert ids: expert e sits in
+slot ``placement[e]`` and rank g owns slots [g*E/G, (g+1)*E/G), so skewed
+expert popularity can be spread evenly over the ranks
+(:func:`balanced_placement`).  The layer relabels the step's ids through it
+before the dispatch; the kernels keep the contiguous slot ownership.
+
 A token whose routes fall on one rank crosses the network once, not once per
 route.  ``transport="nvlink"`` replaces the NCCL transfers with the library's
 own kernels storing straight into the peers' memory (CUDA IPC windows,
@@ -172,6 +178,49 @@ class NvlinkEpWindow:
                 self.window = 0
 
 
+def balanced_placement(route_counts, world: int, tile_rows: int = 128) -> list[int]:
+    """A permutation of expert ids that evens out the ranks' local forward.
+
+    ``route_counts[e]`` is expert e's number of routes over a calibration
+    batch.  Every rank keeps ``E/world`` experts (the slots
+    [g*E/world, (g+1)*E/world)).  An expert's cost is its count of
+    ``tile_rows``-row tiles, because the grouped GEMM decodes an expert's
+    weights once per 128-row tile of its routes; ties go by route count.
+    Experts are placed longest first, each onto the least-loaded rank that
+    still has a free slot (longest-processing-time greedy).  Returns
+    ``slot[e]``, the slot expert e occupies.
+    """
+    counts = [int(c) for c in route_counts]
+    E = len(counts)
+    if world < 1 or E % world:
+        raise ValueError(f"{E} experts do not split evenly over {world} ranks")
+    epr = E // world
+    cost = [((c + tile_rows - 1) // tile_rows, c) for c in counts]
+    order = sorted(range(E), key=lambda e: (cost[e][0], cost[e][1], -e), reverse=True)
+    load = [(0, 0)] * world
+    held = [[] for _ in range(world)]
+    for e in order:
+        g = min((q for q in range(world) if len(held[q]) < epr), key=lambda q: (load[q], q))
+        held[g].append(e)
+        load[g] = (load[g][0] + cost[e][0], load[g][1] + cost[e][1])
+    slot = [0] * E
+    for g in range(world):
+        for j, e in enumerate(sorted(held[g])):
+            slot[e] = g * epr + j
+    return slot
+
+
+def experts_of_rank(placement, world: int, rank: int) -> list[int]:
+    """The global expert ids rank ``rank`` holds, in its local-id order
+    (local id j is slot rank*E/world + j)."""
+    E = len(placement)
+    epr = E // world
+    inv = [0] * E
+    for e, s in enumerate(placement):
+        inv[int(s)] = e
+    return inv[rank * epr:(rank + 1) * epr]
+
+
 class Exl3ExpertParallel(torch.nn.Module):
     """Routed-expert layer sharded by experts over a process group.
 
@@ -189,10 +238,15 @@ class Exl3ExpertParallel(torch.nn.Module):
     the host, and a step can be captured in a CUDA graph; the cost is moving
     the empty slots.  Without it (None) the exchanges carry exactly the
     pairs, with one host synchronisation per step for the split sizes.
+
+    ``placement`` (``n_global`` ints, a permutation, the same on every rank):
+    expert e sits in slot ``placement[e]``; this rank's local expert j is
+    the one in slot ``rank*n_global/world + j`` (:func:`experts_of_rank`).
+    None keeps expert e in slot e.
     """
 
     def __init__(self, local_layer, n_global: int, group=None, combine_dtype: torch.dtype = torch.float32,
-                 ops=None, capacity: int | None = None, transport: str = "nccl"):
+                 ops=None, capacity: int | None = None, transport: str = "nccl", placement=None):
         super().__init__()
         self.layer = local_layer
         self.group = group
@@ -209,6 +263,13 @@ class Exl3ExpertParallel(torch.nn.Module):
         if getattr(local_layer, "expert_map", None) is not None:
             raise ValueError("the local layer of an expert-parallel group takes local ids (no expert_map)")
         self.n_global = int(n_global)
+        self._slot = None
+        self._slot_dev: dict = {}
+        if placement is not None:
+            slot = [int(v) for v in placement]
+            if sorted(slot) != list(range(self.n_global)):
+                raise ValueError(f"placement must be a permutation of the {self.n_global} expert ids")
+            self._slot = torch.tensor(slot, dtype=torch.int64)
         self.combine_dtype = combine_dtype
         self.ops = ops if ops is not None else NativeEpOps()
         if capacity is not None and capacity < 1:
@@ -305,6 +366,8 @@ class Exl3ExpertParallel(torch.nn.Module):
             w = w.float()
         topk = ids.shape[1]
         self._events = []
+        if self._slot is not None:
+            ids = self._relabel(ids)
         if self.transport == "nvlink":
             return self._forward_nvlink(x, ids, w, limit, n_valid, out)
         if self.capacity is not None:
@@ -338,6 +401,18 @@ class Exl3ExpertParallel(torch.nn.Module):
         y = self.ops.combine(back, pair_idx, T, G, x.dtype, n_valid, out=out)
         self._mark()
         return y
+
+    def _relabel(self, ids: torch.Tensor) -> torch.Tensor:
+        """Global expert ids -> slots; ids outside [0, n_global) pass
+        through, so the dispatch treats them as before."""
+        key = (ids.device, ids.dtype)
+        slot = self._slot_dev.get(key)
+        if slot is None:
+            slot = self._slot.to(device=ids.device, dtype=ids.dtype)
+            self._slot_dev[key] = slot
+        n = self.n_global
+        valid = (ids >= 0) & (ids < n)
+        return torch.where(valid, slot[ids.clamp(0, n - 1)], ids)
 
     def _forward_fixed(self, x, ids, w, limit, n_valid, out):
         T, H = x.shape

@@ -122,8 +122,12 @@ def softmax_topk(rng: np.random.Generator, tokens: int, n_experts: int, topk: in
 
 
 def sigmoid_zipf_topk(rng: np.random.Generator, tokens: int, n_experts: int, topk: int,
-                      s: float = 1.1):
-    rank = rng.permutation(n_experts)
+                      s: float = 1.1, ranks: np.ndarray | None = None):
+    """Top-k of sigmoid(N(0,1) logits + a per-expert Zipf(s) bias).  Expert e
+    has popularity rank ``ranks[e]`` (0 = most popular).  A layer's router
+    bias is a property of the layer, so batches of one layer pass the same
+    ``ranks``; without it a permutation is drawn from ``rng``."""
+    rank = rng.permutation(n_experts) if ranks is None else np.asarray(ranks)
     pz = 1.0 / np.power(rank + 1.0, s)
     pz /= pz.sum()
     bias = np.log(pz * n_experts).astype(np.float32)
