@@ -344,24 +344,24 @@ struct EpP2pArgs {
     const int64_t* peers;
 };
 
-// True in the last CTA of the grid to get here.  Every thread's earlier
-// stores (peer memory included) are made visible system-wide before its CTA
-// counts itself done; the last CTA fences again before it signals, so a peer
-// that acquires the signal sees every CTA's stores.  The counter (zero on
-// entry) is reset by the last CTA.
+// True in the last CTA of the grid to get here.  The CTA barrier orders
+// every thread's earlier stores (peer memory included) before thread 0's
+// count, a system-scope acquire-release add: its release half is cumulative,
+// so it publishes the whole CTA's stores, and in the last CTA its acquire
+// half makes every other CTA's published stores visible to the threads that
+// signal after the second barrier.  One fence per CTA, not one per thread.
+// The counter (zero on entry) is reset by the last CTA.
 __device__ __forceinline__ bool ep_last_cta(int* ctr) {
     __shared__ int s_last;
-    __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
-        const int prev = atomicAdd(ctr, 1);
+        int prev;
+        asm volatile("atom.acq_rel.sys.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(ctr) : "memory");
         s_last = prev == int(gridDim.x) - 1;
         if (s_last) *ctr = 0;
     }
     __syncthreads();
-    const bool last = s_last != 0;
-    if (last) __threadfence_system();
-    return last;
+    return s_last != 0;
 }
 
 // raise this step's flag (arrival or return) in every peer's window; with
@@ -373,7 +373,8 @@ __device__ __forceinline__ void ep_raise_flags(const EpP2pArgs& a, size_t flag_o
     const uint32_t epoch = *reinterpret_cast<const uint32_t*>(a.window + kEpCtlEpoch);
     char* dst = reinterpret_cast<char*>(a.peers[g]);
     if (send_counts) reinterpret_cast<volatile int32_t*>(dst + counts_off)[a.rank] = send_counts[g];
-    __threadfence_system();
+    // the release store orders the count above (and, cumulatively, what the
+    // CTA acquired in ep_last_cta) before the flag
     st_release_sys(reinterpret_cast<uint32_t*>(dst + flag_off) + a.rank, epoch + 1u);
 }
 
