@@ -105,6 +105,31 @@ def test_ep_cpu_dispatch_contract():
                 assert float(sw[p, k]) == (float(w[t, k]) if mine else 0.0)
 
 
+def test_ep_gloo_world4_balanced_placement():
+    """Four gloo ranks with the placement balanced_placement picks for
+    skewed counts: every rank's output equals the single-rank eager loop
+    over all experts."""
+    from exl3_b200 import synthetic
+    from exl3_b200.ep import balanced_placement
+
+    E, world = 8, 4
+    counts = [90, 3, 40, 7, 200, 1, 12, 60]
+    placement = balanced_placement(counts, world, tile_rows=16)
+    assert placement != list(range(E))
+    cfg = dict(seed=13, E=E, H=256, I=128, topk=2, T=6, n_valid=None, capacity=8, placement=placement)
+    got = {r: y for r, y, _c in _run_ranks(ep_helpers.gloo_worker, world, cfg, 120)}
+    pack = synthetic.make_moe_pack(cfg["seed"], E, cfg["H"], cfg["I"], synthetic.CB_MCG, (4,))
+    dense = ep_helpers.dense_experts(pack, 0, E)
+    rng = np.random.default_rng(cfg["seed"] + 7)
+    x = synthetic.activations(rng, cfg["T"] * world, cfg["H"])
+    ids, w = synthetic.softmax_topk(rng, cfg["T"] * world, E, cfg["topk"])
+    ids[::5, 0] = -1
+    for r in range(world):
+        sl = slice(r * cfg["T"], (r + 1) * cfg["T"])
+        want = oracle.moe_eager(x[sl], ids[sl], w[sl], dense)
+        np.testing.assert_allclose(got[r], want, rtol=1e-5, atol=1e-5 * float(np.abs(want).max() + 1))
+
+
 def test_balanced_placement_properties():
     """Every rank keeps E/G experts, the result is a permutation, and the
     most-loaded rank (in 128-row tiles) is no worse than under the
