@@ -210,6 +210,16 @@ def balanced_placement(route_counts, world: int, tile_rows: int = 128) -> list[i
     return slot
 
 
+def _layer_device(layer):
+    """The device of a routed-expert layer's weights, or None when its
+    experts are not torch tensors."""
+    try:
+        t = layer._exl3_inners[0]["down"].trellis
+    except (AttributeError, IndexError, KeyError, TypeError):
+        return None
+    return t.device if isinstance(t, torch.Tensor) else None
+
+
 def experts_of_rank(placement, world: int, rank: int) -> list[int]:
     """The global expert ids rank ``rank`` holds, in its local-id order
     (local id j is slot rank*E/world + j)."""
@@ -270,6 +280,12 @@ class Exl3ExpertParallel(torch.nn.Module):
             if sorted(slot) != list(range(self.n_global)):
                 raise ValueError(f"placement must be a permutation of the {self.n_global} expert ids")
             self._slot = torch.tensor(slot, dtype=torch.int64)
+            # the slot table goes to the layer's GPU now, so a first step
+            # inside a CUDA-graph capture needs no host copy
+            dev = _layer_device(local_layer)
+            if dev is not None and dev.type == "cuda":
+                for dt in (torch.int64, torch.int32):
+                    self._slot_dev[(dev, dt)] = self._slot.to(device=dev, dtype=dt)
         self.combine_dtype = combine_dtype
         self.ops = ops if ops is not None else NativeEpOps()
         if capacity is not None and capacity < 1:
@@ -408,6 +424,9 @@ class Exl3ExpertParallel(torch.nn.Module):
         key = (ids.device, ids.dtype)
         slot = self._slot_dev.get(key)
         if slot is None:
+            if ids.is_cuda and torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("the expert placement table is not on this device yet: "
+                                   "run one step outside the CUDA-graph capture first")
             slot = self._slot.to(device=ids.device, dtype=ids.dtype)
             self._slot_dev[key] = slot
         n = self.n_global
