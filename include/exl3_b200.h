@@ -176,7 +176,9 @@ int exl3_ngram_lookup(const void* table, int64_t n_rows, int bits, const void* i
  * which leaves the exchange to vLLM's all-to-all backends and consumes only
  * the resulting expert_map, src/vllm_exl3/exl3.py:2310-2354).  Rank g of
  * `world` owns global experts [g*E/world, (g+1)*E/world), E = n_global
- * (a multiple of world).  For every token t < n_valid (all tokens when
+ * (a multiple of world).  A host with another expert placement maps each
+ * global id to its slot in that order before the call.  For every token
+ * t < n_valid (all tokens when
  * n_valid is NULL) and every rank g owning at least one of its routes it
  * writes one pair p: send_x[p] = x[t], send_ids[p][k] = the local id of
  * route k on g or -1, send_w[p][k] = its weight (fp32) or 0, send_tok[p] = t,
